@@ -1,0 +1,306 @@
+"""Decode throughput of the Qwen3-0.6B Q8_0 token loop on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl cuda|reference] [--config bs1_400|bs1_100|fp32]
+
+Workload (the default): seeded synthetic Qwen3-0.6B
+Q8_0 decoder (28 layers, hidden 1024, 16/8 heads of 128, FFN 3072, vocab
+151936, tied embedding), prefix of 400 N(0,1) audio embeddings + 8 prompt
+token ids, then fixed-length greedy decode (no end-token stop).  One bench
+step = one decode token; the timed region is K consecutive decode steps
+starting right after the prefill, so positions are the config's 408..408+K.
+
+Multi-GPU (torchrun): one process per GPU, each its own replica and session
+(independent utterances, no collective on the data path): weak scaling.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+CONFIGS = {
+    # name: (audio frames, prompt ids, decode tokens, quantized)
+    "bs1_400": (400, 8, 256, True),   # BASELINE configs[1] (metric's config)
+    "bs1_100": (100, 8, 128, True),   # configs[0]
+    "fp32": (100, 8, 128, False),     # configs[2]
+}
+SEED = 1234
+
+
+def model_path(quantized: bool) -> Path:
+    d = Path(os.environ.get("FUNASR_BENCH_DIR", "/tmp"))
+    return d / f"funasrnet_b200_synth_{'q8' if quantized else 'f32'}_{SEED}.gguf"
+
+
+def ensure_model(quantized: bool, rank: int, barrier) -> Path:
+    from funasrnet_b200._lib import check, lib
+
+    p = model_path(quantized)
+    if rank == 0 and not p.exists():
+        tmp = p.with_suffix(f".tmp{os.getpid()}")
+        check(lib().fa_synth_write_gguf(str(tmp).encode(), SEED, 0, 0, 0, 0, 1 if quantized else 0))
+        tmp.replace(p)
+    barrier()
+    return p
+
+
+def prefix(width: int, audio: int, ids: int, vocab: int, embed, seed: int = SEED):
+    """[audio][prompt] embeddings: N(0,1) audio vectors then Embed(ids)."""
+    from funasrnet_b200._lib import check, lib
+
+    a = np.empty(audio * width, np.float32)
+    check(lib().fa_synth_normals(seed, 9001, 0, a.size, a.ctypes.data))
+    rng = np.random.default_rng(seed)
+    toks = rng.integers(0, vocab, ids).astype(np.int32)
+    return np.concatenate([a, embed(toks)]), audio + ids
+
+
+class ClockSampler:
+    """nvidia-smi samples of SM clock and throttle reasons during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device: int):
+        self.device = device
+        self.proc = None
+        self.lines: list[str] = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.device}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            time.sleep(0.25)
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        rows = []
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                rows.append((float(parts[1]), float(parts[2]), parts[5:9]))
+            except ValueError:
+                continue
+        if not rows:
+            return None
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for _, _, r in rows for i, v in enumerate(r) if v.lower() == "active"})
+        return {"sm_mhz": statistics.median(r[0] for r in rows), "sm_max_mhz": max(r[1] for r in rows),
+                "reasons": reasons, "samples": len(rows)}
+
+
+def measured_peak_hbm():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        return float(json.loads(p.read_text())["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def oracle_decode_rate(path: Path, cfg, steps: int, warmup: int, threads: int):
+    """CPU restatement of the reference decoder on this host: prefill (untimed),
+    warm-up steps, then `steps` timed greedy decode steps."""
+    from oracle import oracle as O
+
+    O.build()
+    O.set_threads(threads)
+    audio, ids, _, _ = cfg
+    m = O.Model(path, 2048)
+    s = O.Session(m)
+    emb, frames = prefix(m.width, audio, ids, m.vocab, m.embed)
+    lg = s.decode(emb, frames)
+    tok = O.greedy(lg)
+    for _ in range(warmup):
+        tok = O.greedy(s.decode(m.embed([tok]), 1))
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        tok = O.greedy(s.decode(m.embed([tok]), 1))
+    dt = time.perf_counter() - t0
+    s.close()
+    m.close()
+    return steps / dt, dt
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=256)
+    ap.add_argument("--warmup", type=int, default=8)
+    ap.add_argument("--impl", choices=["cuda", "reference"], default="cuda")
+    ap.add_argument("--config", choices=sorted(CONFIGS), default="bs1_400")
+    ap.add_argument("--cpu-baseline-steps", type=int, default=24)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    cfg = CONFIGS[args.config]
+    audio, ids, tokens, quantized = cfg
+    steps = min(args.steps, tokens)
+    warmup = max(3, args.warmup)
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600))
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+
+    config = {"workload": f"qwen3-0.6b-{'q8_0' if quantized else 'f32'} bs1 prefix {audio}+{ids}, greedy {tokens}",
+              "batch_per_gpu": 1, "prefix": audio + ids, "decode_tokens": tokens,
+              "timed_positions": [audio + ids, audio + ids + steps], "parallelism": f"replicas x{args.gpus}",
+              "l2": "inputs larger than L2: every step streams the full 0.63 GB weight set"}
+    metric = "decode tokens/sec (Qwen3-0.6B Q8_0 bs1)" if quantized else "decode tokens/sec (Qwen3-0.6B FP32 bs1)"
+
+    if args.impl == "reference":
+        # The reference is C# (.NET 10); no dotnet here, so its CPU decoder is
+        # timed through the C++ restatement on all host threads (rank 0 only).
+        if rank == 0:
+            path = ensure_model(quantized, 0, lambda: None)
+            threads = os.cpu_count() or 1
+            rate, dt = oracle_decode_rate(path, cfg, steps, warmup, threads)
+            line = {"metric": metric, "value": rate, "unit": "tokens/s", "n_gpus": args.gpus, "steps": steps,
+                    "warmup": warmup, "ms_per_step": 1000.0 / rate, "higher_is_better": True, "scaling": "weak",
+                    "vs_baseline": None, "dtype": "int8 x int8 -> int32, f32 accumulate", "data": "synthetic",
+                    "config": config, "impl": "reference",
+                    "cpu_baseline": {"value": rate, "unit": "tokens/s", "cores": threads, "kind": "port",
+                                     "sample": f"{steps} decode steps after the {audio + ids}-frame prefill"},
+                    "e2e": {"value": rate, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+            print(json.dumps(line), flush=True)
+        if dist is not None:
+            dist.destroy_process_group()
+        return
+
+    from funasrnet_b200.backend import CudaFloatBackend
+    from funasrnet_b200.decoder import CudaModel, QwenDecoder
+
+    path = ensure_model(quantized, rank, barrier)
+    be = CudaFloatBackend(local)
+    cm = CudaModel(be, path, capacity=2048)
+    dec = QwenDecoder(cm)
+    emb, frames = prefix(cm.width, audio, ids, cm.vocab, dec.embed)
+
+    # warm-up (untimed): prefill + W decode steps, graph capture included
+    dec.reset()
+    dec.decode(emb, frames, want_logits=False)
+    dec.generate(warmup, end_ids=())
+    # timed: fresh prefill (untimed), then K steps through the on-device loop
+    dec.reset()
+    dec.decode(emb, frames, want_logits=False)
+    barrier()
+    with ClockSampler(local) as clocks:
+        toks = dec.generate(steps, end_ids=())
+    dev_ms = dec.last_generate_ms()
+    assert len(toks) == steps
+    if dist is not None:
+        import torch
+
+        t = torch.tensor([dev_ms], dtype=torch.float64, device=f"cuda:{local}")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        dev_ms = float(t.item())
+
+    # e2e: the same K steps through the public per-token API with host buffers
+    # (FunAsr.Transcribe's loop: H2D token id, D2H next token id each step).
+    dec.reset()
+    _, tok = dec.decode(emb, frames, want_logits=False)
+    barrier()
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        tok, _ = dec.step(tok)
+    e2e_s = time.perf_counter() - t0
+    if dist is not None:
+        import torch
+
+        t = torch.tensor([e2e_s], dtype=torch.float64, device=f"cuda:{local}")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_s = float(t.item())
+
+    # roofline of the decode step and of its largest single launch (lm_head GEMV)
+    peak, peak_kind = measured_peak_hbm()
+    kv_bytes_per_pos = cm.layers * 2 * cm.kv_heads * cm.head_size * 2
+    mean_pos = frames + (steps - 1) / 2.0
+    step_bytes = cm.weight_bytes + 1088 + kv_bytes_per_pos * (mean_pos + 1)
+    ms_per_step = dev_ms / steps
+    achieved = step_bytes / (ms_per_step * 1e-3) / 1e9
+    lm_ms = dec.time_lm_head(20) if quantized else None
+    lm_bytes = cm.vocab * cm.width // 32 * 34 + cm.width * 4 * 2
+
+    line = {
+        "metric": metric,
+        "value": world * steps / (dev_ms * 1e-3),
+        "unit": "tokens/s",
+        "n_gpus": world,
+        "steps": steps,
+        "warmup": warmup,
+        "ms_per_step": ms_per_step,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "int8 x int8 -> int32, f32 accumulate" if quantized else "f32",
+        "data": "synthetic (seeded random-init weights and prefix; no model or audio files exist here)",
+        "config": config,
+        "e2e": {"value": world * steps / e2e_s, "unit": "tokens/s", "h2d_bytes_per_step": 4,
+                "d2h_bytes_per_step": 4},
+        "roofline": {"bound": "hbm", "kernel": "decode step (CUDA graph)", "achieved": achieved, "peak": peak,
+                     "unit": "GB/s", "frac": achieved / peak, "traffic": None,
+                     "bytes_per_step": step_bytes, "peak_source": peak_kind},
+        "gpu_launches": dec.kernels_per_step() * steps,
+        "clocks": clocks.summary(),
+    }
+    if lm_ms:
+        a = lm_bytes / (lm_ms * 1e-3) / 1e9
+        line["gemv_lm_head"] = {"ms": lm_ms, "bytes": lm_bytes, "achieved": a, "frac": a / peak}
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        threads = os.cpu_count() or 1
+        rate, dt = oracle_decode_rate(path, cfg, args.cpu_baseline_steps, 2, threads)
+        line["cpu_baseline"] = {"value": rate, "unit": "tokens/s", "cores": threads, "kind": "port",
+                                "sample": f"{args.cpu_baseline_steps} decode steps after the {frames}-frame prefill "
+                                          f"({dt:.1f} s of CPU decode)"}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    dec.close()
+    cm.close()
+    be.dispose()
+    if dist is not None:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

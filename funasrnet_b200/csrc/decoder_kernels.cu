@@ -1,0 +1,848 @@
+// sm_100a kernels of the Qwen3 decoder step.
+//
+// Numerics: the library is compiled with -fmad=false and the order-sensitive
+// arithmetic uses explicit round-to-nearest intrinsics, so each expression is
+// evaluated with the roundings of the reference's C# source (RyuJIT never
+// fuses a*b+c).  Where the reference order is reproduced exactly the result is
+// bit-identical (activation quantiser, Q8 GEMV, RMSNorm up to the double sum's
+// association, RoPE, binary16 KV rounding, residual adds, argmax, embedding);
+// attention and SiLU use expf and a split-K order and stay within tolerance.
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cfloat>
+#include <climits>
+#include <mutex>
+
+#include "kernels.h"
+
+namespace fa {
+namespace {
+
+constexpr int kGemvThreads = 256;
+constexpr int kGemvWarps = kGemvThreads / 32;
+constexpr int kGemvFrames = 4;   // frames per CTA pass
+constexpr int kGemvUnroll = 4;   // (tile, block) units in flight per warp
+constexpr int kGemvMaxSmem = 227 * 1024;
+
+__device__ __forceinline__ bool skipped(const int* skip) { return skip != nullptr && *skip != 0; }
+
+// MathF.Round(v, MidpointRounding.AwayFromZero) as TensorMath.QuantizeAvx.cs:182-189
+// computes it: truncate, then step away from zero when |fraction| >= 0.5.
+__device__ __forceinline__ float round_away(float v) {
+  float t = truncf(v);
+  if (fabsf(__fsub_rn(v, t)) >= 0.5f) t = __fadd_rn(t, copysignf(1.0f, v));
+  return t;
+}
+
+// clamp((int)round_away(x * inv), -127, 127); cvt.rzi saturates and maps NaN
+// to 0 exactly like .NET 9+'s float->int conversion.
+__device__ __forceinline__ int quant1(float x, float inv) {
+  int r = __float2int_rz(round_away(__fmul_rn(x, inv)));
+  return max(-127, min(127, r));
+}
+
+// Block scale from the block's |x| maximum taken on the IEEE bit patterns
+// (TensorMath.QuantizeAvx.cs:145-150): d = amax / 127, inv = d == 0 ? 0 : 1 / d.
+__device__ __forceinline__ void block_scale(float v, float& d, float& inv) {
+  unsigned bits = __float_as_uint(v) & 0x7fffffffu;
+  unsigned mb = __reduce_max_sync(0xffffffffu, bits);
+  d = __fdiv_rn(__uint_as_float(mb), 127.0f);
+  inv = d == 0.0f ? 0.0f : __fdiv_rn(1.0f, d);
+}
+
+__device__ __forceinline__ double warp_sum_d(double v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = __dadd_rn(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+__device__ __forceinline__ float warp_sum_f(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// 1 / sqrt((float)(sumsq / width) + eps)  (TensorMath.Elementwise.cs:78)
+__device__ __forceinline__ float rms_inverse(double sumsq, int width, float eps) {
+  float ms = __double2float_rn(__ddiv_rn(sumsq, (double)width));
+  return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(ms, eps)));
+}
+
+template <bool F16S>
+__device__ __forceinline__ float load_scale(const Q8View& w, int tile, int b, int lane) {
+  if (F16S) {
+    const __half* p = reinterpret_cast<const __half*>(
+        static_cast<const uint8_t*>(w.s) + (((size_t)tile * w.scale_groups + (b >> 3)) * 32 + lane) * 16);
+    return __half2float(p[b & 7]);
+  } else {
+    const float* p = reinterpret_cast<const float*>(
+        static_cast<const uint8_t*>(w.s) + (((size_t)tile * w.scale_groups + (b >> 2)) * 32 + lane) * 16);
+    return p[b & 3];
+  }
+}
+
+__device__ __forceinline__ int dot32(const uint4& wa, const uint4& wb, const int4& x0, const int4& x1) {
+  int d = __dp4a((int)wa.x, x0.x, 0);
+  d = __dp4a((int)wa.y, x0.y, d);
+  d = __dp4a((int)wa.z, x0.z, d);
+  d = __dp4a((int)wa.w, x0.w, d);
+  d = __dp4a((int)wb.x, x1.x, d);
+  d = __dp4a((int)wb.y, x1.y, d);
+  d = __dp4a((int)wb.z, x1.z, d);
+  d = __dp4a((int)wb.w, x1.w, d);
+  return d;
+}
+
+// (value, index) ordering of QwenDecoder.Greedy: larger value wins, equal
+// values keep the lower index, NaN never wins.
+__device__ __forceinline__ bool better(float v2, int i2, float v1, int i1) {
+  if (isnan(v2)) return false;
+  if (isnan(v1)) return true;
+  return v2 > v1 || (v2 == v1 && i2 < i1);
+}
+
+struct GemvSmem {
+  int xq, xs, prod, red, total;
+};
+
+__host__ __device__ inline GemvSmem gemv_smem_layout(int K, int tiles_per_cta) {
+  GemvSmem s;
+  int B = K / 32;
+  s.xq = 0;
+  s.xs = (kGemvFrames * K + 15) & ~15;
+  s.prod = (s.xs + kGemvFrames * B * 4 + 15) & ~15;
+  s.red = (s.prod + kGemvFrames * tiles_per_cta * B * 32 * 4 + 15) & ~15;
+  s.total = s.red + 16 * 8;
+  return s;
+}
+
+// Fused [RMSNorm] -> per-32-block int8 quantisation -> Q8 W8A8 GEMV -> epilogue.
+// One CTA owns one 32-row tile (two for the gate/up pair) and up to 4 frames.
+// Warps split the (tile, block) units; each lane handles one row and stores
+// the block products p_b = ((float)dot_b * ws) * xs, then warp 0 sums them in
+// block order, which is the reference's accumulation order
+// (TensorMath.QuantizedRowsAvx.cs:30-41, TensorMath.QuantizedGroupAvx.cs:121-132).
+template <bool F16S>
+__global__ void __launch_bounds__(kGemvThreads) gemv_kernel(const GemvArgs a) {
+  if (skipped(a.skip)) return;
+  extern __shared__ __align__(16) uint8_t smem[];
+  const int K = a.w.cols, B = K / 32;
+  const int tpc = a.epilogue == kEpiSiluPair ? 2 : 1;
+  const GemvSmem L = gemv_smem_layout(K, tpc);
+  int8_t* xq = reinterpret_cast<int8_t*>(smem + L.xq);
+  float* xs = reinterpret_cast<float*>(smem + L.xs);
+  float* prod = reinterpret_cast<float*>(smem + L.prod);
+  double* red = reinterpret_cast<double*>(smem + L.red);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int tile0 = blockIdx.x * tpc;
+  const int f0 = blockIdx.y * kGemvFrames;
+  const int fc = min(kGemvFrames, a.frames - f0);
+
+  // ---- prologue: activations of this CTA's frames, quantised into smem ----
+  for (int fi = 0; fi < fc; ++fi) {
+    const float* xr = a.x + (size_t)(f0 + fi) * K;
+    float inv = 1.0f;
+    if (a.gamma != nullptr) {
+      double part = 0.0;
+      for (int k = threadIdx.x; k < K; k += kGemvThreads) {
+        double z = (double)xr[k];
+        part = __dadd_rn(part, __dmul_rn(z, z));
+      }
+      part = warp_sum_d(part);
+      if (lane == 0) red[warp] = part;
+      __syncthreads();
+      double var = 0.0;
+#pragma unroll
+      for (int w = 0; w < kGemvWarps; ++w) var = __dadd_rn(var, red[w]);
+      inv = rms_inverse(var, K, a.eps);
+      __syncthreads();
+    }
+    for (int j = warp; j < B; j += kGemvWarps) {
+      float v = xr[j * 32 + lane];
+      if (a.gamma != nullptr) v = __fmul_rn(__fmul_rn(v, inv), a.gamma[j * 32 + lane]);
+      float d, id;
+      block_scale(v, d, id);
+      xq[fi * K + j * 32 + lane] = (int8_t)quant1(v, id);
+      if (lane == 0) xs[fi * B + j] = d;
+    }
+  }
+  __syncthreads();
+
+  // ---- main loop: stream the tile(s), one 32-value block per unit ----
+  const int units = tpc * B;
+  for (int u0 = warp; u0 < units; u0 += kGemvWarps * kGemvUnroll) {
+    uint4 wa[kGemvUnroll], wb[kGemvUnroll];
+    float ws[kGemvUnroll];
+#pragma unroll
+    for (int i = 0; i < kGemvUnroll; ++i) {
+      const int u = u0 + kGemvWarps * i;
+      if (u < units) {
+        const int t = u / B, b = u - t * B, tile = tile0 + t;
+        const uint8_t* tq = a.w.q + (size_t)tile * 32 * K;
+        wa[i] = __ldg(reinterpret_cast<const uint4*>(tq + (size_t)(2 * b) * 512 + lane * 16));
+        wb[i] = __ldg(reinterpret_cast<const uint4*>(tq + (size_t)(2 * b + 1) * 512 + lane * 16));
+        ws[i] = load_scale<F16S>(a.w, tile, b, lane);
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < kGemvUnroll; ++i) {
+      const int u = u0 + kGemvWarps * i;
+      if (u < units) {
+        const int t = u / B, b = u - t * B;
+        for (int fi = 0; fi < fc; ++fi) {
+          const int4* xp = reinterpret_cast<const int4*>(xq + fi * K + b * 32);
+          const int dot = dot32(wa[i], wb[i], xp[0], xp[1]);
+          const float p = __fmul_rn(__fmul_rn(__int2float_rn(dot), ws[i]), xs[fi * B + b]);
+          prod[((fi * tpc + t) * B + b) * 32 + lane] = p;
+        }
+      }
+    }
+  }
+  __syncthreads();
+
+  // ---- ordered block sums + epilogue (warp 0: lane = row) ----
+  if (warp != 0) return;
+  const int N = a.w.rows;
+  if (a.epilogue == kEpiSiluPair) {
+    const int row = blockIdx.x * 32 + lane;  // gate/up row of this pair
+    for (int fi = 0; fi < fc; ++fi) {
+      float g = 0.0f, u = 0.0f;
+      const float* pg = prod + (size_t)(fi * 2 + 0) * B * 32 + lane;
+      const float* pu = prod + (size_t)(fi * 2 + 1) * B * 32 + lane;
+      for (int b = 0; b < B; ++b) g = __fadd_rn(g, pg[b * 32]);
+      for (int b = 0; b < B; ++b) u = __fadd_rn(u, pu[b * 32]);
+      // TensorMath.Elementwise.cs:180: g / (1 + exp(-g)) * u
+      const float act = __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), u);
+      if (row < a.out_stride) a.out[(size_t)(f0 + fi) * a.out_stride + row] = act;
+    }
+    return;
+  }
+  const int row = tile0 * 32 + lane;
+  if (a.epilogue == kEpiArgmax) {
+    float s = 0.0f;
+    const float* pp = prod + lane;
+    for (int b = 0; b < B; ++b) s = __fadd_rn(s, pp[b * 32]);
+    const bool valid = row < N;
+    if (valid && a.logits != nullptr) a.logits[row] = s;
+    float bv = valid ? s : __int_as_float(0x7fc00000);
+    int bi = valid ? row : INT_MAX;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+      int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      if (better(ov, oi, bv, bi)) {
+        bv = ov;
+        bi = oi;
+      }
+    }
+    unsigned last = 0u;
+    if (lane == 0) {
+      a.am.part_value[blockIdx.x] = bv;
+      a.am.part_index[blockIdx.x] = bi;
+      if (blockIdx.x == 0) *a.am.row0_nan = isnan(s) ? 1 : 0;  // lane 0 of CTA 0 holds row 0
+      __threadfence();
+      last = atomicAdd(a.am.counter, 1u) == gridDim.x - 1 ? 1u : 0u;
+    }
+    if (__shfl_sync(0xffffffffu, last, 0) == 0u) return;
+    __threadfence();
+    float best_v = __int_as_float(0x7fc00000);
+    int best_i = INT_MAX;
+    for (int c = lane; c < (int)gridDim.x; c += 32) {
+      float v = __ldcg(a.am.part_value + c);
+      int i = __ldcg(a.am.part_index + c);
+      if (better(v, i, best_v, best_i)) {
+        best_v = v;
+        best_i = i;
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      float ov = __shfl_xor_sync(0xffffffffu, best_v, o);
+      int oi = __shfl_xor_sync(0xffffffffu, best_i, o);
+      if (better(ov, oi, best_v, best_i)) {
+        best_v = ov;
+        best_i = oi;
+      }
+    }
+    if (lane == 0) {
+      const int nan0 = __ldcg(a.am.row0_nan);
+      *a.am.token = (nan0 || best_i == INT_MAX) ? 0 : best_i;
+      *a.am.counter = 0u;
+    }
+    return;
+  }
+  if (row >= N) return;
+  for (int fi = 0; fi < fc; ++fi) {
+    float s = 0.0f;
+    const float* pp = prod + (size_t)fi * B * 32 + lane;
+    for (int b = 0; b < B; ++b) s = __fadd_rn(s, pp[b * 32]);
+    float* o = a.out + (size_t)(f0 + fi) * a.out_stride + row;
+    if (a.epilogue == kEpiResidual) {
+      *o = __fadd_rn(s, a.res[(size_t)(f0 + fi) * a.out_stride + row]);
+    } else {
+      *o = a.bias != nullptr ? __fadd_rn(a.bias[row], s) : s;
+    }
+  }
+}
+
+// ---------------------------------------------------------------- misc ----
+
+__global__ void quantize_kernel(const float* x, long long blocks, int8_t* q, float* scales) {
+  const long long j = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (j >= blocks) return;  // warp-uniform
+  const float v = x[j * 32 + lane];
+  float d, inv;
+  block_scale(v, d, inv);
+  q[j * 32 + lane] = (int8_t)quant1(v, inv);
+  if (lane == 0) scales[j] = d;
+}
+
+// One CTA per row; blockDim = 256.
+__global__ void rmsnorm_kernel(const float* x, int width, const float* gamma, float eps, float* y) {
+  __shared__ double red[8];
+  const float* xr = x + (size_t)blockIdx.x * width;
+  float* yr = y + (size_t)blockIdx.x * width;
+  double part = 0.0;
+  for (int k = threadIdx.x; k < width; k += blockDim.x) {
+    double z = (double)xr[k];
+    part = __dadd_rn(part, __dmul_rn(z, z));
+  }
+  part = warp_sum_d(part);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = part;
+  __syncthreads();
+  double var = 0.0;
+  for (int w = 0; w < (int)(blockDim.x >> 5); ++w) var = __dadd_rn(var, red[w]);
+  const float inv = rms_inverse(var, width, eps);
+  for (int k = threadIdx.x; k < width; k += blockDim.x) yr[k] = __fmul_rn(__fmul_rn(xr[k], inv), gamma[k]);
+}
+
+__global__ void round_half_kernel(const float* x, long long n, float* y) {
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x)
+    y[i] = __half2float(__float2half_rn(x[i]));
+}
+
+__global__ void silu_mul_kernel(float* g, const float* u, long long n) {
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+    const float v = g[i];
+    g[i] = __fmul_rn(__fdiv_rn(v, __fadd_rn(1.0f, expf(-v))), u[i]);
+  }
+}
+
+// Single-CTA first-max argmax (1024 threads).
+__global__ void greedy_kernel(const float* logits, int n, int* token) {
+  __shared__ float sv[32];
+  __shared__ int si[32];
+  float bv = __int_as_float(0x7fc00000);
+  int bi = INT_MAX;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    const float v = logits[i];
+    if (better(v, i, bv, bi)) {
+      bv = v;
+      bi = i;
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+    int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+    if (better(ov, oi, bv, bi)) {
+      bv = ov;
+      bi = oi;
+    }
+  }
+  if ((threadIdx.x & 31) == 0) {
+    sv[threadIdx.x >> 5] = bv;
+    si[threadIdx.x >> 5] = bi;
+  }
+  __syncthreads();
+  if (threadIdx.x >= 32) return;
+  const int nw = blockDim.x >> 5;
+  bv = threadIdx.x < nw ? sv[threadIdx.x] : __int_as_float(0x7fc00000);
+  bi = threadIdx.x < nw ? si[threadIdx.x] : INT_MAX;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+    int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+    if (better(ov, oi, bv, bi)) {
+      bv = ov;
+      bi = oi;
+    }
+  }
+  if (threadIdx.x == 0) *token = (n <= 0 || isnan(logits[0]) || bi == INT_MAX) ? 0 : bi;
+}
+
+// Weight.CopyRow of a Q8 tile-layout matrix: x[j] = q[j] * scale[j / 32]
+// (Gguf.cs:340-344).  One CTA per frame; each thread converts one 16-byte chunk.
+template <bool F16S>
+__global__ void embed_kernel(const Q8View w, const int* tokens, float* x, const int* skip) {
+  if (skipped(skip)) return;
+  const int K = w.cols, f = blockIdx.x;
+  int row = tokens[f];
+  row = row < 0 ? 0 : (row >= w.rows ? w.rows - 1 : row);  // host validates ranges
+  const int tile = row >> 5, r = row & 31;
+  for (int c = threadIdx.x; c < K / 16; c += blockDim.x) {
+    const uint8_t* src = w.q + (size_t)tile * 32 * K + (size_t)c * 512 + r * 16;
+    const uint4 v = *reinterpret_cast<const uint4*>(src);
+    const float s = load_scale<F16S>(w, tile, c >> 1, r);
+    const int8_t* b = reinterpret_cast<const int8_t*>(&v);
+    float* out = x + (size_t)f * K + c * 16;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) out[i] = __fmul_rn((float)b[i], s);
+  }
+}
+
+// --------------------------------------------------------- attention ----
+
+// QK RMSNorm + RoPE + binary16 KV write.  grid (frames, heads + 2*kv_heads),
+// blockDim = head_size (<= 256, multiple of 32 and even).
+__global__ void qk_rope_kv_kernel(const AttnArgs a) {
+  if (skipped(a.skip)) return;
+  __shared__ float y[256];
+  __shared__ double red[8];
+  const int D = a.head_size, half = D / 2, c = threadIdx.x;
+  const int f = blockIdx.x, h = blockIdx.y;
+  const int qw = a.heads * D, kvw = a.kv_heads * D;
+  const int stride = a.qkv_stride ? a.qkv_stride : qw + 2 * kvw;
+  const int p = *a.pos + f;
+  float* base = a.qkv + (size_t)f * stride;
+  if (h < a.heads + a.kv_heads) {
+    const bool isq = h < a.heads;
+    float* xp = isq ? base + h * D : base + qw + (h - a.heads) * D;
+    const float* g = isq ? a.q_norm : a.k_norm;
+    const float v = xp[c];
+    // QwenDecoder.cs:188-192: per-head RMSNorm
+    double part = warp_sum_d(__dmul_rn((double)v, (double)v));
+    if ((c & 31) == 0) red[c >> 5] = part;
+    __syncthreads();
+    double var = 0.0;
+    for (int w = 0; w < D / 32; ++w) var = __dadd_rn(var, red[w]);
+    const float inv = rms_inverse(var, D, a.eps);
+    y[c] = __fmul_rn(__fmul_rn(v, inv), g[c]);
+    __syncthreads();
+    // TensorMath.Rope.cs:51-53 with the QwenDecoder.cs:374-379 table row.
+    const int i = c < half ? c : c - half;
+    const float co = a.rope_cos[(size_t)p * half + i], si = a.rope_sin[(size_t)p * half + i];
+    const float av = y[i], bv = y[i + half];
+    const float o = c < half ? __fsub_rn(__fmul_rn(av, co), __fmul_rn(bv, si))
+                             : __fadd_rn(__fmul_rn(av, si), __fmul_rn(bv, co));
+    if (isq) xp[c] = o;
+    else a.k_cache[(size_t)p * kvw + (h - a.heads) * D + c] = __float2half_rn(o);  // QwenDecoder.cs:199
+  } else {
+    const int vh = h - a.heads - a.kv_heads;
+    a.v_cache[(size_t)p * kvw + vh * D + c] = __float2half_rn(base[qw + kvw + vh * D + c]);  // :200
+  }
+}
+
+// Split-K attention partials for head_size 128 and 2 query heads per KV head
+// (the paired GQA of TensorMath.DecoderAttention.cs:17-52).
+// grid (kv_heads, splits, frames), 128 threads; lane owns channels 4l..4l+3.
+__global__ void __launch_bounds__(128) attn_partial_kernel(const AttnArgs a) {
+  if (skipped(a.skip)) return;
+  constexpr int D = 128;
+  const int g = blockIdx.x, s = blockIdx.y, f = blockIdx.z;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int qw = a.heads * D, kvw = a.kv_heads * D;
+  const int stride = a.qkv_stride ? a.qkv_stride : qw + 2 * kvw;
+  const int len = *a.pos + f + 1;  // causal: frame f sees [0, pos + f]
+  const int chunk = (len + a.splits - 1) / a.splits;
+  const int t0 = s * chunk, t1 = min(len, t0 + chunk);
+  const float* q = a.qkv + (size_t)f * stride + (size_t)(2 * g) * D;
+  float q0[4], q1[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    q0[j] = q[4 * lane + j];
+    q1[j] = q[D + 4 * lane + j];
+  }
+  const float divisor = __fsqrt_rn((float)D);
+  float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.0f, l1 = 0.0f;
+  float acc0[4] = {0, 0, 0, 0}, acc1[4] = {0, 0, 0, 0};
+  for (int t = t0 + warp; t < t1; t += 4) {
+    const __half* kr = a.k_cache + (size_t)t * kvw + g * D + 4 * lane;
+    const __half* vr = a.v_cache + (size_t)t * kvw + g * D + 4 * lane;
+    const uint2 kk = *reinterpret_cast<const uint2*>(kr);
+    const uint2 vv = *reinterpret_cast<const uint2*>(vr);
+    const float2 k01 = __half22float2(*reinterpret_cast<const __half2*>(&kk.x));
+    const float2 k23 = __half22float2(*reinterpret_cast<const __half2*>(&kk.y));
+    const float2 v01 = __half22float2(*reinterpret_cast<const __half2*>(&vv.x));
+    const float2 v23 = __half22float2(*reinterpret_cast<const __half2*>(&vv.y));
+    float d0 = __fmaf_rn(q0[3], k23.y, __fmaf_rn(q0[2], k23.x, __fmaf_rn(q0[1], k01.y, __fmul_rn(q0[0], k01.x))));
+    float d1 = __fmaf_rn(q1[3], k23.y, __fmaf_rn(q1[2], k23.x, __fmaf_rn(q1[1], k01.y, __fmul_rn(q1[0], k01.x))));
+    d0 = warp_sum_f(d0);
+    d1 = warp_sum_f(d1);
+    const float s0 = __fdiv_rn(d0, divisor), s1 = __fdiv_rn(d1, divisor);
+    const float n0 = fmaxf(m0, s0), n1 = fmaxf(m1, s1);
+    const float c0 = expf(m0 - n0), c1 = expf(m1 - n1);
+    const float p0 = expf(s0 - n0), p1 = expf(s1 - n1);
+    l0 = __fmaf_rn(l0, c0, p0);
+    l1 = __fmaf_rn(l1, c1, p1);
+    const float vf[4] = {v01.x, v01.y, v23.x, v23.y};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      acc0[j] = __fmaf_rn(acc0[j], c0, __fmul_rn(p0, vf[j]));
+      acc1[j] = __fmaf_rn(acc1[j], c1, __fmul_rn(p1, vf[j]));
+    }
+    m0 = n0;
+    m1 = n1;
+  }
+  __shared__ float sm[4][2];
+  __shared__ float sl[4][2];
+  __shared__ float sacc[4][2][D];
+  if (lane == 0) {
+    sm[warp][0] = m0;
+    sm[warp][1] = m1;
+    sl[warp][0] = l0;
+    sl[warp][1] = l1;
+  }
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    sacc[warp][0][4 * lane + j] = acc0[j];
+    sacc[warp][1][4 * lane + j] = acc1[j];
+  }
+  __syncthreads();
+  const int c = threadIdx.x;  // channel
+  float* out = a.part + (((size_t)f * a.kv_heads + g) * a.splits + s) * (4 + 2 * D);
+#pragma unroll
+  for (int hh = 0; hh < 2; ++hh) {
+    float M = -INFINITY;
+    for (int w = 0; w < 4; ++w) M = fmaxf(M, sm[w][hh]);
+    float Lsum = 0.0f, A = 0.0f;
+    if (M != -INFINITY) {
+      for (int w = 0; w < 4; ++w) {
+        const float e = expf(sm[w][hh] - M);
+        Lsum = __fmaf_rn(sl[w][hh], e, Lsum);
+        A = __fmaf_rn(sacc[w][hh][c], e, A);
+      }
+    }
+    if (c == 0) {
+      out[hh] = M;
+      out[2 + hh] = Lsum;
+    }
+    out[4 + hh * D + c] = A;
+  }
+}
+
+// grid (frames, heads), 128 threads: merge the split partials of one query head.
+__global__ void __launch_bounds__(128) attn_combine_kernel(const AttnArgs a) {
+  if (skipped(a.skip)) return;
+  constexpr int D = 128;
+  const int f = blockIdx.x, h = blockIdx.y, g = h >> 1, hh = h & 1, c = threadIdx.x;
+  const float* base = a.part + ((size_t)f * a.kv_heads + g) * a.splits * (4 + 2 * D);
+  float M = -INFINITY;
+  for (int s = 0; s < a.splits; ++s) M = fmaxf(M, base[(size_t)s * (4 + 2 * D) + hh]);
+  float Lsum = 0.0f, A = 0.0f;
+  for (int s = 0; s < a.splits; ++s) {
+    const float* p = base + (size_t)s * (4 + 2 * D);
+    const float ms = p[hh];
+    if (ms == -INFINITY) continue;
+    const float e = expf(ms - M);
+    Lsum = __fmaf_rn(p[2 + hh], e, Lsum);
+    A = __fmaf_rn(p[4 + hh * D + c], e, A);
+  }
+  a.attn[(size_t)f * a.heads * D + (size_t)h * D + c] = __fdiv_rn(A, Lsum);
+}
+
+// ------------------------------------------------------------- FP32 ----
+
+constexpr int kF32Frames = 4;
+
+// FP32 GEMV: 8 threads per row, 32 rows per CTA (256 threads), up to 4 frames.
+// Thread j accumulates columns j, j+8, ... sequentially (acc += x * w, two
+// roundings) and the 8 lanes fold as ((a0+a4)+(a1+a5)) + ((a2+a6)+(a3+a7)):
+// FloatRows4Avx's order (TensorMath.FloatRowsAvx.cs:27-47) for frames < 4.
+__global__ void __launch_bounds__(256) gemv_f32_kernel(const F32GemvArgs a) {
+  if (skipped(a.skip)) return;
+  extern __shared__ __align__(16) uint8_t smem[];
+  float* xs = reinterpret_cast<float*>(smem);  // [4][K] permuted
+  __shared__ double red[8];
+  const int K = a.w.cols;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int f0 = blockIdx.y * kF32Frames, fc = min(kF32Frames, a.frames - f0);
+  for (int fi = 0; fi < fc; ++fi) {
+    const float* xr = a.x + (size_t)(f0 + fi) * K;
+    float inv = 1.0f;
+    if (a.gamma != nullptr) {
+      double part = 0.0;
+      for (int k = threadIdx.x; k < K; k += 256) {
+        double z = (double)xr[k];
+        part = __dadd_rn(part, __dmul_rn(z, z));
+      }
+      part = warp_sum_d(part);
+      if (lane == 0) red[warp] = part;
+      __syncthreads();
+      double var = 0.0;
+      for (int w = 0; w < 8; ++w) var = __dadd_rn(var, red[w]);
+      inv = rms_inverse(var, K, a.eps);
+      __syncthreads();
+    }
+    for (int k = threadIdx.x; k < K; k += 256) {
+      float v = xr[k];
+      if (a.gamma != nullptr) v = __fmul_rn(__fmul_rn(v, inv), a.gamma[k]);
+      const int c = k & 31;
+      xs[fi * K + (k & ~31) + 4 * (c & 7) + (c >> 3)] = v;
+    }
+  }
+  __syncthreads();
+  const int row = blockIdx.x * 32 + warp * 4 + (lane >> 3), j = lane & 7;
+  const bool valid = row < a.w.rows;
+  float acc[kF32Frames] = {0, 0, 0, 0};
+  if (valid) {
+    const float* wr = a.w.w + (size_t)row * K + 4 * j;
+    for (int g = 0; g < K; g += 32) {
+      const float4 wv = __ldg(reinterpret_cast<const float4*>(wr + g));
+#pragma unroll
+      for (int fi = 0; fi < kF32Frames; ++fi) {
+        if (fi < fc) {
+          const float4 xv = *reinterpret_cast<const float4*>(xs + fi * K + g + 4 * j);
+          float t = acc[fi];
+          t = __fadd_rn(t, __fmul_rn(xv.x, wv.x));
+          t = __fadd_rn(t, __fmul_rn(xv.y, wv.y));
+          t = __fadd_rn(t, __fmul_rn(xv.z, wv.z));
+          t = __fadd_rn(t, __fmul_rn(xv.w, wv.w));
+          acc[fi] = t;
+        }
+      }
+    }
+  }
+#pragma unroll
+  for (int fi = 0; fi < kF32Frames; ++fi) {
+    float v = acc[fi];
+    v = __fadd_rn(v, __shfl_down_sync(0xffffffffu, v, 4));  // t_j = a_j + a_{j+4}
+    v = __fadd_rn(v, __shfl_down_sync(0xffffffffu, v, 1));  // t0+t1, t2+t3
+    v = __fadd_rn(v, __shfl_down_sync(0xffffffffu, v, 2));  // (t0+t1)+(t2+t3)
+    acc[fi] = v;
+  }
+  if (!valid || j != 0) return;
+  for (int fi = 0; fi < fc; ++fi) {
+    float* o = a.out + (size_t)(f0 + fi) * a.out_stride + row;
+    if (a.epilogue == kEpiResidual) *o = __fadd_rn(acc[fi], a.res[(size_t)(f0 + fi) * a.out_stride + row]);
+    else *o = a.bias != nullptr ? __fadd_rn(a.bias[row], acc[fi]) : __fadd_rn(0.0f, acc[fi]);
+  }
+}
+
+__global__ void silu_pair_kernel(const float* buf, int frames, int ffn, float* act, const int* skip) {
+  if (skipped(skip)) return;
+  const long long n = (long long)frames * ffn;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+    const long long f = i / ffn, k = i - f * ffn;
+    const float g = buf[f * 2 * ffn + k], u = buf[f * 2 * ffn + ffn + k];
+    act[i] = __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), u);
+  }
+}
+
+__global__ void embed_f32_kernel(const F32View w, const int* tokens, float* x, const int* skip) {
+  if (skipped(skip)) return;
+  const int K = w.cols, f = blockIdx.x;
+  int row = tokens[f];
+  row = row < 0 ? 0 : (row >= w.rows ? w.rows - 1 : row);
+  for (int k = threadIdx.x; k < K; k += blockDim.x) {
+    const int c = k & 31;
+    x[(size_t)f * K + k] = w.w[(size_t)row * K + (k & ~31) + 4 * (c & 7) + (c >> 3)];
+  }
+}
+
+__global__ void greedy_dev_kernel(const float* logits, int n, int* token, const int* skip) {
+  if (skipped(skip)) return;
+  __shared__ float sv[32];
+  __shared__ int si[32];
+  float bv = __int_as_float(0x7fc00000);
+  int bi = INT_MAX;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    const float v = logits[i];
+    if (better(v, i, bv, bi)) {
+      bv = v;
+      bi = i;
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+    int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+    if (better(ov, oi, bv, bi)) {
+      bv = ov;
+      bi = oi;
+    }
+  }
+  if ((threadIdx.x & 31) == 0) {
+    sv[threadIdx.x >> 5] = bv;
+    si[threadIdx.x >> 5] = bi;
+  }
+  __syncthreads();
+  if (threadIdx.x >= 32) return;
+  const int nw = blockDim.x >> 5;
+  bv = threadIdx.x < nw ? sv[threadIdx.x] : __int_as_float(0x7fc00000);
+  bi = threadIdx.x < nw ? si[threadIdx.x] : INT_MAX;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+    int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+    if (better(ov, oi, bv, bi)) {
+      bv = ov;
+      bi = oi;
+    }
+  }
+  if (threadIdx.x == 0) *token = (n <= 0 || isnan(logits[0]) || bi == INT_MAX) ? 0 : bi;
+}
+
+__global__ void step_begin_kernel(const StepState s) {
+  if (*s.stopped) return;
+  const int tok = *s.token;
+  for (int i = 0; i < s.n_end; ++i)
+    if (s.end_ids[i] == tok) {
+      *s.stopped = 1;
+      return;
+    }
+  const int n = *s.step;
+  if (n < s.log_cap) s.log[n] = tok;
+  *s.step = n + 1;
+}
+
+__global__ void step_end_kernel(const StepState s, int frames) {
+  if (s.stopped != nullptr && *s.stopped) return;
+  *s.pos += frames;
+}
+
+// Opts every GEMV instantiation into the full 227 KB of dynamic shared memory
+// once per device (the per-launch request still sets the occupancy).
+void ensure_gemv_attributes() {
+  constexpr int kMaxDevices = 64;
+  static std::once_flag flags[kMaxDevices];
+  int dev = 0;
+  FA_CUDA(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= kMaxDevices) throw Error(kErrCuda, "device index out of range");
+  std::call_once(flags[dev], [] {
+    FA_CUDA(cudaFuncSetAttribute(gemv_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemvMaxSmem));
+    FA_CUDA(cudaFuncSetAttribute(gemv_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemvMaxSmem));
+    FA_CUDA(cudaFuncSetAttribute(gemv_f32_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemvMaxSmem));
+  });
+}
+
+}  // namespace
+
+void prepare_kernels() { ensure_gemv_attributes(); }
+
+int gemv_smem_bytes(int K, int epilogue) {
+  return gemv_smem_layout(K, epilogue == kEpiSiluPair ? 2 : 1).total;
+}
+
+void launch_gemv(const GemvArgs& a, cudaStream_t stream) {
+  const int tpc = a.epilogue == kEpiSiluPair ? 2 : 1;
+  const int smem = gemv_smem_layout(a.w.cols, tpc).total;
+  if (smem > kGemvMaxSmem) throw Error(kErrCapacity, "GEMV inner dimension too large for shared memory");
+  ensure_gemv_attributes();
+  dim3 grid((a.w.tiles + tpc - 1) / tpc, (a.frames + kGemvFrames - 1) / kGemvFrames);
+  if (a.epilogue == kEpiArgmax && a.frames != 1) throw Error(kErrArgument, "argmax epilogue needs one frame");
+  if (a.w.scale_f16) {
+    gemv_kernel<true><<<grid, kGemvThreads, smem, stream>>>(a);
+  } else {
+    gemv_kernel<false><<<grid, kGemvThreads, smem, stream>>>(a);
+  }
+  FA_CUDA(cudaGetLastError());
+}
+
+void launch_quantize(const float* x, long long n, int8_t* q, float* scales, cudaStream_t stream) {
+  const long long blocks = n / 32;
+  if (blocks == 0) return;
+  const int warps = 8;
+  quantize_kernel<<<(unsigned)((blocks + warps - 1) / warps), warps * 32, 0, stream>>>(x, blocks, q, scales);
+  FA_CUDA(cudaGetLastError());
+}
+
+void launch_rmsnorm(const float* x, long long rows, int width, const float* gamma, float eps, float* y,
+                    cudaStream_t stream) {
+  if (rows == 0) return;
+  rmsnorm_kernel<<<(unsigned)rows, 256, 0, stream>>>(x, width, gamma, eps, y);
+  FA_CUDA(cudaGetLastError());
+}
+
+void launch_round_half(const float* x, long long n, float* y, cudaStream_t stream) {
+  if (n == 0) return;
+  round_half_kernel<<<(unsigned)std::min<long long>(4096, (n + 255) / 256), 256, 0, stream>>>(x, n, y);
+  FA_CUDA(cudaGetLastError());
+}
+
+void launch_silu_mul(float* gate, const float* up, long long n, cudaStream_t stream) {
+  if (n == 0) return;
+  silu_mul_kernel<<<(unsigned)std::min<long long>(4096, (n + 255) / 256), 256, 0, stream>>>(gate, up, n);
+  FA_CUDA(cudaGetLastError());
+}
+
+void launch_greedy(const float* logits, int n, void*, int* token, cudaStream_t stream) {
+  greedy_kernel<<<1, 1024, 0, stream>>>(logits, n, token);
+  FA_CUDA(cudaGetLastError());
+}
+
+void launch_embed(const Q8View& emb, const int* tokens, int frames, float* x, const int* skip,
+                  cudaStream_t stream) {
+  if (emb.scale_f16) embed_kernel<true><<<frames, 64, 0, stream>>>(emb, tokens, x, skip);
+  else embed_kernel<false><<<frames, 64, 0, stream>>>(emb, tokens, x, skip);
+  FA_CUDA(cudaGetLastError());
+}
+
+void launch_qk_rope_kv(const AttnArgs& a, cudaStream_t stream) {
+  if (a.head_size > 256 || a.head_size % 32 != 0) throw Error(kErrArgument, "head size must be a multiple of 32 up to 256");
+  dim3 grid(a.frames, a.heads + 2 * a.kv_heads);
+  qk_rope_kv_kernel<<<grid, a.head_size, 0, stream>>>(a);
+  FA_CUDA(cudaGetLastError());
+}
+
+void launch_attention(const AttnArgs& a, cudaStream_t stream) {
+  if (a.head_size != 128 || a.heads != 2 * a.kv_heads)
+    throw Error(kErrArgument, "attention kernel needs head_size 128 and 2 query heads per KV head");
+  dim3 g1(a.kv_heads, a.splits, a.frames);
+  attn_partial_kernel<<<g1, 128, 0, stream>>>(a);
+  FA_CUDA(cudaGetLastError());
+  dim3 g2(a.frames, a.heads);
+  attn_combine_kernel<<<g2, 128, 0, stream>>>(a);
+  FA_CUDA(cudaGetLastError());
+}
+
+void pack_f32(const float* w, int rows, int cols, float* out) {
+  for (long long r = 0; r < rows; ++r)
+    for (int k = 0; k < cols; ++k) {
+      const int c = k & 31;
+      out[r * cols + (k & ~31) + 4 * (c & 7) + (c >> 3)] = w[r * cols + k];
+    }
+}
+
+int gemv_f32_smem_bytes(int K) { return kF32Frames * K * 4; }
+
+void launch_gemv_f32(const F32GemvArgs& a, cudaStream_t stream) {
+  const int smem = gemv_f32_smem_bytes(a.w.cols);
+  if (smem > kGemvMaxSmem) throw Error(kErrCapacity, "GEMV inner dimension too large for shared memory");
+  if (a.w.cols % 32 != 0) throw Error(kErrArgument, "FP32 GEMV needs cols % 32 == 0");
+  ensure_gemv_attributes();
+  dim3 grid((a.w.rows + 31) / 32, (a.frames + kF32Frames - 1) / kF32Frames);
+  gemv_f32_kernel<<<grid, 256, smem, stream>>>(a);
+  FA_CUDA(cudaGetLastError());
+}
+
+void launch_silu_pair(const float* buf, int frames, int ffn, float* act, const int* skip, cudaStream_t stream) {
+  const long long n = (long long)frames * ffn;
+  silu_pair_kernel<<<(unsigned)std::min<long long>(2048, (n + 255) / 256), 256, 0, stream>>>(buf, frames, ffn, act, skip);
+  FA_CUDA(cudaGetLastError());
+}
+
+void launch_embed_f32(const F32View& w, const int* tokens, int frames, float* x, const int* skip,
+                      cudaStream_t stream) {
+  embed_f32_kernel<<<frames, 256, 0, stream>>>(w, tokens, x, skip);
+  FA_CUDA(cudaGetLastError());
+}
+
+void launch_greedy_dev(const float* logits, int n, int* token, const int* skip, cudaStream_t stream) {
+  greedy_dev_kernel<<<1, 1024, 0, stream>>>(logits, n, token, skip);
+  FA_CUDA(cudaGetLastError());
+}
+
+void launch_step_begin(const StepState& s, cudaStream_t stream) {
+  step_begin_kernel<<<1, 1, 0, stream>>>(s);
+  FA_CUDA(cudaGetLastError());
+}
+
+void launch_step_end(const StepState& s, int frames, cudaStream_t stream) {
+  step_end_kernel<<<1, 1, 0, stream>>>(s, frames);
+  FA_CUDA(cudaGetLastError());
+}
+
+}  // namespace fa

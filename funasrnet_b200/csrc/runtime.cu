@@ -1,0 +1,1287 @@
+// Host runtime behind the C ABI (include/funasr_cuda.h): backend and weight
+// residency, GGUF model upload into the tile layout, decoder sessions whose
+// single-token step is captured once and replayed as a CUDA graph.
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <memory>
+#include <mutex>
+#include <set>
+#include <string>
+#include <vector>
+
+#include "../../include/funasr_cuda.h"
+#include "fa_common.h"
+#include "gguf.h"
+#include "kernels.h"
+
+using namespace fa;
+
+namespace {
+
+constexpr int kMaxChunkFrames = 64;   // prefill frames per kernel sequence
+constexpr int kAttnSplits = 16;       // split-K CTAs per (frame, KV head)
+
+struct DevBuf {
+  void* p = nullptr;
+  size_t bytes = 0;
+  DevBuf() = default;
+  DevBuf(const DevBuf&) = delete;
+  DevBuf& operator=(const DevBuf&) = delete;
+  ~DevBuf() { release(); }
+  void release() {
+    if (p) cudaFree(p);
+    p = nullptr;
+    bytes = 0;
+  }
+  void ensure(size_t n) {
+    if (n <= bytes) return;
+    release();
+    FA_CUDA(cudaMalloc(&p, n));
+    bytes = n;
+  }
+  template <typename T> T* as() const { return static_cast<T*>(p); }
+};
+
+struct DeviceGuard {
+  int prev = -1;
+  explicit DeviceGuard(int dev) {
+    FA_CUDA(cudaGetDevice(&prev));
+    if (prev != dev) FA_CUDA(cudaSetDevice(dev));
+  }
+  ~DeviceGuard() {
+    int cur = -1;
+    if (cudaGetDevice(&cur) == cudaSuccess && cur != prev && prev >= 0) cudaSetDevice(prev);
+  }
+};
+
+template <typename F>
+int guarded(F&& body) {
+  try {
+    return body();
+  } catch (const Error& e) {
+    set_last_error(e.what());
+    return e.code;
+  } catch (const std::bad_alloc&) {
+    set_last_error("host allocation failed");
+    return kErrCapacity;
+  } catch (const std::exception& e) {
+    set_last_error(e.what());
+    return kErrArgument;
+  }
+}
+
+}  // namespace
+
+struct fa_weight {
+  fa_backend* owner = nullptr;
+  int rows = 0, cols = 0;
+  bool q8 = false;
+  DevBuf q, s, f32;
+  Q8View view;
+  F32View fview;
+};
+
+struct fa_backend {
+  int device = 0;
+  cudaStream_t stream = nullptr;
+  std::mutex mu;
+  bool disposed = false;
+  std::string name;
+  std::set<fa_weight*> weights;
+  int models = 0;
+  DevBuf in, out, aux, aux2;
+  std::vector<float> staging;
+};
+
+struct LayerDev {
+  Q8View qkv, o, gateup, down;
+  F32View fqkv, fo, fgateup, fdown;
+  const float *attn_norm = nullptr, *q_norm = nullptr, *k_norm = nullptr, *ffn_norm = nullptr;
+};
+
+struct fa_model {
+  fa_backend* backend = nullptr;
+  int width = 0, heads = 0, kv_heads = 0, head_size = 0, layers = 0, vocab = 0, ffn = 0, capacity = 0;
+  float eps = 1e-6f, rope_base = 1e6f;
+  bool quantized = true;
+  DevBuf arena;
+  std::vector<LayerDev> L;
+  Q8View embed, lm;
+  F32View fembed, flm;
+  const float* out_norm = nullptr;
+  const float* rope_cos = nullptr;
+  const float* rope_sin = nullptr;
+  int64_t weight_bytes = 0;
+  int sessions = 0;
+};
+
+struct fa_session {
+  fa_model* m = nullptr;
+  int device = 0;
+  cudaStream_t stream = nullptr;
+  std::mutex mu;
+  int pos = 0;             // host mirror of the device KV length
+  int cached_prefix = 0;
+  bool have_token = false; // a device argmax exists (a Decode with logits ran)
+  DevBuf k_cache, v_cache;  // [layers][capacity][kv_width] f16
+  DevBuf x, a, qkv, attn, act, gu, part, logits, am_val, am_idx, ints, end_ids, log;
+  // ints: 0 pos, 1 token, 2 step, 3 stopped, 4 row0_nan, 5 counter, 6 scratch token
+  int log_cap = 0;
+  int n_end_graph = -1;
+  cudaGraphExec_t step_graph = nullptr;      // host-token step (no end test)
+  cudaGraphExec_t gen_graph = nullptr;       // generate iteration (end test + log)
+  int* pinned = nullptr;                     // pinned host words
+  cudaEvent_t ev0 = nullptr, ev1 = nullptr;
+  float last_ms = 0.0f;
+  int gen_kernels = 0;                       // kernel nodes in gen_graph
+  int* d_int(int i) const { return ints.as<int>() + i; }
+};
+
+// ------------------------------------------------------------ helpers ----
+
+static void check_backend(fa_backend* b) {
+  if (b == nullptr) throw Error(kErrArgument, "null backend");
+  if (b->disposed) throw Error(kErrDisposed, "backend disposed");
+}
+
+static Q8View make_view(const void* q, const void* s, int rows, int cols, bool f16) {
+  Q8View v;
+  v.q = static_cast<const uint8_t*>(q);
+  v.s = s;
+  v.rows = rows;
+  v.cols = cols;
+  v.tiles = (rows + kTileRows - 1) / kTileRows;
+  v.scale_f16 = f16 ? 1 : 0;
+  v.scale_groups = q8_scale_groups(cols, f16);
+  return v;
+}
+
+// ------------------------------------------------------------ C ABI ----
+
+extern "C" {
+
+const char* fa_last_error(void) { return last_error(); }
+const char* fa_version(void) { return "funasrnet_b200 0.1 (sm_100a)"; }
+
+int fa_backend_create(int device, fa_backend** out) {
+  return guarded([&] {
+    if (!out) throw Error(kErrArgument, "null output");
+    int count = 0;
+    FA_CUDA(cudaGetDeviceCount(&count));
+    if (device < 0 || device >= count) throw Error(kErrArgument, "no such CUDA device");
+    auto b = std::make_unique<fa_backend>();
+    b->device = device;
+    DeviceGuard g(device);
+    cudaDeviceProp prop;
+    FA_CUDA(cudaGetDeviceProperties(&prop, device));
+    if (prop.major < 10) throw Error(kErrCuda, std::string("sm_100a build needs a Blackwell GPU, found ") + prop.name);
+    FA_CUDA(cudaStreamCreateWithFlags(&b->stream, cudaStreamNonBlocking));
+    prepare_kernels();
+    b->name = std::string("CUDA ") + prop.name + " (sm_" + std::to_string(prop.major) + std::to_string(prop.minor) + ")";
+    *out = b.release();
+    return (int)kHandled;
+  });
+}
+
+int fa_backend_destroy(fa_backend* b) {
+  return guarded([&] {
+    if (!b) throw Error(kErrArgument, "null backend");
+    {
+      std::lock_guard<std::mutex> lk(b->mu);
+      if (b->disposed) throw Error(kErrDisposed, "backend already disposed");
+      if (b->models > 0) throw Error(kErrArgument, "free the backend's models before disposing it");
+      DeviceGuard g(b->device);
+      cudaStreamSynchronize(b->stream);
+      for (auto* w : b->weights) delete w;
+      b->weights.clear();
+      b->in.release();
+      b->out.release();
+      b->aux.release();
+      b->aux2.release();
+      cudaStreamDestroy(b->stream);
+      b->disposed = true;
+    }
+    delete b;
+    return (int)kHandled;
+  });
+}
+
+const char* fa_backend_name(const fa_backend* b) { return b ? b->name.c_str() : ""; }
+
+int fa_weight_upload_q8(fa_backend* b, const int8_t* q, const float* scales, int rows, int cols, fa_weight** out) {
+  return guarded([&] {
+    check_backend(b);
+    if (!q || !scales || !out || rows <= 0 || cols <= 0 || cols % 32 != 0)
+      throw Error(kErrArgument, "Q8 weight needs rows > 0 and cols a positive multiple of 32");
+    std::lock_guard<std::mutex> lk(b->mu);
+    DeviceGuard g(b->device);
+    const size_t nscales = (size_t)rows * (cols / 32);
+    const bool f16 = scales_fit_f16(scales, nscales);
+    std::vector<uint8_t> hq(q8_bytes_q(rows, cols)), hs(q8_bytes_s(rows, cols, f16));
+    pack_q8(q, scales, rows, cols, f16, hq.data(), hs.data());
+    auto w = std::make_unique<fa_weight>();
+    w->owner = b;
+    w->rows = rows;
+    w->cols = cols;
+    w->q8 = true;
+    w->q.ensure(hq.size());
+    w->s.ensure(hs.size());
+    FA_CUDA(cudaMemcpy(w->q.p, hq.data(), hq.size(), cudaMemcpyHostToDevice));
+    FA_CUDA(cudaMemcpy(w->s.p, hs.data(), hs.size(), cudaMemcpyHostToDevice));
+    w->view = make_view(w->q.p, w->s.p, rows, cols, f16);
+    b->weights.insert(w.get());
+    *out = w.release();
+    return (int)kHandled;
+  });
+}
+
+int fa_weight_upload_f32(fa_backend* b, const float* values, int rows, int cols, fa_weight** out) {
+  return guarded([&] {
+    check_backend(b);
+    if (!values || !out || rows <= 0 || cols <= 0) throw Error(kErrArgument, "invalid FP32 weight");
+    std::lock_guard<std::mutex> lk(b->mu);
+    DeviceGuard g(b->device);
+    auto w = std::make_unique<fa_weight>();
+    w->owner = b;
+    w->rows = rows;
+    w->cols = cols;
+    w->q8 = false;
+    if (cols % 32 == 0) {
+      std::vector<float> packed((size_t)rows * cols);
+      pack_f32(values, rows, cols, packed.data());
+      w->f32.ensure(packed.size() * 4);
+      FA_CUDA(cudaMemcpy(w->f32.p, packed.data(), packed.size() * 4, cudaMemcpyHostToDevice));
+      w->fview.w = w->f32.as<float>();
+      w->fview.rows = rows;
+      w->fview.cols = cols;
+    }
+    b->weights.insert(w.get());
+    *out = w.release();
+    return (int)kHandled;
+  });
+}
+
+int fa_weight_release(fa_backend* b, fa_weight* w) {
+  return guarded([&] {
+    check_backend(b);
+    std::lock_guard<std::mutex> lk(b->mu);
+    if (!w || w->owner != b || !b->weights.count(w)) throw Error(kErrArgument, "weight not owned by this backend");
+    DeviceGuard g(b->device);
+    FA_CUDA(cudaStreamSynchronize(b->stream));
+    b->weights.erase(w);
+    delete w;
+    return (int)kHandled;
+  });
+}
+
+static int run_linear(fa_backend* b, const float* input, int frames, const fa_weight* w, const float* bias,
+                      float* output, bool want_q8) {
+  check_backend(b);
+  if (!w || w->owner != b) throw Error(kErrArgument, "weight not owned by this backend");
+  if (w->q8 != want_q8) return kDeclined;
+  if (frames <= 0) return kDeclined;
+  if (!input || !output) throw Error(kErrArgument, "null input or output");
+  if (want_q8 && gemv_smem_bytes(w->cols, kEpiStore) > 227 * 1024) return kDeclined;
+  if (!want_q8 && (w->fview.w == nullptr || gemv_f32_smem_bytes(w->cols) > 227 * 1024)) return kDeclined;
+  std::lock_guard<std::mutex> lk(b->mu);
+  if (b->disposed) throw Error(kErrDisposed, "backend disposed");
+  DeviceGuard g(b->device);
+  const size_t in_n = (size_t)frames * w->cols, out_n = (size_t)frames * w->rows;
+  b->in.ensure(in_n * 4);
+  b->out.ensure(out_n * 4);
+  FA_CUDA(cudaMemcpyAsync(b->in.p, input, in_n * 4, cudaMemcpyHostToDevice, b->stream));
+  const float* dbias = nullptr;
+  if (bias) {
+    b->aux.ensure((size_t)w->rows * 4);
+    FA_CUDA(cudaMemcpyAsync(b->aux.p, bias, (size_t)w->rows * 4, cudaMemcpyHostToDevice, b->stream));
+    dbias = b->aux.as<float>();
+  }
+  if (want_q8) {
+    GemvArgs a;
+    a.x = b->in.as<float>();
+    a.frames = frames;
+    a.w = w->view;
+    a.epilogue = kEpiStore;
+    a.out = b->out.as<float>();
+    a.out_stride = w->rows;
+    a.bias = dbias;
+    launch_gemv(a, b->stream);
+  } else {
+    F32GemvArgs a;
+    a.x = b->in.as<float>();
+    a.frames = frames;
+    a.w = w->fview;
+    a.epilogue = kEpiStore;
+    a.out = b->out.as<float>();
+    a.out_stride = w->rows;
+    a.bias = dbias;
+    launch_gemv_f32(a, b->stream);
+  }
+  FA_CUDA(cudaMemcpyAsync(output, b->out.p, out_n * 4, cudaMemcpyDeviceToHost, b->stream));
+  FA_CUDA(cudaStreamSynchronize(b->stream));
+  return kHandled;
+}
+
+int fa_try_quantized_linear(fa_backend* b, const float* input, int frames, const fa_weight* w, const float* bias,
+                            float* output) {
+  return guarded([&] { return run_linear(b, input, frames, w, bias, output, true); });
+}
+
+int fa_try_linear(fa_backend* b, const float* input, int frames, const fa_weight* w, const float* bias,
+                  float* output) {
+  return guarded([&] { return run_linear(b, input, frames, w, bias, output, false); });
+}
+
+int fa_try_linear_many(fa_backend* b, const float* input, int frames, const fa_weight* const* weights, int count,
+                       float* const* outputs) {
+  return guarded([&] {
+    check_backend(b);
+    // VulkanGroupedBackend.cs:23-31: needs >= 2 Q8 weights of equal width.
+    if (!weights || !outputs || count < 2 || frames <= 0) return (int)kDeclined;
+    for (int i = 0; i < count; ++i) {
+      if (!weights[i] || weights[i]->owner != b) throw Error(kErrArgument, "weight not owned by this backend");
+      if (!weights[i]->q8 || weights[i]->cols != weights[0]->cols) return (int)kDeclined;
+      if (!outputs[i]) throw Error(kErrArgument, "null output");
+    }
+    for (int i = 0; i < count; ++i) {
+      int rc = run_linear(b, input, frames, weights[i], nullptr, outputs[i], true);
+      if (rc != kHandled) return rc;
+    }
+    return (int)kHandled;
+  });
+}
+
+}  // extern "C"
+
+// ----------------------------------------------------------- single ops ----
+
+template <typename F>
+static int with_backend(fa_backend* b, F&& body) {
+  return guarded([&] {
+    check_backend(b);
+    std::lock_guard<std::mutex> lk(b->mu);
+    if (b->disposed) throw Error(kErrDisposed, "backend disposed");
+    DeviceGuard g(b->device);
+    int rc = body();
+    FA_CUDA(cudaStreamSynchronize(b->stream));
+    return rc;
+  });
+}
+
+extern "C" {
+
+int fa_op_quantize(fa_backend* b, const float* x, int64_t n, int8_t* q, float* scales) {
+  return with_backend(b, [&] {
+    if (n < 0 || n % 32 != 0) throw Error(kErrArgument, "Quantization needs matching complete blocks");
+    if (n == 0) return (int)kHandled;
+    if (!x || !q || !scales) throw Error(kErrArgument, "null buffer");
+    const size_t qbytes = (size_t)((n + 15) & ~15LL);
+    b->in.ensure(n * 4);
+    b->out.ensure(qbytes + (n / 32) * 4);
+    FA_CUDA(cudaMemcpyAsync(b->in.p, x, n * 4, cudaMemcpyHostToDevice, b->stream));
+    int8_t* dq = b->out.as<int8_t>();
+    float* ds = reinterpret_cast<float*>(b->out.as<uint8_t>() + qbytes);
+    launch_quantize(b->in.as<float>(), n, dq, ds, b->stream);
+    FA_CUDA(cudaMemcpyAsync(q, dq, n, cudaMemcpyDeviceToHost, b->stream));
+    FA_CUDA(cudaMemcpyAsync(scales, ds, (n / 32) * 4, cudaMemcpyDeviceToHost, b->stream));
+    return (int)kHandled;
+  });
+}
+
+int fa_op_rmsnorm(fa_backend* b, const float* x, int64_t n, int width, const float* gamma, float eps, float* y) {
+  return with_backend(b, [&] {
+    if (width <= 0 || n < 0 || n % width != 0) throw Error(kErrArgument, "Invalid normalization dimensions");
+    if (n == 0) return (int)kHandled;
+    b->in.ensure(n * 4);
+    b->out.ensure(n * 4);
+    b->aux.ensure((size_t)width * 4);
+    FA_CUDA(cudaMemcpyAsync(b->in.p, x, n * 4, cudaMemcpyHostToDevice, b->stream));
+    FA_CUDA(cudaMemcpyAsync(b->aux.p, gamma, (size_t)width * 4, cudaMemcpyHostToDevice, b->stream));
+    launch_rmsnorm(b->in.as<float>(), n / width, width, b->aux.as<float>(), eps, b->out.as<float>(), b->stream);
+    FA_CUDA(cudaMemcpyAsync(y, b->out.p, n * 4, cudaMemcpyDeviceToHost, b->stream));
+    return (int)kHandled;
+  });
+}
+
+int fa_op_round_half(fa_backend* b, const float* x, int64_t n, float* y) {
+  return with_backend(b, [&] {
+    if (n < 0) throw Error(kErrArgument, "negative length");
+    if (n == 0) return (int)kHandled;
+    b->in.ensure(n * 4);
+    b->out.ensure(n * 4);
+    FA_CUDA(cudaMemcpyAsync(b->in.p, x, n * 4, cudaMemcpyHostToDevice, b->stream));
+    launch_round_half(b->in.as<float>(), n, b->out.as<float>(), b->stream);
+    FA_CUDA(cudaMemcpyAsync(y, b->out.p, n * 4, cudaMemcpyDeviceToHost, b->stream));
+    return (int)kHandled;
+  });
+}
+
+int fa_op_silu_mul(fa_backend* b, float* gate, const float* up, int64_t n) {
+  return with_backend(b, [&] {
+    if (n < 0) throw Error(kErrArgument, "negative length");
+    if (n == 0) return (int)kHandled;
+    b->in.ensure(n * 4);
+    b->out.ensure(n * 4);
+    FA_CUDA(cudaMemcpyAsync(b->in.p, gate, n * 4, cudaMemcpyHostToDevice, b->stream));
+    FA_CUDA(cudaMemcpyAsync(b->out.p, up, n * 4, cudaMemcpyHostToDevice, b->stream));
+    launch_silu_mul(b->in.as<float>(), b->out.as<float>(), n, b->stream);
+    FA_CUDA(cudaMemcpyAsync(gate, b->in.p, n * 4, cudaMemcpyDeviceToHost, b->stream));
+    return (int)kHandled;
+  });
+}
+
+int fa_op_greedy(fa_backend* b, const float* logits, int64_t n, int32_t* token) {
+  return with_backend(b, [&] {
+    if (n < 0 || n > INT32_MAX) throw Error(kErrArgument, "invalid length");
+    if (!token) throw Error(kErrArgument, "null token");
+    if (n == 0) {
+      *token = 0;
+      return (int)kHandled;
+    }
+    b->in.ensure(n * 4);
+    b->out.ensure(16);
+    FA_CUDA(cudaMemcpyAsync(b->in.p, logits, n * 4, cudaMemcpyHostToDevice, b->stream));
+    launch_greedy(b->in.as<float>(), (int)n, nullptr, b->out.as<int>(), b->stream);
+    FA_CUDA(cudaMemcpyAsync(token, b->out.p, 4, cudaMemcpyDeviceToHost, b->stream));
+    return (int)kHandled;
+  });
+}
+
+int fa_op_attention_pair(fa_backend* b, const float* query, const float* keys, const float* values, int frames,
+                         int kv_heads, int size, float* output) {
+  return with_backend(b, [&] {
+    if (frames < 1 || kv_heads < 1 || size < 1) return (int)kDeclined;
+    if (size != 128) return (int)kDeclined;
+    if (!query || !keys || !values || !output) throw Error(kErrArgument, "null buffer");
+    const int kvw = kv_heads * size, qw = 2 * kvw;
+    // Device buffers: q (f32), k/v caches (f16), partials, attn, pos.
+    std::vector<__half> hk((size_t)frames * kvw), hv((size_t)frames * kvw);
+    for (size_t i = 0; i < hk.size(); ++i) {
+      hk[i] = __float2half_rn(keys[i]);
+      hv[i] = __float2half_rn(values[i]);
+    }
+    const size_t part_n = (size_t)kv_heads * kAttnSplits * (4 + 2 * size);
+    b->in.ensure((size_t)qw * 4 + 16);
+    b->aux.ensure(hk.size() * 2 * 2 + 16);
+    b->aux2.ensure(part_n * 4);
+    b->out.ensure((size_t)qw * 4 + 16);
+    __half* dk = b->aux.as<__half>();
+    __half* dv = dk + hk.size();
+    FA_CUDA(cudaMemcpyAsync(b->in.p, query, (size_t)qw * 4, cudaMemcpyHostToDevice, b->stream));
+    FA_CUDA(cudaMemcpyAsync(dk, hk.data(), hk.size() * 2, cudaMemcpyHostToDevice, b->stream));
+    FA_CUDA(cudaMemcpyAsync(dv, hv.data(), hv.size() * 2, cudaMemcpyHostToDevice, b->stream));
+    int* dpos = reinterpret_cast<int*>(b->out.as<uint8_t>() + (size_t)qw * 4);
+    const int pos = frames - 1;
+    FA_CUDA(cudaMemcpyAsync(dpos, &pos, 4, cudaMemcpyHostToDevice, b->stream));
+    AttnArgs a;
+    a.qkv = b->in.as<float>();
+    a.qkv_stride = qw;
+    a.frames = 1;
+    a.heads = 2 * kv_heads;
+    a.kv_heads = kv_heads;
+    a.head_size = size;
+    a.k_cache = dk;
+    a.v_cache = dv;
+    a.pos = dpos;
+    a.splits = kAttnSplits;
+    a.part = b->aux2.as<float>();
+    a.attn = b->out.as<float>();
+    launch_attention(a, b->stream);
+    FA_CUDA(cudaMemcpyAsync(output, a.attn, (size_t)qw * 4, cudaMemcpyDeviceToHost, b->stream));
+    return (int)kHandled;
+  });
+}
+
+int fa_synth_write_gguf(const char* path, uint64_t seed, int layers, int vocab, int width, int ffn, int quantized) {
+  return guarded([&] {
+    if (!path) throw Error(kErrArgument, "null path");
+    SynthConfig c;
+    c.seed = seed;
+    if (layers > 0) c.layers = layers;
+    if (vocab > 0) c.vocab = vocab;
+    if (width > 0) c.width = width;
+    if (ffn > 0) c.ffn = ffn;
+    c.quantized = quantized ? 1 : 0;
+    write_synthetic_gguf(path, c);
+    return (int)kHandled;
+  });
+}
+
+int fa_synth_normals(uint64_t seed, uint64_t stream, uint64_t start, int64_t n, float* out) {
+  return guarded([&] {
+    if (n < 0 || (n > 0 && !out)) throw Error(kErrArgument, "invalid output");
+    synth_normals(seed, stream, start, n, out);
+    return (int)kHandled;
+  });
+}
+
+}  // extern "C"
+
+// ================================================================ model ====
+
+namespace {
+
+struct Arena {
+  size_t used = 0;
+  size_t take(size_t bytes) {
+    size_t off = (used + 255) & ~(size_t)255;
+    used = off + bytes;
+    return off;
+  }
+};
+
+// Places tiles of one Q8 tensor into a combined tile-layout matrix:
+// source tile i -> destination tile tile_offset + i * tile_step.
+void upload_q8_tensor(const GgufTensor& t, uint8_t* dq, uint8_t* ds, int tile_offset, int tile_step) {
+  const int rows = t.rows(), cols = t.cols();
+  if (t.type != kQ8_0) throw Error(kErrIo, t.name + ": expected Q8_0");
+  std::vector<uint8_t> hq(q8_bytes_q(rows, cols)), hs(q8_bytes_s(rows, cols, true));
+  pack_q8_from_gguf(t.data, rows, cols, hq.data(), hs.data());
+  const int tiles = (rows + kTileRows - 1) / kTileRows;
+  const size_t tq = (size_t)kTileRows * cols, ts = (size_t)q8_scale_groups(cols, true) * kTileRows * 16;
+  FA_CUDA(cudaMemcpy2D(dq + (size_t)tile_offset * tq, tq * tile_step, hq.data(), tq, tq, tiles, cudaMemcpyHostToDevice));
+  FA_CUDA(cudaMemcpy2D(ds + (size_t)tile_offset * ts, ts * tile_step, hs.data(), ts, ts, tiles, cudaMemcpyHostToDevice));
+}
+
+std::vector<float> tensor_f32(const GgufTensor& t) {
+  std::vector<float> v((size_t)t.count());
+  if (t.type == kF32) std::memcpy(v.data(), t.data, v.size() * 4);
+  else if (t.type == kF16) {
+    const uint16_t* h = reinterpret_cast<const uint16_t*>(t.data);
+    for (size_t i = 0; i < v.size(); ++i) v[i] = half_bits_to_float(h[i]);
+  } else {
+    throw Error(kErrIo, t.name + ": expected F32 or F16");
+  }
+  return v;
+}
+
+// Row-concatenated FP32 tensors, each packed into the F32 layout.
+void upload_f32_rows(const GgufTensor& t, float* dst_row0) {
+  auto v = tensor_f32(t);
+  std::vector<float> packed(v.size());
+  pack_f32(v.data(), t.rows(), t.cols(), packed.data());
+  FA_CUDA(cudaMemcpy(dst_row0, packed.data(), packed.size() * 4, cudaMemcpyHostToDevice));
+}
+
+}  // namespace
+
+extern "C" {
+
+int fa_model_load_gguf(fa_backend* b, const char* path, int capacity, fa_model** out) {
+  return guarded([&] {
+    check_backend(b);
+    if (!path || !out) throw Error(kErrArgument, "null argument");
+    GgufFile f(path);
+    auto m = std::make_unique<fa_model>();
+    m->backend = b;
+    // QwenDecoder.cs:63-68,78 (defaults are the reference's).
+    m->width = f.integer("qwen3.embedding_length", 1024);
+    m->heads = f.integer("qwen3.attention.head_count", 16);
+    m->kv_heads = f.integer("qwen3.attention.head_count_kv", 8);
+    m->head_size = f.integer("qwen3.attention.key_length", 128);
+    m->layers = f.integer("qwen3.block_count", 28);
+    m->eps = f.real("qwen3.attention.layer_norm_rms_epsilon", 1e-6f);
+    m->rope_base = f.real("qwen3.rope.freq_base", 1000000.0f);
+    m->capacity = capacity > 0 ? capacity : 2048;
+    if (m->heads % m->kv_heads != 0) throw Error(kErrIo, "Invalid GQA head counts");
+    if (m->head_size != 128 || m->heads != 2 * m->kv_heads)
+      throw Error(kErrArgument, "the CUDA decoder supports head_size 128 with 2 query heads per KV head");
+    if (m->width % 256 != 0) throw Error(kErrArgument, "hidden width must be a multiple of 256");
+    const GgufTensor& emb = f.at("token_embd.weight");
+    const GgufTensor* outw = f.find("output.weight");
+    m->vocab = (outw ? outw : &emb)->rows();
+    m->ffn = f.at("blk.0.ffn_gate.weight").rows();
+    m->quantized = f.at("blk.0.attn_q.weight").type == kQ8_0;
+    const int W = m->width, D = m->head_size, qw = m->heads * D, kvw = m->kv_heads * D, ffn = m->ffn;
+    if (ffn % 32 != 0) throw Error(kErrArgument, "FFN width must be a multiple of 32");
+    DeviceGuard g(b->device);
+
+    // ---- arena plan ----
+    Arena ar;
+    struct QSlot { size_t q, s; int rows, cols; };
+    auto qslot = [&](int rows, int cols) {
+      QSlot s{ar.take(q8_bytes_q(rows, cols)), ar.take(q8_bytes_s(rows, cols, true)), rows, cols};
+      return s;
+    };
+    auto fslot = [&](int rows, int cols) { return ar.take((size_t)rows * cols * 4); };
+    struct LayerPlan { QSlot qkv, o, gu, down; size_t fqkv, fo, fgu, fdown, an, qn, kn, fn; };
+    std::vector<LayerPlan> plan(m->layers);
+    for (int l = 0; l < m->layers; ++l) {
+      auto& p = plan[l];
+      if (m->quantized) {
+        p.qkv = qslot(qw + 2 * kvw, W);
+        p.o = qslot(W, qw);
+        p.gu = qslot(2 * ffn, W);
+        p.down = qslot(W, ffn);
+      } else {
+        p.fqkv = fslot(qw + 2 * kvw, W);
+        p.fo = fslot(W, qw);
+        p.fgu = fslot(2 * ffn, W);
+        p.fdown = fslot(W, ffn);
+      }
+      p.an = ar.take(W * 4);
+      p.qn = ar.take(D * 4);
+      p.kn = ar.take(D * 4);
+      p.fn = ar.take(W * 4);
+    }
+    const bool emb_q8 = emb.type == kQ8_0;
+    QSlot qemb{}, qlm{};
+    size_t femb = 0, flm = 0;
+    if (emb_q8) qemb = qslot(emb.rows(), emb.cols());
+    else femb = fslot(emb.rows(), emb.cols());
+    if (outw) {
+      if (outw->type == kQ8_0) qlm = qslot(outw->rows(), outw->cols());
+      else flm = fslot(outw->rows(), outw->cols());
+    }
+    size_t onorm = ar.take(W * 4);
+    size_t rcos = ar.take((size_t)m->capacity * (D / 2) * 4), rsin = ar.take((size_t)m->capacity * (D / 2) * 4);
+    if (ffn % 32 != 0 || (ffn / 32) % 1 != 0) throw Error(kErrArgument, "bad FFN width");
+    if (m->quantized && (m->ffn % kTileRows != 0)) throw Error(kErrArgument, "FFN width must be a multiple of 32");
+    m->arena.ensure(ar.used);
+    uint8_t* base = m->arena.as<uint8_t>();
+
+    auto norm_up = [&](const std::string& name, size_t off, int n) {
+      auto v = tensor_f32(f.at(name));
+      if ((int)v.size() != n) throw Error(kErrIo, name + ": unexpected size");
+      FA_CUDA(cudaMemcpy(base + off, v.data(), (size_t)n * 4, cudaMemcpyHostToDevice));
+      return reinterpret_cast<const float*>(base + off);
+    };
+    m->L.resize(m->layers);
+    for (int l = 0; l < m->layers; ++l) {
+      const std::string p = "blk." + std::to_string(l) + ".";
+      auto& P = plan[l];
+      auto& Ld = m->L[l];
+      const GgufTensor &tq = f.at(p + "attn_q.weight"), &tk = f.at(p + "attn_k.weight"), &tv = f.at(p + "attn_v.weight"),
+                       &to = f.at(p + "attn_output.weight"), &tg = f.at(p + "ffn_gate.weight"),
+                       &tu = f.at(p + "ffn_up.weight"), &td = f.at(p + "ffn_down.weight");
+      if (tq.rows() != qw || tk.rows() != kvw || tv.rows() != kvw || tq.cols() != W || to.cols() != qw ||
+          to.rows() != W || tg.rows() != ffn || tu.rows() != ffn || td.cols() != ffn || td.rows() != W)
+        throw Error(kErrIo, "layer " + std::to_string(l) + ": unexpected projection shapes");
+      if (m->quantized) {
+        uint8_t *q0 = base + P.qkv.q, *s0 = base + P.qkv.s;
+        upload_q8_tensor(tq, q0, s0, 0, 1);
+        upload_q8_tensor(tk, q0, s0, qw / kTileRows, 1);
+        upload_q8_tensor(tv, q0, s0, (qw + kvw) / kTileRows, 1);
+        Ld.qkv = make_view(q0, s0, qw + 2 * kvw, W, true);
+        upload_q8_tensor(to, base + P.o.q, base + P.o.s, 0, 1);
+        Ld.o = make_view(base + P.o.q, base + P.o.s, W, qw, true);
+        upload_q8_tensor(tg, base + P.gu.q, base + P.gu.s, 0, 2);  // gate tile i -> 2i
+        upload_q8_tensor(tu, base + P.gu.q, base + P.gu.s, 1, 2);  // up tile i -> 2i + 1
+        Ld.gateup = make_view(base + P.gu.q, base + P.gu.s, 2 * ffn, W, true);
+        Ld.gateup.rows = ffn;  // epilogue rows per half of the pair
+        upload_q8_tensor(td, base + P.down.q, base + P.down.s, 0, 1);
+        Ld.down = make_view(base + P.down.q, base + P.down.s, W, ffn, true);
+      } else {
+        float* qkv0 = reinterpret_cast<float*>(base + P.fqkv);
+        upload_f32_rows(tq, qkv0);
+        upload_f32_rows(tk, qkv0 + (size_t)qw * W);
+        upload_f32_rows(tv, qkv0 + (size_t)(qw + kvw) * W);
+        Ld.fqkv = F32View{qkv0, qw + 2 * kvw, W};
+        upload_f32_rows(to, reinterpret_cast<float*>(base + P.fo));
+        Ld.fo = F32View{reinterpret_cast<float*>(base + P.fo), W, qw};
+        float* gu0 = reinterpret_cast<float*>(base + P.fgu);
+        upload_f32_rows(tg, gu0);
+        upload_f32_rows(tu, gu0 + (size_t)ffn * W);
+        Ld.fgateup = F32View{gu0, 2 * ffn, W};
+        upload_f32_rows(td, reinterpret_cast<float*>(base + P.fdown));
+        Ld.fdown = F32View{reinterpret_cast<float*>(base + P.fdown), W, ffn};
+      }
+      Ld.attn_norm = norm_up(p + "attn_norm.weight", P.an, W);
+      Ld.q_norm = norm_up(p + "attn_q_norm.weight", P.qn, D);
+      Ld.k_norm = norm_up(p + "attn_k_norm.weight", P.kn, D);
+      Ld.ffn_norm = norm_up(p + "ffn_norm.weight", P.fn, W);
+    }
+    if (emb.cols() != W) throw Error(kErrIo, "token_embd.weight: unexpected width");
+    if (emb_q8) {
+      upload_q8_tensor(emb, base + qemb.q, base + qemb.s, 0, 1);
+      m->embed = make_view(base + qemb.q, base + qemb.s, emb.rows(), W, true);
+    } else {
+      upload_f32_rows(emb, reinterpret_cast<float*>(base + femb));
+      m->fembed = F32View{reinterpret_cast<float*>(base + femb), emb.rows(), W};
+    }
+    if (outw) {
+      if (outw->type == kQ8_0) {
+        upload_q8_tensor(*outw, base + qlm.q, base + qlm.s, 0, 1);
+        m->lm = make_view(base + qlm.q, base + qlm.s, outw->rows(), W, true);
+      } else {
+        upload_f32_rows(*outw, reinterpret_cast<float*>(base + flm));
+        m->flm = F32View{reinterpret_cast<float*>(base + flm), outw->rows(), W};
+      }
+    } else {
+      m->lm = m->embed;
+      m->flm = m->fembed;
+    }
+    if (m->quantized != (m->lm.q != nullptr))
+      throw Error(kErrArgument, "mixed Q8/FP32 projection and lm_head types are not supported");
+    m->out_norm = norm_up("output_norm.weight", onorm, W);
+    // RoPE table exactly as QwenDecoder.cs:78-95 builds it (float pow/cos/sin).
+    {
+      const int half = D / 2;
+      std::vector<float> freq(half), c((size_t)m->capacity * half), s((size_t)m->capacity * half);
+      for (int i = 0; i < half; ++i) freq[i] = std::pow(m->rope_base, (-2.0f * (float)i) / (float)D);
+      for (int t = 0; t < m->capacity; ++t)
+        for (int i = 0; i < half; ++i) {
+          float angle = (float)t * freq[i];
+          c[(size_t)t * half + i] = std::cos(angle);
+          s[(size_t)t * half + i] = std::sin(angle);
+        }
+      FA_CUDA(cudaMemcpy(base + rcos, c.data(), c.size() * 4, cudaMemcpyHostToDevice));
+      FA_CUDA(cudaMemcpy(base + rsin, s.data(), s.size() * 4, cudaMemcpyHostToDevice));
+      m->rope_cos = reinterpret_cast<const float*>(base + rcos);
+      m->rope_sin = reinterpret_cast<const float*>(base + rsin);
+    }
+    // Algorithmic weight bytes per decode step: every projection and the
+    // lm_head once (34 B per 32 Q8 values, 4 B per FP32 value) + norm vectors.
+    int64_t per_layer_vals = (int64_t)(qw + 2 * kvw) * W + (int64_t)W * qw + (int64_t)2 * ffn * W + (int64_t)W * ffn;
+    int64_t lm_vals = (int64_t)m->vocab * W;
+    int64_t vals = per_layer_vals * m->layers + lm_vals;
+    m->weight_bytes = (m->quantized ? vals / 32 * 34 : vals * 4) + (int64_t)(m->layers * (2 * W + 2 * D) + W) * 4;
+    {
+      std::lock_guard<std::mutex> lk(b->mu);
+      b->models++;
+    }
+    *out = m.release();
+    return (int)kHandled;
+  });
+}
+
+int fa_model_free(fa_model* m) {
+  return guarded([&] {
+    if (!m) throw Error(kErrArgument, "null model");
+    if (m->sessions > 0) throw Error(kErrArgument, "free the model's sessions first");
+    fa_backend* b = m->backend;
+    {
+      DeviceGuard g(b->device);
+      FA_CUDA(cudaDeviceSynchronize());
+      m->arena.release();
+    }
+    {
+      std::lock_guard<std::mutex> lk(b->mu);
+      b->models--;
+    }
+    delete m;
+    return (int)kHandled;
+  });
+}
+
+int fa_model_dims(const fa_model* m, int32_t* dims) {
+  return guarded([&] {
+    if (!m || !dims) throw Error(kErrArgument, "null argument");
+    dims[0] = m->width;
+    dims[1] = m->heads;
+    dims[2] = m->kv_heads;
+    dims[3] = m->head_size;
+    dims[4] = m->layers;
+    dims[5] = m->vocab;
+    dims[6] = m->ffn;
+    dims[7] = m->capacity;
+    return (int)kHandled;
+  });
+}
+
+int64_t fa_model_weight_bytes(const fa_model* m) { return m ? m->weight_bytes : -1; }
+
+}  // extern "C"
+
+// ============================================================== session ====
+
+namespace {
+
+AttnArgs attn_args(fa_session* s, int layer, int frames, const int* skip) {
+  fa_model* m = s->m;
+  const int kvw = m->kv_heads * m->head_size;
+  AttnArgs a;
+  a.qkv = s->qkv.as<float>();
+  a.frames = frames;
+  a.heads = m->heads;
+  a.kv_heads = m->kv_heads;
+  a.head_size = m->head_size;
+  a.q_norm = m->L[layer].q_norm;
+  a.k_norm = m->L[layer].k_norm;
+  a.eps = m->eps;
+  a.rope_cos = m->rope_cos;
+  a.rope_sin = m->rope_sin;
+  a.k_cache = s->k_cache.as<__half>() + (size_t)layer * m->capacity * kvw;
+  a.v_cache = s->v_cache.as<__half>() + (size_t)layer * m->capacity * kvw;
+  a.pos = s->d_int(0);
+  a.splits = kAttnSplits;
+  a.part = s->part.as<float>();
+  a.attn = s->attn.as<float>();
+  a.skip = skip;
+  return a;
+}
+
+// QwenDecoder.Decode's layer loop (QwenDecoder.cs:180-252) for `frames`
+// frames already in s->x; KV positions come from the device word pos.
+void enqueue_layers(fa_session* s, int frames, const int* skip) {
+  fa_model* m = s->m;
+  const int W = m->width, qw = m->heads * m->head_size, kvw = m->kv_heads * m->head_size;
+  cudaStream_t st = s->stream;
+  for (int l = 0; l < m->layers; ++l) {
+    const LayerDev& L = m->L[l];
+    if (m->quantized) {
+      GemvArgs g;
+      g.x = s->x.as<float>();
+      g.frames = frames;
+      g.gamma = L.attn_norm;
+      g.eps = m->eps;
+      g.w = L.qkv;
+      g.epilogue = kEpiStore;
+      g.out = s->qkv.as<float>();
+      g.out_stride = qw + 2 * kvw;
+      g.skip = skip;
+      launch_gemv(g, st);
+    } else {
+      F32GemvArgs g;
+      g.x = s->x.as<float>();
+      g.frames = frames;
+      g.gamma = L.attn_norm;
+      g.eps = m->eps;
+      g.w = L.fqkv;
+      g.out = s->qkv.as<float>();
+      g.out_stride = qw + 2 * kvw;
+      g.skip = skip;
+      launch_gemv_f32(g, st);
+    }
+    AttnArgs a = attn_args(s, l, frames, skip);
+    launch_qk_rope_kv(a, st);
+    launch_attention(a, st);
+    if (m->quantized) {
+      GemvArgs g;
+      g.x = s->attn.as<float>();
+      g.frames = frames;
+      g.w = L.o;
+      g.epilogue = kEpiResidual;
+      g.out = s->a.as<float>();
+      g.res = s->x.as<float>();
+      g.out_stride = W;
+      g.skip = skip;
+      launch_gemv(g, st);
+      GemvArgs u;
+      u.x = s->a.as<float>();
+      u.frames = frames;
+      u.gamma = L.ffn_norm;
+      u.eps = m->eps;
+      u.w = L.gateup;
+      u.epilogue = kEpiSiluPair;
+      u.out = s->act.as<float>();
+      u.out_stride = m->ffn;
+      u.skip = skip;
+      launch_gemv(u, st);
+      GemvArgs d;
+      d.x = s->act.as<float>();
+      d.frames = frames;
+      d.w = L.down;
+      d.epilogue = kEpiResidual;
+      d.out = s->x.as<float>();
+      d.res = s->a.as<float>();
+      d.out_stride = W;
+      d.skip = skip;
+      launch_gemv(d, st);
+    } else {
+      F32GemvArgs g;
+      g.x = s->attn.as<float>();
+      g.frames = frames;
+      g.w = L.fo;
+      g.epilogue = kEpiResidual;
+      g.out = s->a.as<float>();
+      g.res = s->x.as<float>();
+      g.out_stride = W;
+      g.skip = skip;
+      launch_gemv_f32(g, st);
+      F32GemvArgs u;
+      u.x = s->a.as<float>();
+      u.frames = frames;
+      u.gamma = L.ffn_norm;
+      u.eps = m->eps;
+      u.w = L.fgateup;
+      u.out = s->gu.as<float>();
+      u.out_stride = 2 * m->ffn;
+      u.skip = skip;
+      launch_gemv_f32(u, st);
+      launch_silu_pair(s->gu.as<float>(), frames, m->ffn, s->act.as<float>(), skip, st);
+      F32GemvArgs d;
+      d.x = s->act.as<float>();
+      d.frames = frames;
+      d.w = L.fdown;
+      d.epilogue = kEpiResidual;
+      d.out = s->x.as<float>();
+      d.res = s->a.as<float>();
+      d.out_stride = W;
+      d.skip = skip;
+      launch_gemv_f32(d, st);
+    }
+  }
+}
+
+// Final norm + lm_head + Greedy on the last frame (QwenDecoder.cs:262-268,278-326).
+void enqueue_head(fa_session* s, const float* x_last, const int* skip) {
+  fa_model* m = s->m;
+  if (m->quantized) {
+    GemvArgs g;
+    g.x = x_last;
+    g.frames = 1;
+    g.gamma = m->out_norm;
+    g.eps = m->eps;
+    g.w = m->lm;
+    g.epilogue = kEpiArgmax;
+    g.logits = s->logits.as<float>();
+    g.am.part_value = s->am_val.as<float>();
+    g.am.part_index = s->am_idx.as<int>();
+    g.am.counter = reinterpret_cast<unsigned*>(s->d_int(5));
+    g.am.row0_nan = s->d_int(4);
+    g.am.token = s->d_int(1);
+    g.skip = skip;
+    launch_gemv(g, s->stream);
+  } else {
+    F32GemvArgs g;
+    g.x = x_last;
+    g.frames = 1;
+    g.gamma = m->out_norm;
+    g.eps = m->eps;
+    g.w = m->flm;
+    g.out = s->logits.as<float>();
+    g.out_stride = m->vocab;
+    g.skip = skip;
+    launch_gemv_f32(g, s->stream);
+    launch_greedy_dev(s->logits.as<float>(), m->vocab, s->d_int(1), skip, s->stream);
+  }
+}
+
+void enqueue_embed(fa_session* s, const int* tokens, int frames, const int* skip) {
+  if (s->m->quantized) launch_embed(s->m->embed, tokens, frames, s->x.as<float>(), skip, s->stream);
+  else launch_embed_f32(s->m->fembed, tokens, frames, s->x.as<float>(), skip, s->stream);
+}
+
+StepState step_state(fa_session* s) {
+  StepState st;
+  st.pos = s->d_int(0);
+  st.token = s->d_int(1);
+  st.step = s->d_int(2);
+  st.stopped = s->d_int(3);
+  st.log = s->log.as<int>();
+  st.log_cap = s->log_cap;
+  st.end_ids = s->end_ids.as<int>();
+  return st;
+}
+
+cudaGraphExec_t capture(fa_session* s, bool generate, int n_end) {
+  cudaGraph_t graph = nullptr;
+  FA_CUDA(cudaStreamBeginCapture(s->stream, cudaStreamCaptureModeThreadLocal));
+  try {
+    StepState st = step_state(s);
+    st.n_end = n_end;
+    const int* skip = nullptr;
+    if (generate) {
+      launch_step_begin(st, s->stream);
+      skip = st.stopped;
+    } else {
+      st.stopped = nullptr;
+    }
+    enqueue_embed(s, s->d_int(1), 1, skip);
+    enqueue_layers(s, 1, skip);
+    enqueue_head(s, s->x.as<float>(), skip);
+    launch_step_end(st, 1, s->stream);
+  } catch (...) {
+    cudaStreamEndCapture(s->stream, &graph);
+    if (graph) cudaGraphDestroy(graph);
+    throw;
+  }
+  FA_CUDA(cudaStreamEndCapture(s->stream, &graph));
+  if (generate) {
+    size_t n = 0;
+    cudaGraphGetNodes(graph, nullptr, &n);
+    std::vector<cudaGraphNode_t> nodes(n);
+    cudaGraphGetNodes(graph, nodes.data(), &n);
+    int kernels = 0;
+    for (auto node : nodes) {
+      cudaGraphNodeType t;
+      if (cudaGraphNodeGetType(node, &t) == cudaSuccess && t == cudaGraphNodeTypeKernel) ++kernels;
+    }
+    s->gen_kernels = kernels;
+  }
+  cudaGraphExec_t exec = nullptr;
+  cudaError_t e = cudaGraphInstantiate(&exec, graph, 0);
+  cudaGraphDestroy(graph);
+  FA_CUDA(e);
+  return exec;
+}
+
+template <typename F>
+int with_session(fa_session* s, F&& body) {
+  return guarded([&] {
+    if (!s) throw Error(kErrArgument, "null session");
+    std::lock_guard<std::mutex> lk(s->mu);
+    DeviceGuard g(s->device);
+    return body();
+  });
+}
+
+void check_tokens(const fa_session* s, const int32_t* tokens, int n) {
+  for (int i = 0; i < n; ++i)
+    if (tokens[i] < 0 || tokens[i] >= (s->m->quantized ? s->m->embed.rows : s->m->fembed.rows))
+      throw Error(kErrArgument, "token id out of range");
+}
+
+}  // namespace
+
+extern "C" {
+
+int fa_session_create(fa_model* m, fa_session** out) {
+  return guarded([&] {
+    if (!m || !out) throw Error(kErrArgument, "null argument");
+    auto s = std::make_unique<fa_session>();
+    s->m = m;
+    s->device = m->backend->device;
+    DeviceGuard g(s->device);
+    const int W = m->width, D = m->head_size, qw = m->heads * D, kvw = m->kv_heads * D, F = kMaxChunkFrames;
+    const size_t kv = (size_t)m->layers * m->capacity * kvw * 2;
+    s->k_cache.ensure(kv);
+    s->v_cache.ensure(kv);
+    FA_CUDA(cudaMemset(s->k_cache.p, 0, kv));
+    FA_CUDA(cudaMemset(s->v_cache.p, 0, kv));
+    s->x.ensure((size_t)F * W * 4);
+    s->a.ensure((size_t)F * W * 4);
+    s->qkv.ensure((size_t)F * (qw + 2 * kvw) * 4);
+    s->attn.ensure((size_t)F * qw * 4);
+    s->act.ensure((size_t)F * m->ffn * 4);
+    if (!m->quantized) s->gu.ensure((size_t)F * 2 * m->ffn * 4);
+    s->part.ensure((size_t)F * m->kv_heads * kAttnSplits * (4 + 2 * D) * 4);
+    s->logits.ensure((size_t)m->vocab * 4);
+    const int lm_ctas = (m->vocab + kTileRows - 1) / kTileRows;
+    s->am_val.ensure((size_t)lm_ctas * 4);
+    s->am_idx.ensure((size_t)lm_ctas * 4);
+    s->ints.ensure(64 * 4);
+    FA_CUDA(cudaMemset(s->ints.p, 0, 64 * 4));
+    s->end_ids.ensure(64 * 4);
+    s->log_cap = m->capacity;
+    s->log.ensure((size_t)s->log_cap * 4);
+    FA_CUDA(cudaStreamCreateWithFlags(&s->stream, cudaStreamNonBlocking));
+    prepare_kernels();
+    FA_CUDA(cudaEventCreate(&s->ev0));
+    FA_CUDA(cudaEventCreate(&s->ev1));
+    FA_CUDA(cudaMallocHost(&s->pinned, 64 * 4));
+    m->sessions++;
+    *out = s.release();
+    return (int)kHandled;
+  });
+}
+
+int fa_session_free(fa_session* s) {
+  return guarded([&] {
+    if (!s) throw Error(kErrArgument, "null session");
+    {
+      DeviceGuard g(s->device);
+      cudaStreamSynchronize(s->stream);
+      if (s->step_graph) cudaGraphExecDestroy(s->step_graph);
+      if (s->gen_graph) cudaGraphExecDestroy(s->gen_graph);
+      cudaEventDestroy(s->ev0);
+      cudaEventDestroy(s->ev1);
+      cudaFreeHost(s->pinned);
+      cudaStreamDestroy(s->stream);
+    }
+    s->m->sessions--;
+    delete s;
+    return (int)kHandled;
+  });
+}
+
+int fa_session_reset(fa_session* s) {
+  return with_session(s, [&] {
+    FA_CUDA(cudaMemsetAsync(s->d_int(0), 0, 4, s->stream));
+    FA_CUDA(cudaStreamSynchronize(s->stream));
+    s->pos = 0;
+    s->have_token = false;
+    return (int)kHandled;
+  });
+}
+
+int fa_session_position(const fa_session* s) { return s ? s->pos : -1; }
+
+int fa_session_embed(fa_session* s, const int32_t* tokens, int n, float* out) {
+  return with_session(s, [&] {
+    if (n < 0 || (n > 0 && (!tokens || !out))) throw Error(kErrArgument, "invalid arguments");
+    check_tokens(s, tokens, n);
+    const int W = s->m->width;
+    for (int done = 0; done < n;) {
+      const int c = std::min(kMaxChunkFrames, n - done);
+      FA_CUDA(cudaMemcpyAsync(s->d_int(16), tokens + done, (size_t)c * 4, cudaMemcpyHostToDevice, s->stream));
+      enqueue_embed(s, s->d_int(16), c, nullptr);
+      FA_CUDA(cudaMemcpyAsync(out + (size_t)done * W, s->x.p, (size_t)c * W * 4, cudaMemcpyDeviceToHost, s->stream));
+      FA_CUDA(cudaStreamSynchronize(s->stream));
+      done += c;
+    }
+    return (int)kHandled;
+  });
+}
+
+static int session_decode_locked(fa_session* s, const float* emb, const int32_t* tokens, int frames, int output_logits,
+                                 float* logits, int32_t* argmax) {
+  fa_model* m = s->m;
+  const int W = m->width;
+  if (frames < 1 || s->pos + frames > m->capacity)
+    throw Error(kErrArgument, "Decoder context exhausted or invalid embeddings");
+  for (int done = 0; done < frames;) {
+    const int c = std::min(kMaxChunkFrames, frames - done);
+    if (emb) {
+      FA_CUDA(cudaMemcpyAsync(s->x.p, emb + (size_t)done * W, (size_t)c * W * 4, cudaMemcpyHostToDevice, s->stream));
+    } else {
+      FA_CUDA(cudaMemcpyAsync(s->d_int(16), tokens + done, (size_t)c * 4, cudaMemcpyHostToDevice, s->stream));
+      enqueue_embed(s, s->d_int(16), c, nullptr);
+    }
+    enqueue_layers(s, c, nullptr);
+    done += c;
+    if (done == frames && output_logits) enqueue_head(s, s->x.as<float>() + (size_t)(c - 1) * W, nullptr);
+    StepState st = step_state(s);
+    st.stopped = nullptr;
+    launch_step_end(st, c, s->stream);
+  }
+  if (output_logits) {
+    if (logits) FA_CUDA(cudaMemcpyAsync(logits, s->logits.p, (size_t)m->vocab * 4, cudaMemcpyDeviceToHost, s->stream));
+    FA_CUDA(cudaMemcpyAsync(s->pinned, s->d_int(1), 4, cudaMemcpyDeviceToHost, s->stream));
+  }
+  FA_CUDA(cudaStreamSynchronize(s->stream));
+  s->pos += frames;
+  if (output_logits) {
+    s->have_token = true;
+    if (argmax) *argmax = s->pinned[0];
+  }
+  return kHandled;
+}
+
+int fa_session_decode(fa_session* s, const float* embeddings, int frames, int output_logits, float* logits,
+                      int32_t* argmax) {
+  return with_session(s, [&] {
+    if (!embeddings) throw Error(kErrArgument, "null embeddings");
+    return session_decode_locked(s, embeddings, nullptr, frames, output_logits, logits, argmax);
+  });
+}
+
+int fa_session_step(fa_session* s, int32_t token, float* logits, int32_t* next) {
+  return with_session(s, [&] {
+    fa_model* m = s->m;
+    check_tokens(s, &token, 1);
+    if (s->pos + 1 > m->capacity) throw Error(kErrArgument, "Decoder context exhausted or invalid embeddings");
+    if (!s->step_graph) s->step_graph = capture(s, false, 0);
+    s->pinned[0] = token;
+    FA_CUDA(cudaMemcpyAsync(s->d_int(1), s->pinned, 4, cudaMemcpyHostToDevice, s->stream));
+    FA_CUDA(cudaGraphLaunch(s->step_graph, s->stream));
+    FA_CUDA(cudaMemcpyAsync(s->pinned + 1, s->d_int(1), 4, cudaMemcpyDeviceToHost, s->stream));
+    if (logits) FA_CUDA(cudaMemcpyAsync(logits, s->logits.p, (size_t)m->vocab * 4, cudaMemcpyDeviceToHost, s->stream));
+    FA_CUDA(cudaStreamSynchronize(s->stream));
+    s->pos += 1;
+    s->have_token = true;
+    if (next) *next = s->pinned[1];
+    return (int)kHandled;
+  });
+}
+
+int fa_session_generate(fa_session* s, int max_tokens, const int32_t* end_ids, int n_end, int32_t* tokens,
+                        int32_t* n_out) {
+  return with_session(s, [&] {
+    fa_model* m = s->m;
+    if (max_tokens < 0 || n_end < 0 || n_end > 64 || (n_end > 0 && !end_ids) || !n_out ||
+        (max_tokens > 0 && !tokens))
+      throw Error(kErrArgument, "invalid arguments");
+    if (!s->have_token) throw Error(kErrArgument, "generate needs the logits of a previous Decode");
+    *n_out = 0;
+    if (max_tokens == 0) return (int)kHandled;
+    const int steps = std::min(max_tokens, m->capacity - s->pos);
+    if (n_end > 0) FA_CUDA(cudaMemcpyAsync(s->end_ids.p, end_ids, (size_t)n_end * 4, cudaMemcpyHostToDevice, s->stream));
+    if (!s->gen_graph || s->n_end_graph != n_end) {
+      if (s->gen_graph) cudaGraphExecDestroy(s->gen_graph);
+      s->gen_graph = nullptr;
+      s->gen_graph = capture(s, true, n_end);
+      s->n_end_graph = n_end;
+    }
+    FA_CUDA(cudaMemsetAsync(s->d_int(2), 0, 8, s->stream));  // step, stopped
+    FA_CUDA(cudaEventRecord(s->ev0, s->stream));
+    for (int i = 0; i < steps; ++i) FA_CUDA(cudaGraphLaunch(s->gen_graph, s->stream));
+    FA_CUDA(cudaEventRecord(s->ev1, s->stream));
+    FA_CUDA(cudaMemcpyAsync(s->pinned, s->d_int(0), 16, cudaMemcpyDeviceToHost, s->stream));
+    FA_CUDA(cudaStreamSynchronize(s->stream));
+    FA_CUDA(cudaEventElapsedTime(&s->last_ms, s->ev0, s->ev1));
+    const int count = s->pinned[2], stopped = s->pinned[3], next = s->pinned[1];
+    if (count > 0) FA_CUDA(cudaMemcpy(tokens, s->log.p, (size_t)count * 4, cudaMemcpyDeviceToHost));
+    s->pos = s->pinned[0];
+    *n_out = count;
+    if (!stopped && max_tokens > steps) {
+      // The reference would add `next` and then fail in Decode (QwenDecoder.cs:163-166).
+      bool is_end = false;
+      for (int i = 0; i < n_end; ++i) is_end |= end_ids[i] == next;
+      if (!is_end) throw Error(kErrCapacity, "Decoder context exhausted or invalid embeddings");
+    }
+    return (int)kHandled;
+  });
+}
+
+int fa_session_last_generate_ms(const fa_session* s, float* ms) {
+  if (!s || !ms) return kErrArgument;
+  *ms = s->last_ms;
+  return kHandled;
+}
+
+int fa_session_cache_prefix(fa_session* s, const int32_t* tokens, int n) {
+  return with_session(s, [&] {
+    if (s->cached_prefix != 0) throw Error(kErrArgument, "Prefix is already cached");
+    if (n < 1 || !tokens) throw Error(kErrArgument, "empty prefix");
+    check_tokens(s, tokens, n);
+    FA_CUDA(cudaMemsetAsync(s->d_int(0), 0, 4, s->stream));
+    s->pos = 0;
+    session_decode_locked(s, nullptr, tokens, n, 0, nullptr, nullptr);
+    s->cached_prefix = n;
+    s->have_token = false;
+    return (int)kHandled;
+  });
+}
+
+int fa_session_restore_prefix(fa_session* s) {
+  return with_session(s, [&] {
+    s->pinned[0] = s->cached_prefix;
+    FA_CUDA(cudaMemcpyAsync(s->d_int(0), s->pinned, 4, cudaMemcpyHostToDevice, s->stream));
+    FA_CUDA(cudaStreamSynchronize(s->stream));
+    s->pos = s->cached_prefix;
+    s->have_token = false;
+    return (int)kHandled;
+  });
+}
+
+int fa_session_kernels_per_step(const fa_session* s) { return s ? s->gen_kernels : -1; }
+
+int fa_session_time_lm_head(fa_session* s, int iters, float* ms) {
+  return with_session(s, [&] {
+    if (iters < 1 || !ms) throw Error(kErrArgument, "invalid arguments");
+    for (int i = 0; i < 2; ++i) enqueue_head(s, s->x.as<float>(), nullptr);  // warm-up
+    FA_CUDA(cudaEventRecord(s->ev0, s->stream));
+    for (int i = 0; i < iters; ++i) enqueue_head(s, s->x.as<float>(), nullptr);
+    FA_CUDA(cudaEventRecord(s->ev1, s->stream));
+    FA_CUDA(cudaStreamSynchronize(s->stream));
+    float t = 0.0f;
+    FA_CUDA(cudaEventElapsedTime(&t, s->ev0, s->ev1));
+    *ms = t / iters;
+    return (int)kHandled;
+  });
+}
+
+int fa_session_kv(fa_session* s, int layer, float* keys, float* values) {
+  return with_session(s, [&] {
+    fa_model* m = s->m;
+    if (layer < 0 || layer >= m->layers || !keys || !values) throw Error(kErrArgument, "invalid layer");
+    const size_t kvw = (size_t)m->kv_heads * m->head_size, n = (size_t)s->pos * kvw;
+    std::vector<__half> hk(n), hv(n);
+    const size_t off = (size_t)layer * m->capacity * kvw;
+    FA_CUDA(cudaMemcpy(hk.data(), s->k_cache.as<__half>() + off, n * 2, cudaMemcpyDeviceToHost));
+    FA_CUDA(cudaMemcpy(hv.data(), s->v_cache.as<__half>() + off, n * 2, cudaMemcpyDeviceToHost));
+    for (size_t i = 0; i < n; ++i) {
+      keys[i] = __half2float(hk[i]);
+      values[i] = __half2float(hv[i]);
+    }
+    return (int)kHandled;
+  });
+}
+
+}  // extern "C"

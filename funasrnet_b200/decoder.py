@@ -1,0 +1,172 @@
+"""QwenDecoder and the FunAsr.Transcribe token loop on the CUDA library.
+
+Mirrors the reference's decoder surface (src/FunAsrNet/QwenDecoder.cs):
+``reset`` (:117), ``embed`` (:143-152), ``decode`` (:161-271), ``greedy``
+(:278-326), ``cache_prefix``/``restore_prefix`` (:122-137), and the greedy
+loop of ``FunAsr.Transcribe`` (src/FunAsrNet/FunAsr.cs:164-189) as
+``transcribe_tokens``.  Every op runs in libfunasr_cuda.so; errors surface as
+``FaError`` (ArgumentException for exhausted context or bad embeddings).
+"""
+from __future__ import annotations
+
+import ctypes as C
+import time
+from dataclasses import dataclass
+
+import numpy as np
+
+from ._lib import FA_OK, check, lib, ptr
+from .backend import CudaFloatBackend, Ops
+
+# ByteBpe.IsEnd (src/FunAsrNet/ByteBpe.cs:57-71) ends on <|endoftext|>, <|im_end|>,
+# <|fim_suffix|> when the vocabulary has them, plus tokenizer.ggml.eos_token_id.
+# The ids below are <|endoftext|> and <|im_end|> of the Qwen3 vocabulary (and of
+# the synthetic GGUF); callers with a real tokenizer pass its own set.
+QWEN_END_TOKENS = (151643, 151645)
+
+
+class CudaModel:
+    """A GGUF decoder model resident on one GPU (Gguf + QwenDecoder weights)."""
+
+    def __init__(self, backend: CudaFloatBackend, path: str, capacity: int = 2048):
+        self.backend = backend
+        h = C.c_void_p()
+        check(lib().fa_model_load_gguf(backend.handle, str(path).encode(), capacity, C.byref(h)))
+        self._h = h
+        dims = np.zeros(8, np.int32)
+        check(lib().fa_model_dims(h, ptr(dims)))
+        (self.width, self.heads, self.kv_heads, self.head_size, self.layers, self.vocab, self.ffn,
+         self.capacity) = (int(v) for v in dims)
+        self.weight_bytes = int(lib().fa_model_weight_bytes(h))
+
+    @property
+    def handle(self):
+        return self._h
+
+    def close(self) -> None:
+        if self._h is not None:
+            check(lib().fa_model_free(self._h))
+            self._h = None
+
+
+class QwenDecoder:
+    """One decoding context: its own F16 KV cache, position and CUDA stream."""
+
+    def __init__(self, model: CudaModel):
+        self.model = model
+        h = C.c_void_p()
+        check(lib().fa_session_create(model.handle, C.byref(h)))
+        self._h = h
+
+    @property
+    def width(self) -> int:
+        return self.model.width
+
+    @property
+    def position(self) -> int:
+        return int(lib().fa_session_position(self._h))
+
+    def reset(self) -> None:
+        check(lib().fa_session_reset(self._h))
+
+    def embed(self, tokens) -> np.ndarray:
+        t = np.ascontiguousarray(tokens, dtype=np.int32).reshape(-1)
+        out = np.empty(t.size * self.width, np.float32)
+        check(lib().fa_session_embed(self._h, ptr(t), t.size, ptr(out)))
+        return out
+
+    def decode(self, embeddings, frames: int, output_logits: bool = True, want_logits: bool = True):
+        """Decode(embeddings, frames, outputLogits): returns (logits or None, argmax or None)."""
+        e = np.ascontiguousarray(embeddings, dtype=np.float32).reshape(-1)
+        if frames < 1 or e.size != frames * self.width:
+            raise ValueError("Decoder context exhausted or invalid embeddings")
+        logits = np.empty(self.model.vocab, np.float32) if (output_logits and want_logits) else None
+        arg = C.c_int32(-1)
+        check(lib().fa_session_decode(self._h, ptr(e), frames, 1 if output_logits else 0, ptr(logits),
+                                      C.byref(arg)))
+        return logits, (arg.value if output_logits else None)
+
+    def step(self, token: int, want_logits: bool = False):
+        """Decode(Embed([token]), 1) + Greedy: returns (next_token, logits or None)."""
+        logits = np.empty(self.model.vocab, np.float32) if want_logits else None
+        nxt = C.c_int32()
+        check(lib().fa_session_step(self._h, int(token), ptr(logits), C.byref(nxt)))
+        return nxt.value, logits
+
+    def generate(self, max_tokens: int, end_ids=QWEN_END_TOKENS) -> list[int]:
+        """The FunAsr.Transcribe greedy loop on the device, from the last argmax."""
+        ends = np.ascontiguousarray(end_ids, dtype=np.int32)
+        toks = np.empty(max(1, max_tokens), np.int32)
+        n = C.c_int32()
+        check(lib().fa_session_generate(self._h, int(max_tokens), ptr(ends) if ends.size else None, ends.size,
+                                        ptr(toks), C.byref(n)))
+        return toks[: n.value].tolist()
+
+    def last_generate_ms(self) -> float:
+        ms = C.c_float()
+        check(lib().fa_session_last_generate_ms(self._h, C.byref(ms)))
+        return float(ms.value)
+
+    def kernels_per_step(self) -> int:
+        return int(lib().fa_session_kernels_per_step(self._h))
+
+    def time_lm_head(self, iters: int = 20) -> float:
+        ms = C.c_float()
+        check(lib().fa_session_time_lm_head(self._h, iters, C.byref(ms)))
+        return float(ms.value)
+
+    def cache_prefix(self, tokens) -> None:
+        t = np.ascontiguousarray(tokens, dtype=np.int32).reshape(-1)
+        check(lib().fa_session_cache_prefix(self._h, ptr(t), t.size))
+
+    def restore_prefix(self) -> None:
+        check(lib().fa_session_restore_prefix(self._h))
+
+    def kv(self, layer: int):
+        n = self.position * self.model.kv_heads * self.model.head_size
+        k = np.empty(n, np.float32)
+        v = np.empty(n, np.float32)
+        check(lib().fa_session_kv(self._h, layer, ptr(k), ptr(v)))
+        return k, v
+
+    @staticmethod
+    def greedy(backend: CudaFloatBackend, logits) -> int:
+        return Ops(backend).greedy(logits)
+
+    def close(self) -> None:
+        if self._h is not None:
+            check(lib().fa_session_free(self._h))
+            self._h = None
+
+
+@dataclass
+class DecodeResult:
+    tokens: list
+    prefill_seconds: float
+    generation_seconds: float
+
+
+def transcribe_tokens(decoder: QwenDecoder, embeddings: np.ndarray, frames: int, max_tokens: int = 128,
+                      end_ids=QWEN_END_TOKENS, on_device: bool = True) -> DecodeResult:
+    """The decoder half of FunAsr.Transcribe (FunAsr.cs:156-189) with prompt cache off.
+
+    on_device=True runs the whole greedy loop as replayed CUDA graphs with one
+    synchronisation at the end; on_device=False drives it token by token from
+    the host, as the reference's loop does.
+    """
+    t0 = time.perf_counter()
+    decoder.reset()
+    _, token = decoder.decode(embeddings, frames, output_logits=True, want_logits=False)
+    t1 = time.perf_counter()
+    if on_device:
+        tokens = decoder.generate(max_tokens, end_ids)
+    else:
+        ends = set(int(e) for e in end_ids)
+        tokens = []
+        for _ in range(max_tokens):
+            if token in ends:
+                break
+            tokens.append(token)
+            token, _ = decoder.step(token)
+    t2 = time.perf_counter()
+    return DecodeResult(tokens, t1 - t0, t2 - t1)

@@ -1,0 +1,179 @@
+/*
+ * funasr_cuda.h -- C ABI of libfunasr_cuda.so, the B200 (sm_100a) backend for
+ * FunAsrNet's Qwen3 decoder token loop.
+ *
+ * Reference paths below are relative to the FunAsrNet repository root.
+ *
+ * Conventions
+ *  - Every entry point returns an int status unless noted:
+ *        FA_OK (0)        handled; outputs fully written
+ *        FA_DECLINED (1)  unsupported here; outputs untouched, the caller's CPU
+ *                         path continues (the "return false" of the reference's
+ *                         Try* interfaces, IFloatComputeBackend.cs:18)
+ *        < 0              error; fa_last_error() (per thread) describes it
+ *  - All pointers are host pointers; calls are synchronous and blocking.
+ *  - A backend serialises its own per-op calls; a session serialises its own
+ *    calls.  Different sessions may be driven from different threads.
+ *  - Weight "Rows"/"Columns" follow the reference's Weight (Gguf.cs:303-307):
+ *    cols = K = Shape[0] (inner), rows = N = Shape[1] (outputs).
+ */
+#ifndef FUNASR_CUDA_H
+#define FUNASR_CUDA_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define FA_OK 0
+#define FA_DECLINED 1
+#define FA_ERR_ARGUMENT (-1)  /* ArgumentException in the reference */
+#define FA_ERR_CAPACITY (-2)  /* NotSupportedException / decoder context exhausted */
+#define FA_ERR_DISPOSED (-3)  /* ObjectDisposedException */
+#define FA_ERR_CUDA (-4)
+#define FA_ERR_IO (-5)        /* InvalidDataException / file errors */
+#define FA_ERR_TIMEOUT (-6)
+
+typedef struct fa_backend fa_backend;
+typedef struct fa_weight fa_weight;
+typedef struct fa_model fa_model;
+typedef struct fa_session fa_session;
+
+/* Message of the last failed call on this thread. */
+const char* fa_last_error(void);
+/* Library version string. */
+const char* fa_version(void);
+
+/* ---------------------------------------------------------------------------
+ * Backend: replaces VulkanFloatBackend in the FunAsr.FloatBackend slot
+ * (src/FunAsrNet/FunAsr.cs:67-71, src/FunAsrNet/TensorMath.cs:30-33).
+ * ------------------------------------------------------------------------ */
+
+/* new VulkanFloatBackend(...) (src/FunAsrNet.Vulkan/VulkanFloatBackend.cs:7). */
+int fa_backend_create(int device, fa_backend** out);
+/* IDisposable.Dispose: waits for idle, frees device memory
+ * (VulkanFloatBackend.cs:435-472).  Later calls on the handle are invalid. */
+int fa_backend_destroy(fa_backend* backend);
+/* IFloatComputeBackend.Name (src/FunAsrNet/IFloatComputeBackend.cs:7-10). */
+const char* fa_backend_name(const fa_backend* backend);
+
+/* Makes a read-only weight resident (the Vulkan backend's residency cache keyed
+ * by array identity, VulkanFloatBackend.cs:14,242-283).  q8: row-major int8
+ * values [rows x cols] and float scales [rows x cols/32] as Gguf.cs:132-173
+ * unpacks them.  Scales exactly representable in binary16 are kept as f16. */
+int fa_weight_upload_q8(fa_backend* backend, const int8_t* q, const float* scales, int rows, int cols,
+                        fa_weight** out);
+/* FP32 weights (Weight.Values), row-major [rows x cols]. */
+int fa_weight_upload_f32(fa_backend* backend, const float* values, int rows, int cols, fa_weight** out);
+int fa_weight_release(fa_backend* backend, fa_weight* weight);
+
+/* IQuantizedComputeBackend.TryQuantizedLinear
+ * (src/FunAsrNet/IQuantizedComputeBackend.cs:13; VulkanQuantizedBackend.cs:40-133):
+ * quantises input per 32-block exactly as TensorMath.Quantize and computes
+ * output[t*rows+r] = bias[r] + sum_b ((float)dot_b * ws) * xs in block order.
+ * input [frames x cols], bias [rows] or NULL, output [frames x rows]. */
+int fa_try_quantized_linear(fa_backend* backend, const float* input, int frames, const fa_weight* weight,
+                            const float* bias, float* output);
+/* IFloatComputeBackend.TryLinear (src/FunAsrNet/IFloatComputeBackend.cs:19) for
+ * FP32 weights.  Declines Q8 weights (the reference routes those to
+ * TryQuantizedLinear, TensorMath.cs:89-94). */
+int fa_try_linear(fa_backend* backend, const float* input, int frames, const fa_weight* weight,
+                  const float* bias, float* output);
+/* IGroupedComputeBackend.TryLinearMany (src/FunAsrNet/IGroupedComputeBackend.cs:12;
+ * VulkanGroupedBackend.cs:17-67): several Q8 projections of one input sharing
+ * one activation quantisation.  outputs[i] holds frames x rows(weights[i]). */
+int fa_try_linear_many(fa_backend* backend, const float* input, int frames, const fa_weight* const* weights,
+                       int count, float* const* outputs);
+
+/* ---------------------------------------------------------------------------
+ * Single-op entry points for the decoder ops that have no backend interface
+ * in the reference (they run on its CPU between backend calls,
+ * QwenDecoder.cs:183-245).  They run the same kernels the decode step uses.
+ * ------------------------------------------------------------------------ */
+
+/* TensorMath.Quantize (src/FunAsrNet/TensorMath.cs:378-412); n % 32 == 0. */
+int fa_op_quantize(fa_backend* backend, const float* x, int64_t n, int8_t* q, float* scales);
+/* TensorMath.Norm with rms=true over rows of `width` (TensorMath.cs:537-573,
+ * TensorMath.Elementwise.cs:26-100). */
+int fa_op_rmsnorm(fa_backend* backend, const float* x, int64_t n, int width, const float* gamma, float eps,
+                  float* y);
+/* TensorMath.RoundHalfCopy (src/FunAsrNet/TensorMath.Half.cs:18-55). */
+int fa_op_round_half(fa_backend* backend, const float* x, int64_t n, float* y);
+/* TensorMath.SiluMultiply (src/FunAsrNet/TensorMath.Elementwise.cs:167-196); gate overwritten. */
+int fa_op_silu_mul(fa_backend* backend, float* gate, const float* up, int64_t n);
+/* QwenDecoder.Greedy (src/FunAsrNet/QwenDecoder.cs:278-326). */
+int fa_op_greedy(fa_backend* backend, const float* logits, int64_t n, int32_t* token);
+/* TensorMath.TryDecoderAttentionPair (src/FunAsrNet/TensorMath.DecoderAttention.cs:17-52):
+ * query [2*kv_heads*size], keys/values [frames x kv_heads*size] holding
+ * binary16-representable values, output [2*kv_heads*size].  Declines
+ * (output untouched) unless size == 128. */
+int fa_op_attention_pair(fa_backend* backend, const float* query, const float* keys, const float* values,
+                         int frames, int kv_heads, int size, float* output);
+
+/* ---------------------------------------------------------------------------
+ * Model and decoder sessions: the whole-step surface (IDecoderStepBackend)
+ * a QwenDecoder hook calls instead of per-op round trips.
+ * ------------------------------------------------------------------------ */
+
+/* Gguf(path) + QwenDecoder(model, math, capacity) (src/FunAsrNet/Gguf.cs:43-185,
+ * src/FunAsrNet/QwenDecoder.cs:46-112): reads qwen3.* metadata and uploads
+ * Q8_0 blocks (f16 scales kept) into the device tile layout. */
+int fa_model_load_gguf(fa_backend* backend, const char* path, int capacity, fa_model** out);
+int fa_model_free(fa_model* model);
+/* dims[8]: width, heads, kv_heads, head_size, layers, vocab, ffn, capacity. */
+int fa_model_dims(const fa_model* model, int32_t* dims);
+/* Device bytes streamed per decode step for the weights (roofline numerator). */
+int64_t fa_model_weight_bytes(const fa_model* model);
+
+/* Seeded synthetic Qwen3 GGUF (N(0,stddev) weights, Q8_0 per 32-block, norm
+ * weights 1.0, tied embedding).  Full-size defaults when a dim is <= 0:
+ * width 1024, heads 16, kv_heads 8, head 128, layers 28, ffn 3072, vocab 151936. */
+int fa_synth_write_gguf(const char* path, uint64_t seed, int layers, int vocab, int width, int ffn,
+                        int quantized);
+/* out[i] = N(0,1) sample i+start of stream `stream` under `seed` (the same
+ * generator the synthetic weights use). */
+int fa_synth_normals(uint64_t seed, uint64_t stream, uint64_t start, int64_t n, float* out);
+
+/* One decoding context (QwenDecoder's KV state, QwenDecoder.cs:15,102-109). */
+int fa_session_create(fa_model* model, fa_session** out);
+int fa_session_free(fa_session* session);
+/* QwenDecoder.Reset (QwenDecoder.cs:117). */
+int fa_session_reset(fa_session* session);
+int fa_session_position(const fa_session* session);
+/* QwenDecoder.Embed (QwenDecoder.cs:143-152): out [n x width]. */
+int fa_session_embed(fa_session* session, const int32_t* tokens, int n, float* out);
+/* QwenDecoder.Decode(embeddings, frames, outputLogits) (QwenDecoder.cs:161-271).
+ * logits (vocab floats) may be NULL; argmax (Greedy of the logits) may be NULL.
+ * output_logits == 0 skips the lm_head as outputLogits=false does. */
+int fa_session_decode(fa_session* session, const float* embeddings, int frames, int output_logits,
+                      float* logits, int32_t* argmax);
+/* Decode(Embed([token]), 1) followed by Greedy: one step of the
+ * FunAsr.Transcribe loop (FunAsr.cs:167-178) through a replayed CUDA graph.
+ * logits may be NULL. */
+int fa_session_step(fa_session* session, int32_t token, float* logits, int32_t* next);
+/* The whole greedy loop of FunAsr.Transcribe (FunAsr.cs:167-178) on the device,
+ * starting from the argmax of the last Decode/step: emits up to max_tokens
+ * tokens, stopping before an end token (ByteBpe.IsEnd).  tokens gets n_out ids. */
+int fa_session_generate(fa_session* session, int max_tokens, const int32_t* end_ids, int n_end,
+                        int32_t* tokens, int32_t* n_out);
+/* CUDA-event time (ms) of the device work of the last fa_session_generate. */
+int fa_session_last_generate_ms(const fa_session* session, float* ms);
+/* CachePrefix / RestorePrefix (QwenDecoder.cs:122-137). */
+int fa_session_cache_prefix(fa_session* session, const int32_t* tokens, int n);
+int fa_session_restore_prefix(fa_session* session);
+/* Test hook: the F16-valued KV history of one layer as floats, [position x kv_width]. */
+int fa_session_kv(fa_session* session, int layer, float* keys, float* values);
+/* Number of kernel launches one generate iteration replays (kernel nodes of
+ * its CUDA graph); 0 before the first fa_session_generate. */
+int fa_session_kernels_per_step(const fa_session* session);
+/* Measurement hook: launches the lm_head GEMV (final norm + Q8 GEMV + argmax,
+ * one decode step's largest launch) `iters` times on the session stream and
+ * returns its mean CUDA-event duration in ms. */
+int fa_session_time_lm_head(fa_session* session, int iters, float* ms);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif

@@ -1,0 +1,222 @@
+"""End-to-end decoder parity with the CPU oracle through the C ABI.
+
+Tolerances are the north-star ones: logits within 2e-2 absolute and 1e-3
+relative to max|logit|, greedy tokens identical wherever the oracle's top-2
+margin exceeds 1e-2.  Sequences are compared teacher-forced (both sides are fed
+the oracle's token) so one near-tie cannot derail the comparison.
+"""
+import numpy as np
+import pytest
+
+from conftest import assert_bits_equal
+
+pytestmark = pytest.mark.gpu
+
+ABS_TOL = 2e-2
+REL_TOL = 1e-3
+MARGIN = 1e-2
+
+
+def check_logits(got, exp, what=""):
+    err = np.max(np.abs(got.astype(np.float64) - exp))
+    scale = np.max(np.abs(exp))
+    assert err <= ABS_TOL, f"{what}: max abs error {err}"
+    assert err <= REL_TOL * max(1.0, scale), f"{what}: relative error {err / scale}"
+    top2 = np.sort(exp)[-2:]
+    if top2[1] - top2[0] > MARGIN:
+        assert int(np.argmax(got)) == int(np.argmax(exp)), f"{what}: argmax differs with margin {top2[1] - top2[0]}"
+    return err
+
+
+def prefix_embeddings(om, audio, ids, seed):
+    """N audio vectors ~ N(0,1) followed by the embeddings of `ids` prompt tokens."""
+    rng = np.random.default_rng(seed)
+    a = rng.standard_normal(audio * om.width).astype(np.float32)
+    toks = rng.integers(0, om.vocab, ids)
+    return np.concatenate([a, om.embed(toks)]), audio + ids
+
+
+@pytest.fixture(scope="module")
+def small(backend, oracle, small_gguf):
+    from funasrnet_b200.decoder import CudaModel
+
+    cm = CudaModel(backend, small_gguf, capacity=512)
+    om = oracle.Model(small_gguf, 512)
+    yield cm, om
+    cm.close()
+    om.close()
+
+
+def test_model_dims(small):
+    cm, om = small
+    assert (cm.width, cm.heads, cm.kv_heads, cm.head_size, cm.layers, cm.vocab, cm.ffn) == \
+        (om.width, om.heads, om.kv_heads, om.head_size, om.layers, om.vocab, om.ffn)
+    assert cm.weight_bytes > 0
+
+
+def test_embed_exact(small):
+    from funasrnet_b200.decoder import QwenDecoder
+
+    cm, om = small
+    d = QwenDecoder(cm)
+    toks = [0, 1, 31, 32, 4095, 1234]
+    assert_bits_equal(d.embed(toks), om.embed(toks), "Embed")
+    d.close()
+
+
+def test_prefill_then_teacher_forced_steps(small, oracle):
+    from funasrnet_b200.decoder import QwenDecoder
+
+    cm, om = small
+    emb, frames = prefix_embeddings(om, 13, 8, seed=1)
+    d = QwenDecoder(cm)
+    os_ = oracle.Session(om)
+    lg, arg = d.decode(emb, frames)
+    exp = os_.decode(emb, frames)
+    check_logits(lg, exp, "prefill")
+    tok = oracle.greedy(exp)
+    for i in range(24):
+        nxt, lg = d.step(tok, want_logits=True)
+        exp = os_.decode(om.embed([tok]), 1)
+        check_logits(lg, exp, f"step {i}")
+        assert nxt == int(np.argmax(lg)) or np.isnan(lg[0])
+        tok = oracle.greedy(exp)
+    assert d.position == os_.position == frames + 24
+    d.close()
+    os_.close()
+
+
+def test_layer0_kv_exact_and_deeper_close(small, oracle):
+    from funasrnet_b200.decoder import QwenDecoder
+
+    cm, om = small
+    emb, frames = prefix_embeddings(om, 21, 8, seed=2)
+    d = QwenDecoder(cm)
+    os_ = oracle.Session(om)
+    d.decode(emb, frames, output_logits=False)
+    os_.decode(emb, frames, want_logits=False)
+    k, v = d.kv(0)
+    ek, ev = os_.kv(0)
+    # Layer 0 sees the embeddings directly: projection, QK-norm, RoPE and the
+    # binary16 rounding are all bit-exact.
+    assert_bits_equal(k, ek, "layer-0 keys")
+    assert_bits_equal(v, ev, "layer-0 values")
+    k1, v1 = d.kv(1)
+    ek1, ev1 = os_.kv(1)
+    assert np.max(np.abs(k1 - ek1)) <= 2e-2 and np.max(np.abs(v1 - ev1)) <= 2e-2
+    d.close()
+    os_.close()
+
+
+def test_multiframe_equals_single_frames(small):
+    from funasrnet_b200.decoder import QwenDecoder
+
+    cm, om = small
+    emb, frames = prefix_embeddings(om, 6, 3, seed=3)
+    a, b = QwenDecoder(cm), QwenDecoder(cm)
+    la, _ = a.decode(emb, frames)
+    for t in range(frames):
+        lb, _ = b.decode(emb[t * cm.width:(t + 1) * cm.width], 1)
+    assert_bits_equal(la, lb, "batched prefill vs frame-by-frame")
+    a.close()
+    b.close()
+
+
+def test_generate_matches_host_loop_and_oracle(small, oracle):
+    from funasrnet_b200.decoder import QwenDecoder, transcribe_tokens
+
+    cm, om = small
+    emb, frames = prefix_embeddings(om, 30, 8, seed=4)
+    a, b = QwenDecoder(cm), QwenDecoder(cm)
+    ra = transcribe_tokens(a, emb, frames, max_tokens=40, end_ids=(), on_device=True)
+    rb = transcribe_tokens(b, emb, frames, max_tokens=40, end_ids=(), on_device=False)
+    assert ra.tokens == rb.tokens and len(ra.tokens) == 40
+    assert a.position == frames + 40
+    # Oracle greedy sequence: identical until the first near-tie (margin <= 1e-2).
+    os_ = oracle.Session(om)
+    lg = os_.decode(emb, frames)
+    for i, t in enumerate(ra.tokens):
+        top2 = np.sort(lg)[-2:]
+        if top2[1] - top2[0] <= MARGIN:
+            break
+        assert t == oracle.greedy(lg), f"token {i}"
+        lg = os_.decode(om.embed([t]), 1)
+    a.close()
+    b.close()
+    os_.close()
+
+
+def test_generate_stops_before_end_token(small):
+    from funasrnet_b200.decoder import QwenDecoder
+
+    cm, om = small
+    emb, frames = prefix_embeddings(om, 10, 8, seed=5)
+    d = QwenDecoder(cm)
+    d.decode(emb, frames, want_logits=False)
+    full = d.generate(12, end_ids=())
+    d.reset()
+    d.decode(emb, frames, want_logits=False)
+    cut = d.generate(12, end_ids=(full[5],))
+    assert cut == full[:full.index(full[5])]
+    assert d.position == frames + len(cut)
+    d.close()
+
+
+def test_context_exhausted_raises(backend, small_gguf):
+    from funasrnet_b200._lib import FaError
+    from funasrnet_b200.decoder import CudaModel, QwenDecoder
+
+    cm = CudaModel(backend, small_gguf, capacity=16)
+    d = QwenDecoder(cm)
+    d.decode(np.zeros(10 * cm.width, np.float32), 10)
+    with pytest.raises(FaError):
+        d.decode(np.zeros(7 * cm.width, np.float32), 7)
+    assert d.position == 10
+    with pytest.raises(FaError):
+        d.generate(20, end_ids=())  # runs out of context before the 20th token
+    with pytest.raises(FaError):
+        d.step(cm.vocab, want_logits=False)  # token id out of range
+    d.close()
+    cm.close()
+
+
+def test_prefix_cache_restore(small):
+    from funasrnet_b200.decoder import QwenDecoder
+
+    cm, om = small
+    prompt = [11, 22, 33, 44, 55]
+    rest, n = prefix_embeddings(om, 4, 2, seed=6)
+    a = QwenDecoder(cm)
+    a.cache_prefix(prompt)
+    a.restore_prefix()
+    la, _ = a.decode(rest, n)
+    b = QwenDecoder(cm)
+    lb, _ = b.decode(np.concatenate([b.embed(prompt), rest]), len(prompt) + n)
+    assert_bits_equal(la, lb, "restored prefix")
+    a.restore_prefix()
+    assert a.position == len(prompt)
+    a.close()
+    b.close()
+
+
+def test_fp32_weights_model(backend, oracle, small_gguf_f32):
+    from funasrnet_b200.decoder import CudaModel, QwenDecoder
+
+    cm = CudaModel(backend, small_gguf_f32, capacity=256)
+    om = oracle.Model(small_gguf_f32, 256)
+    emb, frames = prefix_embeddings(om, 9, 8, seed=7)
+    d = QwenDecoder(cm)
+    os_ = oracle.Session(om)
+    lg, _ = d.decode(emb, frames)
+    exp = os_.decode(emb, frames)
+    check_logits(lg, exp, "fp32 prefill")
+    tok = oracle.greedy(exp)
+    for i in range(6):
+        _, lg = d.step(tok, want_logits=True)
+        exp = os_.decode(om.embed([tok]), 1)
+        check_logits(lg, exp, f"fp32 step {i}")
+        tok = oracle.greedy(exp)
+    d.close()
+    os_.close()
+    cm.close()
+    om.close()
