@@ -24,7 +24,9 @@ constexpr int kGemvThreads = 256;
 constexpr int kGemvWarps = kGemvThreads / 32;
 constexpr int kGemvFrames = 4;   // frames per CTA pass
 constexpr int kGemvUnroll = 4;   // (tile, block) units in flight per warp
-constexpr int kGemvMaxSmem = 227 * 1024;
+// Dynamic shared memory cap: the 227 KB per-block opt-in limit less 1 KB for
+// the kernels' static shared arrays.
+constexpr int kGemvMaxSmem = 226 * 1024;
 
 __device__ __forceinline__ bool skipped(const int* skip) { return skip != nullptr && *skip != 0; }
 
@@ -61,6 +63,35 @@ __device__ __forceinline__ float warp_sum_f(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, o));
   return v;
+}
+
+// exp as the reference's TensorMath.ExpAvx (TensorMath.ExpAvx.cs:83-116)
+// evaluates it per lane: clamp to [-104, 104] (NaN propagates), x = n*ln2 + r
+// with n = round-half-even(x * log2 e), degree-8 Taylor polynomial of exp(r)
+// in double with FMAs, scaled by 2^n and narrowed to float.  Every operation
+// is a correctly rounded IEEE double op, so the result is bit-identical to the
+// same evaluation on the host.
+__device__ __forceinline__ float exp_ref(float v) {
+  if (isnan(v)) return v;
+  const float c = v < -104.0f ? -104.0f : (v > 104.0f ? 104.0f : v);
+  const double x = (double)c;
+  const double n = rint(__dmul_rn(x, 1.4426950408889634074));
+  const double r = __fma_rn(n, -0.6931471805599453094, x);
+  const double square = __dmul_rn(r, r);
+  const double fourth = __dmul_rn(square, square);
+  const double p23 = __fma_rn(r, 1.0 / 6, 0.5);
+  const double p45 = __fma_rn(r, 1.0 / 120, 1.0 / 24);
+  const double p67 = __fma_rn(r, 1.0 / 5040, 1.0 / 720);
+  const double low = __fma_rn(square, p23, __dadd_rn(1.0, r));
+  const double high = __fma_rn(square, __fma_rn(square, 1.0 / 40320, p67), p45);
+  const double e = __fma_rn(fourth, high, low);
+  const double scale = __longlong_as_double((long long)(__double2int_rz(n) + 1023) << 52);
+  return __double2float_rn(__dmul_rn(e, scale));
+}
+
+// SiLU(g) * u as TensorMath.Elementwise.cs:180: g / (1 + exp(-g)) * u.
+__device__ __forceinline__ float silu_mul1(float g, float u) {
+  return __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, exp_ref(-g))), u);
 }
 
 // 1 / sqrt((float)(sumsq / width) + eps)  (TensorMath.Elementwise.cs:78)
@@ -213,7 +244,7 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_kernel(const GemvArgs a) {
       for (int b = 0; b < B; ++b) g = __fadd_rn(g, pg[b * 32]);
       for (int b = 0; b < B; ++b) u = __fadd_rn(u, pu[b * 32]);
       // TensorMath.Elementwise.cs:180: g / (1 + exp(-g)) * u
-      const float act = __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), u);
+      const float act = silu_mul1(g, u);
       if (row < a.out_stride) a.out[(size_t)(f0 + fi) * a.out_stride + row] = act;
     }
     return;
@@ -326,7 +357,7 @@ __global__ void round_half_kernel(const float* x, long long n, float* y) {
 __global__ void silu_mul_kernel(float* g, const float* u, long long n) {
   for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
     const float v = g[i];
-    g[i] = __fmul_rn(__fdiv_rn(v, __fadd_rn(1.0f, expf(-v))), u[i]);
+    g[i] = silu_mul1(v, u[i]);
   }
 }
 
@@ -394,6 +425,15 @@ __global__ void embed_kernel(const Q8View w, const int* tokens, float* x, const 
 }
 
 // --------------------------------------------------------- attention ----
+//
+// K cache layout: each head's row stores channel c = j + 8i (j < 8 lanes,
+// i < D/8) at position j*(D/8) + i, so the 8 accumulator lanes of the
+// reference's Vector256 dot product (AudioKernels.cs:101-112,
+// TensorMath.AttentionAvx.cs:87-111) each read one contiguous run.  V keeps
+// channel order (it is summed per channel).
+
+__host__ __device__ __forceinline__ int kpos(int c, int D) { return (c & 7) * (D >> 3) + (c >> 3); }
+__host__ __device__ __forceinline__ int kchan(int p, int D) { return p / (D >> 3) + 8 * (p % (D >> 3)); }
 
 // QK RMSNorm + RoPE + binary16 KV write.  grid (frames, heads + 2*kv_heads),
 // blockDim = head_size (<= 256, multiple of 32 and even).
@@ -428,7 +468,7 @@ __global__ void qk_rope_kv_kernel(const AttnArgs a) {
     const float o = c < half ? __fsub_rn(__fmul_rn(av, co), __fmul_rn(bv, si))
                              : __fadd_rn(__fmul_rn(av, si), __fmul_rn(bv, co));
     if (isq) xp[c] = o;
-    else a.k_cache[(size_t)p * kvw + (h - a.heads) * D + c] = __float2half_rn(o);  // QwenDecoder.cs:199
+    else a.k_cache[(size_t)p * kvw + (h - a.heads) * D + kpos(c, D)] = __float2half_rn(o);  // QwenDecoder.cs:199
   } else {
     const int vh = h - a.heads - a.kv_heads;
     a.v_cache[(size_t)p * kvw + vh * D + c] = __float2half_rn(base[qw + kvw + vh * D + c]);  // :200
@@ -449,11 +489,11 @@ __global__ void __launch_bounds__(128) attn_partial_kernel(const AttnArgs a) {
   const int chunk = (len + a.splits - 1) / a.splits;
   const int t0 = s * chunk, t1 = min(len, t0 + chunk);
   const float* q = a.qkv + (size_t)f * stride + (size_t)(2 * g) * D;
-  float q0[4], q1[4];
+  float q0[4], q1[4];  // q in the K cache's lane-permuted channel order
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
-    q0[j] = q[4 * lane + j];
-    q1[j] = q[D + 4 * lane + j];
+    q0[j] = q[kchan(4 * lane + j, D)];
+    q1[j] = q[D + kchan(4 * lane + j, D)];
   }
   const float divisor = __fsqrt_rn((float)D);
   float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.0f, l1 = 0.0f;
@@ -543,6 +583,131 @@ __global__ void __launch_bounds__(128) attn_combine_kernel(const AttnArgs a) {
   a.attn[(size_t)f * a.heads * D + (size_t)h * D + c] = __fdiv_rn(A, Lsum);
 }
 
+// ---- exact attention (the reference's arithmetic order) ----
+//
+// Scores: s_t = dot(q, K_t) / sqrt(D) with the dot accumulated in 8 lanes
+// (lane j: channels j, j+8, ... sequentially, acc + q*k with two roundings) and
+// folded as ((l0+l4)+(l1+l5)) + ((l2+l6)+(l3+l7))
+// (TensorMath.AttentionAvx.cs:87-159, AudioKernels.cs:101-112).
+// grid (frames, kv_heads, splits), 256 threads: 8 threads per position, 32
+// positions per pass; both query heads of the KV head share the K loads.
+__global__ void __launch_bounds__(256) attn_scores_kernel(const AttnArgs a) {
+  if (skipped(a.skip)) return;
+  constexpr int D = 128, M = D / 8;
+  __shared__ float qs[2][D];
+  const int f = blockIdx.x, g = blockIdx.y, s = blockIdx.z;
+  const int qw = a.heads * D, kvw = a.kv_heads * D;
+  const int stride = a.qkv_stride ? a.qkv_stride : qw + 2 * kvw;
+  const float* q = a.qkv + (size_t)f * stride + (size_t)(2 * g) * D;
+  qs[threadIdx.x >> 7][threadIdx.x & (D - 1)] = q[threadIdx.x];
+  __syncthreads();
+  const int j = threadIdx.x & 7, slot = threadIdx.x >> 3;
+  float q0[M], q1[M];
+#pragma unroll
+  for (int i = 0; i < M; ++i) {
+    q0[i] = qs[0][j + 8 * i];
+    q1[i] = qs[1][j + 8 * i];
+  }
+  const int len = *a.pos + f + 1;
+  const int chunk = (len + a.splits - 1) / a.splits;
+  const int t0 = s * chunk, t1 = min(len, t0 + chunk);
+  const float divisor = __fsqrt_rn((float)D);
+  float* out0 = a.scores + ((size_t)f * a.heads + 2 * g) * a.capacity;
+  float* out1 = out0 + a.capacity;
+  for (int base = t0; base < t1; base += 32) {
+    const int t = base + slot;
+    float acc0 = 0.0f, acc1 = 0.0f;
+    if (t < t1) {
+      const uint4* kr = reinterpret_cast<const uint4*>(a.k_cache + (size_t)t * kvw + g * D + j * M);
+      const uint4 ka = kr[0], kb = kr[1];
+      const __half* kh0 = reinterpret_cast<const __half*>(&ka);
+      const __half* kh1 = reinterpret_cast<const __half*>(&kb);
+#pragma unroll
+      for (int i = 0; i < M; ++i) {
+        const float k = __half2float(i < 8 ? kh0[i] : kh1[i - 8]);
+        acc0 = __fadd_rn(acc0, __fmul_rn(q0[i], k));
+        acc1 = __fadd_rn(acc1, __fmul_rn(q1[i], k));
+      }
+    }
+    // fold the 8 lanes of this position (lanes 8*slot .. 8*slot+7 of the warp)
+    acc0 = __fadd_rn(acc0, __shfl_down_sync(0xffffffffu, acc0, 4));
+    acc1 = __fadd_rn(acc1, __shfl_down_sync(0xffffffffu, acc1, 4));
+    acc0 = __fadd_rn(acc0, __shfl_down_sync(0xffffffffu, acc0, 1));
+    acc1 = __fadd_rn(acc1, __shfl_down_sync(0xffffffffu, acc1, 1));
+    acc0 = __fadd_rn(acc0, __shfl_down_sync(0xffffffffu, acc0, 2));
+    acc1 = __fadd_rn(acc1, __shfl_down_sync(0xffffffffu, acc1, 2));
+    if (j == 0 && t < t1) {
+      out0[t] = __fdiv_rn(acc0, divisor);
+      out1[t] = __fdiv_rn(acc1, divisor);
+    }
+  }
+}
+
+// Softmax + weighted V sum of one query head, in the reference's order
+// (TensorMath.SoftmaxAvx.cs:11-58, TensorMath.AttentionAvx.cs:173-224):
+// max; e_t = exp(s_t - max); sum in double over 8 lane accumulators
+// (lane j: e_{8i+j}), folded (s0+s2)+(s1+s3) with s_k = lane_k + lane_{k+4},
+// then the len % 8 tail sequentially; p_t = e_t * (float)(1/sum); each channel
+// accumulates acc + v_t * p_t over t = 0..len-1 in order.
+// grid (frames, heads), 128 threads (one per channel); dynamic smem
+// capacity floats.
+__global__ void __launch_bounds__(128) attn_softmax_v_kernel(const AttnArgs a) {
+  if (skipped(a.skip)) return;
+  constexpr int D = 128;
+  extern __shared__ __align__(16) float e[];
+  __shared__ float red_f[4];
+  __shared__ double lanes[8];
+  __shared__ float s_inv;
+  const int f = blockIdx.x, h = blockIdx.y, g = h >> 1, c = threadIdx.x;
+  const int kvw = a.kv_heads * D;
+  const int len = *a.pos + f + 1;
+  const float* sc = a.scores + ((size_t)f * a.heads + h) * a.capacity;
+  float mx = -INFINITY;
+  for (int t = c; t < len; t += D) {
+    const float v = sc[t];
+    e[t] = v;
+    mx = fmaxf(mx, v);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  if ((c & 31) == 0) red_f[c >> 5] = mx;
+  __syncthreads();
+  mx = fmaxf(fmaxf(red_f[0], red_f[1]), fmaxf(red_f[2], red_f[3]));
+  for (int t = c; t < len; t += D) e[t] = exp_ref(__fsub_rn(e[t], mx));
+  __syncthreads();
+  const int full = len & ~7;
+  if (c < 8) {
+    double acc = 0.0;
+    for (int t = c; t < full; t += 8) acc = __dadd_rn(acc, (double)e[t]);
+    lanes[c] = acc;
+  }
+  __syncthreads();
+  if (c == 0) {
+    const double s0 = __dadd_rn(lanes[0], lanes[4]), s1 = __dadd_rn(lanes[1], lanes[5]);
+    const double s2 = __dadd_rn(lanes[2], lanes[6]), s3 = __dadd_rn(lanes[3], lanes[7]);
+    double sum = __dadd_rn(__dadd_rn(s0, s2), __dadd_rn(s1, s3));
+    for (int t = full; t < len; ++t) sum = __dadd_rn(sum, (double)e[t]);
+    s_inv = __double2float_rn(__ddiv_rn(1.0, sum));
+  }
+  __syncthreads();
+  const float inv = s_inv;
+  for (int t = c; t < len; t += D) e[t] = __fmul_rn(e[t], inv);
+  __syncthreads();
+  // Sequential V sum per channel: 8 loads in flight ahead of the adds.
+  const __half* vc = a.v_cache + g * D + c;
+  float acc = 0.0f;
+  int t = 0;
+  for (; t + 8 <= len; t += 8) {
+    float v[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) v[u] = __half2float(vc[(size_t)(t + u) * kvw]);
+#pragma unroll
+    for (int u = 0; u < 8; ++u) acc = __fadd_rn(acc, __fmul_rn(v[u], e[t + u]));
+  }
+  for (; t < len; ++t) acc = __fadd_rn(acc, __fmul_rn(__half2float(vc[(size_t)t * kvw]), e[t]));
+  a.attn[(size_t)f * a.heads * D + (size_t)h * D + c] = acc;
+}
+
 // ------------------------------------------------------------- FP32 ----
 
 constexpr int kF32Frames = 4;
@@ -627,7 +792,7 @@ __global__ void silu_pair_kernel(const float* buf, int frames, int ffn, float* a
   for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
     const long long f = i / ffn, k = i - f * ffn;
     const float g = buf[f * 2 * ffn + k], u = buf[f * 2 * ffn + ffn + k];
-    act[i] = __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), u);
+    act[i] = silu_mul1(g, u);
   }
 }
 
@@ -722,6 +887,8 @@ void ensure_gemv_attributes() {
 
 void prepare_kernels() { ensure_gemv_attributes(); }
 
+int k_cache_pos(int c, int head_size) { return kpos(c, head_size); }
+
 int gemv_smem_bytes(int K, int epilogue) {
   return gemv_smem_layout(K, epilogue == kEpiSiluPair ? 2 : 1).total;
 }
@@ -790,6 +957,17 @@ void launch_qk_rope_kv(const AttnArgs& a, cudaStream_t stream) {
 void launch_attention(const AttnArgs& a, cudaStream_t stream) {
   if (a.head_size != 128 || a.heads != 2 * a.kv_heads)
     throw Error(kErrArgument, "attention kernel needs head_size 128 and 2 query heads per KV head");
+  if (a.exact) {
+    if (a.scores == nullptr || a.capacity <= 0 || a.capacity * 4 > kGemvMaxSmem)
+      throw Error(kErrArgument, "exact attention needs a scores buffer and capacity <= 57856");
+    dim3 g1(a.frames, a.kv_heads, a.splits);
+    attn_scores_kernel<<<g1, 256, 0, stream>>>(a);
+    FA_CUDA(cudaGetLastError());
+    dim3 g2(a.frames, a.heads);
+    attn_softmax_v_kernel<<<g2, 128, (size_t)a.capacity * 4, stream>>>(a);
+    FA_CUDA(cudaGetLastError());
+    return;
+  }
   dim3 g1(a.kv_heads, a.splits, a.frames);
   attn_partial_kernel<<<g1, 128, 0, stream>>>(a);
   FA_CUDA(cudaGetLastError());

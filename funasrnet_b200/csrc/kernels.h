@@ -111,10 +111,17 @@ struct AttnArgs {
   __half* v_cache = nullptr;
   const int* pos = nullptr;         // device: KV length before this call
   int splits = 16;                  // partial CTAs per (frame, kv head)
-  float* part = nullptr;            // [F x kv_heads x splits x (4 + 2*head)]
+  float* part = nullptr;            // [F x kv_heads x splits x (4 + 2*head)] (split-K mode)
   float* attn = nullptr;            // [F x q_width]
   const int* skip = nullptr;
+  // exact = 1 (default): scores, softmax and the V sum in the reference's
+  // arithmetic order (bit-identical results); 0: split-K online softmax.
+  int exact = 1;
+  float* scores = nullptr;          // [F x heads x capacity] (exact mode)
+  int capacity = 0;                 // KV capacity (rows of the caches)
 };
+// Cache position of channel c in a K row (lane-permuted layout).
+int k_cache_pos(int c, int head_size);
 
 // QK RMSNorm + RoPE (in place on q), F16 rounding of k/v into the caches.
 void launch_qk_rope_kv(const AttnArgs& a, cudaStream_t stream);

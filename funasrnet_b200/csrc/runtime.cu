@@ -138,6 +138,11 @@ struct fa_session {
   cudaEvent_t ev0 = nullptr, ev1 = nullptr;
   float last_ms = 0.0f;
   int gen_kernels = 0;                       // kernel nodes in gen_graph
+  bool exact_attention = true;               // reference-order attention (bit-identical)
+  DevBuf scores;                             // [frames x heads x capacity] attention scores
+  bool debug = false;                        // keep layer-0 intermediates of decode calls
+  int dbg_frames = 0;
+  DevBuf dbg_q, dbg_attn, dbg_a, dbg_act, dbg_x;
   int* d_int(int i) const { return ints.as<int>() + i; }
 };
 
@@ -285,8 +290,8 @@ static int run_linear(fa_backend* b, const float* input, int frames, const fa_we
   if (w->q8 != want_q8) return kDeclined;
   if (frames <= 0) return kDeclined;
   if (!input || !output) throw Error(kErrArgument, "null input or output");
-  if (want_q8 && gemv_smem_bytes(w->cols, kEpiStore) > 227 * 1024) return kDeclined;
-  if (!want_q8 && (w->fview.w == nullptr || gemv_f32_smem_bytes(w->cols) > 227 * 1024)) return kDeclined;
+  if (want_q8 && gemv_smem_bytes(w->cols, kEpiStore) > 226 * 1024) return kDeclined;
+  if (!want_q8 && (w->fview.w == nullptr || gemv_f32_smem_bytes(w->cols) > 226 * 1024)) return kDeclined;
   std::lock_guard<std::mutex> lk(b->mu);
   if (b->disposed) throw Error(kErrDisposed, "backend disposed");
   DeviceGuard g(b->device);
@@ -461,10 +466,12 @@ int fa_op_attention_pair(fa_backend* b, const float* query, const float* keys, c
     // Device buffers: q (f32), k/v caches (f16), partials, attn, pos.
     std::vector<__half> hk((size_t)frames * kvw), hv((size_t)frames * kvw);
     for (size_t i = 0; i < hk.size(); ++i) {
-      hk[i] = __float2half_rn(keys[i]);
+      const size_t row = i / size, c = i % size;  // K rows in the lane-permuted cache layout
+      hk[row * size + k_cache_pos((int)c, size)] = __float2half_rn(keys[i]);
       hv[i] = __float2half_rn(values[i]);
     }
-    const size_t part_n = (size_t)kv_heads * kAttnSplits * (4 + 2 * size);
+    if ((size_t)frames * 4 > 200 * 1024) return (int)kDeclined;
+    const size_t part_n = (size_t)kv_heads * kAttnSplits * (4 + 2 * size) + (size_t)2 * kv_heads * frames;
     b->in.ensure((size_t)qw * 4 + 16);
     b->aux.ensure(hk.size() * 2 * 2 + 16);
     b->aux2.ensure(part_n * 4);
@@ -489,6 +496,8 @@ int fa_op_attention_pair(fa_backend* b, const float* query, const float* keys, c
     a.pos = dpos;
     a.splits = kAttnSplits;
     a.part = b->aux2.as<float>();
+    a.scores = b->aux2.as<float>() + (size_t)kv_heads * kAttnSplits * (4 + 2 * size);
+    a.capacity = frames;
     a.attn = b->out.as<float>();
     launch_attention(a, b->stream);
     FA_CUDA(cudaMemcpyAsync(output, a.attn, (size_t)qw * 4, cudaMemcpyDeviceToHost, b->stream));
@@ -812,6 +821,9 @@ AttnArgs attn_args(fa_session* s, int layer, int frames, const int* skip) {
   a.part = s->part.as<float>();
   a.attn = s->attn.as<float>();
   a.skip = skip;
+  a.exact = s->exact_attention ? 1 : 0;
+  a.scores = s->scores.as<float>();
+  a.capacity = m->capacity;
   return a;
 }
 
@@ -915,6 +927,22 @@ void enqueue_layers(fa_session* s, int frames, const int* skip) {
       d.skip = skip;
       launch_gemv_f32(d, st);
     }
+    if (l == 0 && s->debug) {
+      // Layer-0 intermediates for the debug hook (never inside a graph).
+      const size_t F = frames;
+      s->dbg_q.ensure(F * qw * 4);
+      s->dbg_attn.ensure(F * qw * 4);
+      s->dbg_a.ensure(F * W * 4);
+      s->dbg_act.ensure(F * m->ffn * 4);
+      s->dbg_x.ensure(F * W * 4);
+      FA_CUDA(cudaMemcpy2DAsync(s->dbg_q.p, qw * 4, s->qkv.p, (size_t)(qw + 2 * kvw) * 4, qw * 4, F,
+                                cudaMemcpyDeviceToDevice, st));
+      FA_CUDA(cudaMemcpyAsync(s->dbg_attn.p, s->attn.p, F * qw * 4, cudaMemcpyDeviceToDevice, st));
+      FA_CUDA(cudaMemcpyAsync(s->dbg_a.p, s->a.p, F * W * 4, cudaMemcpyDeviceToDevice, st));
+      FA_CUDA(cudaMemcpyAsync(s->dbg_act.p, s->act.p, F * m->ffn * 4, cudaMemcpyDeviceToDevice, st));
+      FA_CUDA(cudaMemcpyAsync(s->dbg_x.p, s->x.p, F * W * 4, cudaMemcpyDeviceToDevice, st));
+      s->dbg_frames = frames;
+    }
   }
 }
 
@@ -971,6 +999,12 @@ StepState step_state(fa_session* s) {
 
 cudaGraphExec_t capture(fa_session* s, bool generate, int n_end) {
   cudaGraph_t graph = nullptr;
+  struct DebugOff {  // the debug copies allocate, which a capture must not
+    fa_session* s;
+    bool was;
+    ~DebugOff() { s->debug = was; }
+  } debug_off{s, s->debug};
+  s->debug = false;
   FA_CUDA(cudaStreamBeginCapture(s->stream, cudaStreamCaptureModeThreadLocal));
   try {
     StepState st = step_state(s);
@@ -1051,6 +1085,7 @@ int fa_session_create(fa_model* m, fa_session** out) {
     s->act.ensure((size_t)F * m->ffn * 4);
     if (!m->quantized) s->gu.ensure((size_t)F * 2 * m->ffn * 4);
     s->part.ensure((size_t)F * m->kv_heads * kAttnSplits * (4 + 2 * D) * 4);
+    s->scores.ensure((size_t)F * m->heads * m->capacity * 4);
     s->logits.ensure((size_t)m->vocab * 4);
     const int lm_ctas = (m->vocab + kTileRows - 1) / kTileRows;
     s->am_val.ensure((size_t)lm_ctas * 4);
@@ -1252,6 +1287,28 @@ int fa_session_restore_prefix(fa_session* s) {
 
 int fa_session_kernels_per_step(const fa_session* s) { return s ? s->gen_kernels : -1; }
 
+int fa_session_set_debug(fa_session* s, int on) {
+  return with_session(s, [&] {
+    s->debug = on != 0;
+    return (int)kHandled;
+  });
+}
+
+int fa_session_debug_layer0(fa_session* s, const char* name, float* out) {
+  return with_session(s, [&] {
+    if (!name || !s->debug || s->dbg_frames == 0) throw Error(kErrArgument, "no debug capture");
+    fa_model* m = s->m;
+    const size_t F = s->dbg_frames, qw = (size_t)m->heads * m->head_size;
+    const std::string n(name);
+    const DevBuf* b = n == "q" ? &s->dbg_q : n == "attn" ? &s->dbg_attn : n == "a" ? &s->dbg_a
+                    : n == "act" ? &s->dbg_act : n == "x" ? &s->dbg_x : nullptr;
+    if (!b) throw Error(kErrArgument, "unknown debug buffer");
+    const size_t count = F * (n == "q" || n == "attn" ? qw : n == "act" ? (size_t)m->ffn : (size_t)m->width);
+    if (out) FA_CUDA(cudaMemcpy(out, b->p, count * 4, cudaMemcpyDeviceToHost));
+    return (int)count;
+  });
+}
+
 int fa_session_time_lm_head(fa_session* s, int iters, float* ms) {
   return with_session(s, [&] {
     if (iters < 1 || !ms) throw Error(kErrArgument, "invalid arguments");
@@ -1276,9 +1333,22 @@ int fa_session_kv(fa_session* s, int layer, float* keys, float* values) {
     const size_t off = (size_t)layer * m->capacity * kvw;
     FA_CUDA(cudaMemcpy(hk.data(), s->k_cache.as<__half>() + off, n * 2, cudaMemcpyDeviceToHost));
     FA_CUDA(cudaMemcpy(hv.data(), s->v_cache.as<__half>() + off, n * 2, cudaMemcpyDeviceToHost));
+    const size_t D = m->head_size;
     for (size_t i = 0; i < n; ++i) {
-      keys[i] = __half2float(hk[i]);
+      keys[i] = __half2float(hk[(i / D) * D + k_cache_pos((int)(i % D), (int)D)]);
       values[i] = __half2float(hv[i]);
+    }
+    return (int)kHandled;
+  });
+}
+
+int fa_session_set_exact_attention(fa_session* s, int on) {
+  return with_session(s, [&] {
+    if (s->exact_attention != (on != 0)) {
+      s->exact_attention = on != 0;
+      if (s->step_graph) cudaGraphExecDestroy(s->step_graph);
+      if (s->gen_graph) cudaGraphExecDestroy(s->gen_graph);
+      s->step_graph = s->gen_graph = nullptr;
     }
     return (int)kHandled;
   });

@@ -48,6 +48,12 @@ class CudaModel:
             check(lib().fa_model_free(self._h))
             self._h = None
 
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
 
 class QwenDecoder:
     """One decoding context: its own F16 KV cache, position and CUDA stream."""
@@ -107,6 +113,19 @@ class QwenDecoder:
         check(lib().fa_session_last_generate_ms(self._h, C.byref(ms)))
         return float(ms.value)
 
+    def set_exact_attention(self, on: bool = True) -> None:
+        """True (default): the reference's attention order, bit-identical logits."""
+        check(lib().fa_session_set_exact_attention(self._h, 1 if on else 0))
+
+    def set_debug(self, on: bool = True) -> None:
+        check(lib().fa_session_set_debug(self._h, 1 if on else 0))
+
+    def debug_layer0(self, name: str) -> np.ndarray:
+        n = check(lib().fa_session_debug_layer0(self._h, name.encode(), None))
+        out = np.empty(n, np.float32)
+        check(lib().fa_session_debug_layer0(self._h, name.encode(), ptr(out)))
+        return out
+
     def kernels_per_step(self) -> int:
         return int(lib().fa_session_kernels_per_step(self._h))
 
@@ -137,6 +156,12 @@ class QwenDecoder:
         if self._h is not None:
             check(lib().fa_session_free(self._h))
             self._h = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
 
 
 @dataclass

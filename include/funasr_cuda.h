@@ -164,6 +164,17 @@ int fa_session_cache_prefix(fa_session* session, const int32_t* tokens, int n);
 int fa_session_restore_prefix(fa_session* session);
 /* Test hook: the F16-valued KV history of one layer as floats, [position x kv_width]. */
 int fa_session_kv(fa_session* session, int layer, float* keys, float* values);
+/* Debug hook (the reference's Trace("qwen_layer0", ...) snapshot, QwenDecoder.cs:35,248-251,
+ * extended): when on, later Decode calls keep layer-0 intermediates. */
+int fa_session_set_debug(fa_session* session, int on);
+/* Copies the layer-0 intermediate `name` ("q" after RoPE, "attn", "a", "act",
+ * "x") of the last Decode; returns its float count (out may be NULL). */
+int fa_session_debug_layer0(fa_session* session, const char* name, float* out);
+/* Attention arithmetic: 1 (default) reproduces the reference's order
+ * (8-lane scores, lane-ordered double softmax sum, sequential V sum), giving
+ * logits bit-identical to the CPU decoder; 0 selects split-K online softmax,
+ * faster at long contexts but reassociated (outside the reference's order). */
+int fa_session_set_exact_attention(fa_session* session, int on);
 /* Number of kernel launches one generate iteration replays (kernel nodes of
  * its CUDA graph); 0 before the first fa_session_generate. */
 int fa_session_kernels_per_step(const fa_session* session);

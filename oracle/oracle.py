@@ -66,6 +66,7 @@ def lib() -> C.CDLL:
             "or_session_restore_prefix": (i32, [vp]),
             "or_session_kv": (i32, [vp, i32, vp, vp]),
             "or_session_trace_layer0": (i32, [vp, vp]),
+            "or_session_debug": (i32, [vp, C.c_char_p, vp]),
         }
         for name, (res, args) in sigs.items():
             fn = getattr(h, name)
@@ -246,6 +247,14 @@ class Session:
 
     def restore_prefix(self):
         lib().or_session_restore_prefix(self.h)
+
+    def debug_layer0(self, name):
+        n = lib().or_session_debug(self.h, name.encode(), None)
+        if n < 0:
+            raise KeyError(name)
+        out = np.empty(n, np.float32)
+        lib().or_session_debug(self.h, name.encode(), _p(out))
+        return out
 
     def kv(self, layer):
         n = self.position * self.model.kv_heads * self.model.head_size

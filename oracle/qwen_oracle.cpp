@@ -54,6 +54,32 @@ inline int net_float_to_int(float f) {
 // MathF.Round(v, MidpointRounding.AwayFromZero).
 inline float round_away(float v) { return std::round(v); }
 
+// TensorMath.ExpAvx / ExpReduced (TensorMath.ExpAvx.cs:83-116), one lane:
+// clamp to [-104, 104] (NaN propagates), x = n*ln2 + r with n = round-to-even
+// of x*log2(e), degree-8 Taylor polynomial of exp(r) in double with FMAs,
+// times 2^n, narrowed to float.  The reference selects this exp on .NET 11
+// (its .NET 10 build calls Vector256.Exp, within an ulp of it); the oracle uses
+// it for every exp of the decoder (softmax lanes and tail, SiLU).
+inline float exp_avx(float v) {
+  if (std::isnan(v)) return v;
+  float c = v < -104.0f ? -104.0f : (v > 104.0f ? 104.0f : v);
+  double x = (double)c;
+  double n = std::nearbyint(x * 1.4426950408889634074);
+  double r = std::fma(n, -0.6931471805599453094, x);
+  double square = r * r;
+  double fourth = square * square;
+  double p23 = std::fma(r, 1.0 / 6, 0.5);
+  double p45 = std::fma(r, 1.0 / 120, 1.0 / 24);
+  double p67 = std::fma(r, 1.0 / 5040, 1.0 / 720);
+  double low = std::fma(square, p23, 1.0 + r);
+  double high = std::fma(square, std::fma(square, 1.0 / 40320, p67), p45);
+  double e = std::fma(fourth, high, low);
+  uint64_t bits = (uint64_t)((int64_t)(int32_t)n + 1023) << 52;
+  double scale;
+  std::memcpy(&scale, &bits, 8);
+  return (float)(e * scale);
+}
+
 // Vector128<float>.Sum as lowered by RyuJIT on x64: (v0 + v1) + (v2 + v3).
 inline float sum4(float v0, float v1, float v2, float v3) { return (v0 + v1) + (v2 + v3); }
 
@@ -249,14 +275,14 @@ void or_softmax(float* x, int n) {
   int i = 0;
   for (; i <= n - 8; i += 8)
     for (int j = 0; j < 8; ++j) {
-      x[i + j] = std::exp(x[i + j] - max);
+      x[i + j] = exp_avx(x[i + j] - max);
       lane[j] = lane[j] + (double)x[i + j];
     }
   // Vector256<double>.Sum(low + high): (s0 + s2) + (s1 + s3).
   double s0 = lane[0] + lane[4], s1 = lane[1] + lane[5], s2 = lane[2] + lane[6], s3 = lane[3] + lane[7];
   double sum = (s0 + s2) + (s1 + s3);
   for (; i < n; ++i) {
-    x[i] = std::exp(x[i] - max);
+    x[i] = exp_avx(x[i] - max);
     sum += (double)x[i];
   }
   float inv = (float)(1.0 / sum);
@@ -295,7 +321,7 @@ int or_attention_pair(const float* query, const float* keys, const float* values
 
 void or_silu_mul(float* gate, const float* up, int64_t n) {
   // TensorMath.Elementwise.cs:180,194: g / (1 + exp(-g)) * u.
-  for (int64_t i = 0; i < n; ++i) gate[i] = (gate[i] / (1.0f + std::exp(-gate[i]))) * up[i];
+  for (int64_t i = 0; i < n; ++i) gate[i] = (gate[i] / (1.0f + exp_avx(-gate[i]))) * up[i];
 }
 
 int64_t or_greedy(const float* logits, int64_t n) {
@@ -477,6 +503,9 @@ struct Session {
   int cache_frames = 0;
   std::vector<std::vector<float>> keys, values;
   std::vector<float> layer0;
+  // Layer-0 intermediates of the last Decode (debug hook): q after RoPE,
+  // attention output, residual a, SiLU*up activation, layer output x.
+  std::map<std::string, std::vector<float>> debug;
 };
 
 int decode(Session& s, const float* emb, int frames, float* logits) {
@@ -541,6 +570,13 @@ int decode(Session& s, const float* emb, int frames, float* logits) {
     linear(m.t(p + "ffn_down.weight"), gate.data(), frames, x.data());
     for (size_t i = 0; i < x.size(); ++i) x[i] = x[i] + a[i];  // TensorMath.Add(x, a)
     if (s.position == 0 && layer == 0) s.layer0 = x;
+    if (layer == 0) {
+      s.debug["q"] = q;
+      s.debug["attn"] = attn;
+      s.debug["a"] = a;
+      s.debug["act"] = gate;
+      s.debug["x"] = x;
+    }
   }
   s.position += frames;
   if (!logits) return 0;
@@ -698,6 +734,14 @@ int or_session_kv(void* session, int layer, float* keys, float* values) {
   std::memcpy(keys, s->keys[layer].data(), n * 4);
   std::memcpy(values, s->values[layer].data(), n * 4);
   return 0;
+}
+
+int or_session_debug(void* session, const char* name, float* out) {
+  Session* s = static_cast<Session*>(session);
+  auto it = s->debug.find(name);
+  if (it == s->debug.end()) return -1;
+  if (out) std::memcpy(out, it->second.data(), it->second.size() * 4);
+  return (int)it->second.size();
 }
 
 int or_session_trace_layer0(void* session, float* out) {

@@ -111,6 +111,9 @@ int or_session_restore_prefix(void* session);
 int or_session_kv(void* session, int layer, float* keys, float* values);
 /* Layer-0 residual output of the last Decode at position 0 (the qwen_layer0 trace). */
 int or_session_trace_layer0(void* session, float* out);
+/* Layer-0 intermediates of the last Decode: "q" (after RoPE), "attn", "a",
+ * "act", "x".  Returns the float count (out may be NULL to query it). */
+int or_session_debug(void* session, const char* name, float* out);
 
 #ifdef __cplusplus
 }

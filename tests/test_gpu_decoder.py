@@ -1,9 +1,17 @@
 """End-to-end decoder parity with the CPU oracle through the C ABI.
 
-Tolerances are the north-star ones: logits within 2e-2 absolute and 1e-3
-relative to max|logit|, greedy tokens identical wherever the oracle's top-2
-margin exceeds 1e-2.  Sequences are compared teacher-forced (both sides are fed
-the oracle's token) so one near-tie cannot derail the comparison.
+The default (exact-attention) decoder reproduces the reference's arithmetic
+order everywhere, so its logits are compared bit for bit.  The north-star
+tolerance (numpy.allclose: every logit within 2e-2 + 1e-3 * |oracle logit|;
+greedy tokens identical wherever the oracle's top-2 margin exceeds 1e-2) is
+checked as well.  Sequences are compared teacher-forced (both sides are fed
+the oracle's token).
+
+Why bit-exactness is required rather than nice to have: every projection
+re-quantises its input to int8 per 32-block, so a 1-ulp difference upstream
+can flip one rounding (one quantum, ~1e-4..1e-3 in the residual stream) and
+28 layers amplify that past the tolerance; the split-K attention option
+(fa_session_set_exact_attention(0)) shows exactly that.
 """
 import numpy as np
 import pytest
@@ -17,15 +25,17 @@ REL_TOL = 1e-3
 MARGIN = 1e-2
 
 
-def check_logits(got, exp, what=""):
-    err = np.max(np.abs(got.astype(np.float64) - exp))
-    scale = np.max(np.abs(exp))
-    assert err <= ABS_TOL, f"{what}: max abs error {err}"
-    assert err <= REL_TOL * max(1.0, scale), f"{what}: relative error {err / scale}"
+def check_logits(got, exp, what="", exact=True):
+    if exact:
+        assert_bits_equal(got, exp, what)
+    err = np.abs(got.astype(np.float64) - exp)
+    bound = ABS_TOL + REL_TOL * np.abs(exp.astype(np.float64))
+    worst = int(np.argmax(err - bound))
+    assert np.all(err <= bound), f"{what}: logit {worst} off by {err[worst]} (bound {bound[worst]})"
     top2 = np.sort(exp)[-2:]
     if top2[1] - top2[0] > MARGIN:
         assert int(np.argmax(got)) == int(np.argmax(exp)), f"{what}: argmax differs with margin {top2[1] - top2[0]}"
-    return err
+    return float(err.max())
 
 
 def prefix_embeddings(om, audio, ids, seed):
@@ -34,6 +44,26 @@ def prefix_embeddings(om, audio, ids, seed):
     a = rng.standard_normal(audio * om.width).astype(np.float32)
     toks = rng.integers(0, om.vocab, ids)
     return np.concatenate([a, om.embed(toks)]), audio + ids
+
+
+@pytest.fixture(autouse=True)
+def _close_sessions(monkeypatch):
+    """Closes every decoder session a test opened, even when it fails, so the
+    module's model can be freed (the library refuses to free a model with
+    live sessions)."""
+    from funasrnet_b200 import decoder as D
+
+    opened = []
+    orig = D.QwenDecoder.__init__
+
+    def init(self, *a, **k):
+        orig(self, *a, **k)
+        opened.append(self)
+
+    monkeypatch.setattr(D.QwenDecoder, "__init__", init)
+    yield
+    for d in opened:
+        d.close()
 
 
 @pytest.fixture(scope="module")
