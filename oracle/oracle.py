@@ -47,6 +47,7 @@ def lib() -> C.CDLL:
             "or_attention_pair": (i32, [vp, vp, vp, i32, i32, i32, vp]),
             "or_silu_mul": (None, [vp, vp, i64]),
             "or_greedy": (i64, [vp, i64]),
+            "or_exp": (f32, [f32]),
             "or_half_to_float": (f32, [C.c_uint16]),
             "or_float_to_half": (C.c_uint16, [f32]),
             "or_model_load": (vp, [C.c_char_p, i32]),

@@ -324,6 +324,8 @@ void or_silu_mul(float* gate, const float* up, int64_t n) {
   for (int64_t i = 0; i < n; ++i) gate[i] = (gate[i] / (1.0f + exp_avx(-gate[i]))) * up[i];
 }
 
+float or_exp(float x) { return exp_avx(x); }
+
 int64_t or_greedy(const float* logits, int64_t n) {
   // QwenDecoder.cs:278-326: first index of the strict maximum; NaN never wins,
   // and a NaN logits[0] makes every comparison false (returns 0).

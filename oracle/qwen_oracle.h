@@ -73,6 +73,10 @@ int or_attention_pair(const float* query, const float* keys, const float* values
 /* TensorMath.SiluMultiply, TensorMath.Elementwise.cs:167-196 (gate overwritten). */
 void or_silu_mul(float* gate, const float* up, int64_t n);
 
+/* TensorMath.ExpAvx (TensorMath.ExpAvx.cs:83-116) for one value: the exp the
+ * oracle uses everywhere. */
+float or_exp(float x);
+
 /* QwenDecoder.Greedy, QwenDecoder.cs:278-326. */
 int64_t or_greedy(const float* logits, int64_t n);
 
