@@ -15,10 +15,13 @@
 #include <climits>
 #include <mutex>
 
+#include "device_math.cuh"
 #include "kernels.h"
 
 namespace fa {
 namespace {
+
+using namespace dev;
 
 constexpr int kGemvThreads = 256;
 constexpr int kGemvWarps = kGemvThreads / 32;
@@ -30,143 +33,45 @@ constexpr int kGemvMaxSmem = 226 * 1024;
 
 __device__ __forceinline__ bool skipped(const int* skip) { return skip != nullptr && *skip != 0; }
 
-// MathF.Round(v, MidpointRounding.AwayFromZero) as TensorMath.QuantizeAvx.cs:182-189
-// computes it: truncate, then step away from zero when |fraction| >= 0.5.
-__device__ __forceinline__ float round_away(float v) {
-  float t = truncf(v);
-  if (fabsf(__fsub_rn(v, t)) >= 0.5f) t = __fadd_rn(t, copysignf(1.0f, v));
-  return t;
-}
-
-// clamp((int)round_away(x * inv), -127, 127); cvt.rzi saturates and maps NaN
-// to 0 exactly like .NET 9+'s float->int conversion.
-__device__ __forceinline__ int quant1(float x, float inv) {
-  int r = __float2int_rz(round_away(__fmul_rn(x, inv)));
-  return max(-127, min(127, r));
-}
-
-// Block scale from the block's |x| maximum taken on the IEEE bit patterns
-// (TensorMath.QuantizeAvx.cs:145-150): d = amax / 127, inv = d == 0 ? 0 : 1 / d.
-__device__ __forceinline__ void block_scale(float v, float& d, float& inv) {
-  unsigned bits = __float_as_uint(v) & 0x7fffffffu;
-  unsigned mb = __reduce_max_sync(0xffffffffu, bits);
-  d = __fdiv_rn(__uint_as_float(mb), 127.0f);
-  inv = d == 0.0f ? 0.0f : __fdiv_rn(1.0f, d);
-}
-
-__device__ __forceinline__ double warp_sum_d(double v) {
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) v = __dadd_rn(v, __shfl_xor_sync(0xffffffffu, v, o));
-  return v;
-}
-__device__ __forceinline__ float warp_sum_f(float v) {
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, o));
-  return v;
-}
-
-// exp as the reference's TensorMath.ExpAvx (TensorMath.ExpAvx.cs:83-116)
-// evaluates it per lane: clamp to [-104, 104] (NaN propagates), x = n*ln2 + r
-// with n = round-half-even(x * log2 e), degree-8 Taylor polynomial of exp(r)
-// in double with FMAs, scaled by 2^n and narrowed to float.  Every operation
-// is a correctly rounded IEEE double op, so the result is bit-identical to the
-// same evaluation on the host.
-__device__ __forceinline__ float exp_ref(float v) {
-  if (isnan(v)) return v;
-  const float c = v < -104.0f ? -104.0f : (v > 104.0f ? 104.0f : v);
-  const double x = (double)c;
-  const double n = rint(__dmul_rn(x, 1.4426950408889634074));
-  const double r = __fma_rn(n, -0.6931471805599453094, x);
-  const double square = __dmul_rn(r, r);
-  const double fourth = __dmul_rn(square, square);
-  const double p23 = __fma_rn(r, 1.0 / 6, 0.5);
-  const double p45 = __fma_rn(r, 1.0 / 120, 1.0 / 24);
-  const double p67 = __fma_rn(r, 1.0 / 5040, 1.0 / 720);
-  const double low = __fma_rn(square, p23, __dadd_rn(1.0, r));
-  const double high = __fma_rn(square, __fma_rn(square, 1.0 / 40320, p67), p45);
-  const double e = __fma_rn(fourth, high, low);
-  const double scale = __longlong_as_double((long long)(__double2int_rz(n) + 1023) << 52);
-  return __double2float_rn(__dmul_rn(e, scale));
-}
-
-// SiLU(g) * u as TensorMath.Elementwise.cs:180: g / (1 + exp(-g)) * u.
-__device__ __forceinline__ float silu_mul1(float g, float u) {
-  return __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, exp_ref(-g))), u);
-}
-
-// 1 / sqrt((float)(sumsq / width) + eps)  (TensorMath.Elementwise.cs:78)
-__device__ __forceinline__ float rms_inverse(double sumsq, int width, float eps) {
-  float ms = __double2float_rn(__ddiv_rn(sumsq, (double)width));
-  return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(ms, eps)));
-}
-
-template <bool F16S>
-__device__ __forceinline__ float load_scale(const Q8View& w, int tile, int b, int lane) {
-  if (F16S) {
-    const __half* p = reinterpret_cast<const __half*>(
-        static_cast<const uint8_t*>(w.s) + (((size_t)tile * w.scale_groups + (b >> 3)) * 32 + lane) * 16);
-    return __half2float(p[b & 7]);
-  } else {
-    const float* p = reinterpret_cast<const float*>(
-        static_cast<const uint8_t*>(w.s) + (((size_t)tile * w.scale_groups + (b >> 2)) * 32 + lane) * 16);
-    return p[b & 3];
-  }
-}
-
-__device__ __forceinline__ int dot32(const uint4& wa, const uint4& wb, const int4& x0, const int4& x1) {
-  int d = __dp4a((int)wa.x, x0.x, 0);
-  d = __dp4a((int)wa.y, x0.y, d);
-  d = __dp4a((int)wa.z, x0.z, d);
-  d = __dp4a((int)wa.w, x0.w, d);
-  d = __dp4a((int)wb.x, x1.x, d);
-  d = __dp4a((int)wb.y, x1.y, d);
-  d = __dp4a((int)wb.z, x1.z, d);
-  d = __dp4a((int)wb.w, x1.w, d);
-  return d;
-}
-
-// (value, index) ordering of QwenDecoder.Greedy: larger value wins, equal
-// values keep the lower index, NaN never wins.
-__device__ __forceinline__ bool better(float v2, int i2, float v1, int i1) {
-  if (isnan(v2)) return false;
-  if (isnan(v1)) return true;
-  return v2 > v1 || (v2 == v1 && i2 < i1);
-}
-
 struct GemvSmem {
-  int xq, xs, prod, red, total;
+  int xq, xs, prod, red, total, pstride;
 };
 
-__host__ __device__ inline GemvSmem gemv_smem_layout(int K, int tiles_per_cta) {
+constexpr int kGemvTiles = 4;  // 8-row tiles per CTA (32 rows; 2 gate/up pairs)
+
+__host__ __device__ inline GemvSmem gemv_smem_layout(int K) {
   GemvSmem s;
-  int B = K / 32;
+  const int B = K / 32;
+  s.pstride = B * 8 + 8;  // floats per (frame, tile) of products, padded against bank conflicts
   s.xq = 0;
   s.xs = (kGemvFrames * K + 15) & ~15;
   s.prod = (s.xs + kGemvFrames * B * 4 + 15) & ~15;
-  s.red = (s.prod + kGemvFrames * tiles_per_cta * B * 32 * 4 + 15) & ~15;
+  s.red = (s.prod + kGemvFrames * kGemvTiles * s.pstride * 4 + 15) & ~15;
   s.total = s.red + 16 * 8;
   return s;
 }
 
-// Fused [RMSNorm] -> per-32-block int8 quantisation -> Q8 W8A8 GEMV -> epilogue.
-// One CTA owns one 32-row tile (two for the gate/up pair) and up to 4 frames.
-// Warps split the (tile, block) units; each lane handles one row and stores
-// the block products p_b = ((float)dot_b * ws) * xs, then warp 0 sums them in
-// block order, which is the reference's accumulation order
+// Fused [RMSNorm] -> per-32-block int8 quantisation -> Q8 W8A8 GEMV -> epilogue
+// over 8-row tiles.  One CTA owns 4 consecutive tiles (32 rows, or two
+// gate/up pairs) and up to 4 frames.  A warp unit is (tile, block pair): lane
+// = (block parity, chunk half, row), so one instruction reads 512 contiguous
+// bytes; the two chunk halves' integer dots are added with a shuffle and the
+// even-half lanes store the block product p_b = ((float)dot_b * ws) * xs.
+// Then one thread per row sums p_b in block order: the reference's order
 // (TensorMath.QuantizedRowsAvx.cs:30-41, TensorMath.QuantizedGroupAvx.cs:121-132).
 template <bool F16S>
 __global__ void __launch_bounds__(kGemvThreads) gemv_kernel(const GemvArgs a) {
   if (skipped(a.skip)) return;
   extern __shared__ __align__(16) uint8_t smem[];
-  const int K = a.w.cols, B = K / 32;
-  const int tpc = a.epilogue == kEpiSiluPair ? 2 : 1;
-  const GemvSmem L = gemv_smem_layout(K, tpc);
+  const int K = a.w.cols, B = K / 32, BP = (B + 1) / 2;
+  const GemvSmem L = gemv_smem_layout(K);
   int8_t* xq = reinterpret_cast<int8_t*>(smem + L.xq);
   float* xs = reinterpret_cast<float*>(smem + L.xs);
   float* prod = reinterpret_cast<float*>(smem + L.prod);
   double* red = reinterpret_cast<double*>(smem + L.red);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int tile0 = blockIdx.x * tpc;
+  const int tile0 = blockIdx.x * kGemvTiles;
+  const int ntiles = min(kGemvTiles, a.w.tiles - tile0);
   const int f0 = blockIdx.y * kGemvFrames;
   const int fc = min(kGemvFrames, a.frames - f0);
 
@@ -200,64 +105,70 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_kernel(const GemvArgs a) {
   }
   __syncthreads();
 
-  // ---- main loop: stream the tile(s), one 32-value block per unit ----
-  const int units = tpc * B;
+  // ---- main loop: warp units (tile, block pair) ----
+  const int row = lane & 7, half = (lane >> 3) & 1, bsel = lane >> 4;
+  const int units = ntiles * BP;
   for (int u0 = warp; u0 < units; u0 += kGemvWarps * kGemvUnroll) {
-    uint4 wa[kGemvUnroll], wb[kGemvUnroll];
+    uint4 wv[kGemvUnroll];
     float ws[kGemvUnroll];
 #pragma unroll
     for (int i = 0; i < kGemvUnroll; ++i) {
       const int u = u0 + kGemvWarps * i;
-      if (u < units) {
-        const int t = u / B, b = u - t * B, tile = tile0 + t;
-        const uint8_t* tq = a.w.q + (size_t)tile * 32 * K;
-        wa[i] = __ldg(reinterpret_cast<const uint4*>(tq + (size_t)(2 * b) * 512 + lane * 16));
-        wb[i] = __ldg(reinterpret_cast<const uint4*>(tq + (size_t)(2 * b + 1) * 512 + lane * 16));
-        ws[i] = load_scale<F16S>(a.w, tile, b, lane);
+      const int t = u / BP, b = 2 * (u - t * BP) + bsel;
+      wv[i] = make_uint4(0, 0, 0, 0);
+      ws[i] = 0.0f;
+      if (u < units && b < B) {
+        const uint8_t* tile = a.w.base + (size_t)(tile0 + t) * a.w.tile_bytes;
+        wv[i] = __ldg(reinterpret_cast<const uint4*>(tile + (size_t)(2 * b + half) * 128 + row * 16));
+        ws[i] = tile_scale<F16S>(tile, K, b, row);
       }
     }
 #pragma unroll
     for (int i = 0; i < kGemvUnroll; ++i) {
       const int u = u0 + kGemvWarps * i;
-      if (u < units) {
-        const int t = u / B, b = u - t * B;
-        for (int fi = 0; fi < fc; ++fi) {
-          const int4* xp = reinterpret_cast<const int4*>(xq + fi * K + b * 32);
-          const int dot = dot32(wa[i], wb[i], xp[0], xp[1]);
-          const float p = __fmul_rn(__fmul_rn(__int2float_rn(dot), ws[i]), xs[fi * B + b]);
-          prod[((fi * tpc + t) * B + b) * 32 + lane] = p;
-        }
+      if (u >= units) break;  // warp-uniform
+      const int t = u / BP, b = 2 * (u - t * BP) + bsel;
+      const bool valid = b < B;
+      for (int fi = 0; fi < fc; ++fi) {
+        int part = 0;
+        if (valid) part = dot16(wv[i], *reinterpret_cast<const int4*>(xq + fi * K + b * 32 + half * 16));
+        const int dot = part + __shfl_xor_sync(0xffffffffu, part, 8);
+        if (valid && half == 0)
+          prod[(fi * kGemvTiles + t) * L.pstride + b * 8 + row] =
+              __fmul_rn(__fmul_rn(__int2float_rn(dot), ws[i]), xs[fi * B + b]);
       }
     }
   }
   __syncthreads();
 
-  // ---- ordered block sums + epilogue (warp 0: lane = row) ----
-  if (warp != 0) return;
+  // ---- ordered block sums + epilogue: thread t < 32 owns (tile t/8, row t%8) ----
+  if (threadIdx.x >= kGemvTiles * 8) return;
+  const int ti = threadIdx.x >> 3, r = threadIdx.x & 7;
   const int N = a.w.rows;
   if (a.epilogue == kEpiSiluPair) {
-    const int row = blockIdx.x * 32 + lane;  // gate/up row of this pair
+    if ((ti & 1) || ti + 1 >= ntiles) return;  // even tile = gate, odd = up
+    const int grow = ((tile0 + ti) >> 1) * 8 + r;
     for (int fi = 0; fi < fc; ++fi) {
       float g = 0.0f, u = 0.0f;
-      const float* pg = prod + (size_t)(fi * 2 + 0) * B * 32 + lane;
-      const float* pu = prod + (size_t)(fi * 2 + 1) * B * 32 + lane;
-      for (int b = 0; b < B; ++b) g = __fadd_rn(g, pg[b * 32]);
-      for (int b = 0; b < B; ++b) u = __fadd_rn(u, pu[b * 32]);
-      // TensorMath.Elementwise.cs:180: g / (1 + exp(-g)) * u
-      const float act = silu_mul1(g, u);
-      if (row < a.out_stride) a.out[(size_t)(f0 + fi) * a.out_stride + row] = act;
+      const float* pg = prod + (fi * kGemvTiles + ti) * L.pstride + r;
+      const float* pu = pg + L.pstride;
+      for (int b = 0; b < B; ++b) g = __fadd_rn(g, pg[b * 8]);
+      for (int b = 0; b < B; ++b) u = __fadd_rn(u, pu[b * 8]);
+      if (grow < a.out_stride) a.out[(size_t)(f0 + fi) * a.out_stride + grow] = silu_mul1(g, u);
     }
     return;
   }
-  const int row = tile0 * 32 + lane;
+  const int grow = (tile0 + ti) * 8 + r;
   if (a.epilogue == kEpiArgmax) {
     float s = 0.0f;
-    const float* pp = prod + lane;
-    for (int b = 0; b < B; ++b) s = __fadd_rn(s, pp[b * 32]);
-    const bool valid = row < N;
-    if (valid && a.logits != nullptr) a.logits[row] = s;
+    if (ti < ntiles) {
+      const float* pp = prod + ti * L.pstride + r;
+      for (int b = 0; b < B; ++b) s = __fadd_rn(s, pp[b * 8]);
+    }
+    const bool valid = ti < ntiles && grow < N;
+    if (valid && a.logits != nullptr) a.logits[grow] = s;
     float bv = valid ? s : __int_as_float(0x7fc00000);
-    int bi = valid ? row : INT_MAX;
+    int bi = valid ? grow : INT_MAX;
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
       float ov = __shfl_xor_sync(0xffffffffu, bv, o);
@@ -268,10 +179,10 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_kernel(const GemvArgs a) {
       }
     }
     unsigned last = 0u;
-    if (lane == 0) {
+    if (threadIdx.x == 0) {
       a.am.part_value[blockIdx.x] = bv;
       a.am.part_index[blockIdx.x] = bi;
-      if (blockIdx.x == 0) *a.am.row0_nan = isnan(s) ? 1 : 0;  // lane 0 of CTA 0 holds row 0
+      if (blockIdx.x == 0) *a.am.row0_nan = isnan(s) ? 1 : 0;  // thread 0 of CTA 0 holds row 0
       __threadfence();
       last = atomicAdd(a.am.counter, 1u) == gridDim.x - 1 ? 1u : 0u;
     }
@@ -303,16 +214,16 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_kernel(const GemvArgs a) {
     }
     return;
   }
-  if (row >= N) return;
+  if (ti >= ntiles || grow >= N) return;
   for (int fi = 0; fi < fc; ++fi) {
     float s = 0.0f;
-    const float* pp = prod + (size_t)fi * B * 32 + lane;
-    for (int b = 0; b < B; ++b) s = __fadd_rn(s, pp[b * 32]);
-    float* o = a.out + (size_t)(f0 + fi) * a.out_stride + row;
+    const float* pp = prod + (fi * kGemvTiles + ti) * L.pstride + r;
+    for (int b = 0; b < B; ++b) s = __fadd_rn(s, pp[b * 8]);
+    float* o = a.out + (size_t)(f0 + fi) * a.out_stride + grow;
     if (a.epilogue == kEpiResidual) {
-      *o = __fadd_rn(s, a.res[(size_t)(f0 + fi) * a.out_stride + row]);
+      *o = __fadd_rn(s, a.res[(size_t)(f0 + fi) * a.out_stride + grow]);
     } else {
-      *o = a.bias != nullptr ? __fadd_rn(a.bias[row], s) : s;
+      *o = a.bias != nullptr ? __fadd_rn(a.bias[grow], s) : s;
     }
   }
 }
@@ -412,11 +323,11 @@ __global__ void embed_kernel(const Q8View w, const int* tokens, float* x, const 
   const int K = w.cols, f = blockIdx.x;
   int row = tokens[f];
   row = row < 0 ? 0 : (row >= w.rows ? w.rows - 1 : row);  // host validates ranges
-  const int tile = row >> 5, r = row & 31;
+  const int r = row & 7;
+  const uint8_t* tile = w.base + (size_t)(row >> 3) * w.tile_bytes;
   for (int c = threadIdx.x; c < K / 16; c += blockDim.x) {
-    const uint8_t* src = w.q + (size_t)tile * 32 * K + (size_t)c * 512 + r * 16;
-    const uint4 v = *reinterpret_cast<const uint4*>(src);
-    const float s = load_scale<F16S>(w, tile, c >> 1, r);
+    const uint4 v = *reinterpret_cast<const uint4*>(tile + (size_t)c * 128 + r * 16);
+    const float s = tile_scale<F16S>(tile, K, c >> 1, r);
     const int8_t* b = reinterpret_cast<const int8_t*>(&v);
     float* out = x + (size_t)f * K + c * 16;
 #pragma unroll
@@ -468,10 +379,10 @@ __global__ void qk_rope_kv_kernel(const AttnArgs a) {
     const float o = c < half ? __fsub_rn(__fmul_rn(av, co), __fmul_rn(bv, si))
                              : __fadd_rn(__fmul_rn(av, si), __fmul_rn(bv, co));
     if (isq) xp[c] = o;
-    else a.k_cache[(size_t)p * kvw + (h - a.heads) * D + kpos(c, D)] = __float2half_rn(o);  // QwenDecoder.cs:199
+    else a.k_cache[((size_t)(h - a.heads) * a.capacity + p) * D + kpos(c, D)] = __float2half_rn(o);  // QwenDecoder.cs:199
   } else {
     const int vh = h - a.heads - a.kv_heads;
-    a.v_cache[(size_t)p * kvw + vh * D + c] = __float2half_rn(base[qw + kvw + vh * D + c]);  // :200
+    a.v_cache[((size_t)vh * a.capacity + p) * D + c] = __float2half_rn(base[qw + kvw + vh * D + c]);  // :200
   }
 }
 
@@ -499,8 +410,8 @@ __global__ void __launch_bounds__(128) attn_partial_kernel(const AttnArgs a) {
   float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.0f, l1 = 0.0f;
   float acc0[4] = {0, 0, 0, 0}, acc1[4] = {0, 0, 0, 0};
   for (int t = t0 + warp; t < t1; t += 4) {
-    const __half* kr = a.k_cache + (size_t)t * kvw + g * D + 4 * lane;
-    const __half* vr = a.v_cache + (size_t)t * kvw + g * D + 4 * lane;
+    const __half* kr = a.k_cache + ((size_t)g * a.capacity + t) * D + 4 * lane;
+    const __half* vr = a.v_cache + ((size_t)g * a.capacity + t) * D + 4 * lane;
     const uint2 kk = *reinterpret_cast<const uint2*>(kr);
     const uint2 vv = *reinterpret_cast<const uint2*>(vr);
     const float2 k01 = __half22float2(*reinterpret_cast<const __half2*>(&kk.x));
@@ -618,7 +529,7 @@ __global__ void __launch_bounds__(256) attn_scores_kernel(const AttnArgs a) {
     const int t = base + slot;
     float acc0 = 0.0f, acc1 = 0.0f;
     if (t < t1) {
-      const uint4* kr = reinterpret_cast<const uint4*>(a.k_cache + (size_t)t * kvw + g * D + j * M);
+      const uint4* kr = reinterpret_cast<const uint4*>(a.k_cache + ((size_t)g * a.capacity + t) * D + j * M);
       const uint4 ka = kr[0], kb = kr[1];
       const __half* kh0 = reinterpret_cast<const __half*>(&ka);
       const __half* kh1 = reinterpret_cast<const __half*>(&kb);
@@ -694,17 +605,17 @@ __global__ void __launch_bounds__(128) attn_softmax_v_kernel(const AttnArgs a) {
   for (int t = c; t < len; t += D) e[t] = __fmul_rn(e[t], inv);
   __syncthreads();
   // Sequential V sum per channel: 8 loads in flight ahead of the adds.
-  const __half* vc = a.v_cache + g * D + c;
+  const __half* vc = a.v_cache + (size_t)g * a.capacity * D + c;
   float acc = 0.0f;
   int t = 0;
   for (; t + 8 <= len; t += 8) {
     float v[8];
 #pragma unroll
-    for (int u = 0; u < 8; ++u) v[u] = __half2float(vc[(size_t)(t + u) * kvw]);
+    for (int u = 0; u < 8; ++u) v[u] = __half2float(vc[(size_t)(t + u) * D]);
 #pragma unroll
     for (int u = 0; u < 8; ++u) acc = __fadd_rn(acc, __fmul_rn(v[u], e[t + u]));
   }
-  for (; t < len; ++t) acc = __fadd_rn(acc, __fmul_rn(__half2float(vc[(size_t)t * kvw]), e[t]));
+  for (; t < len; ++t) acc = __fadd_rn(acc, __fmul_rn(__half2float(vc[(size_t)t * D]), e[t]));
   a.attn[(size_t)f * a.heads * D + (size_t)h * D + c] = acc;
 }
 
@@ -889,16 +800,14 @@ void prepare_kernels() { ensure_gemv_attributes(); }
 
 int k_cache_pos(int c, int head_size) { return kpos(c, head_size); }
 
-int gemv_smem_bytes(int K, int epilogue) {
-  return gemv_smem_layout(K, epilogue == kEpiSiluPair ? 2 : 1).total;
-}
+int gemv_smem_bytes(int K, int) { return gemv_smem_layout(K).total; }
 
 void launch_gemv(const GemvArgs& a, cudaStream_t stream) {
-  const int tpc = a.epilogue == kEpiSiluPair ? 2 : 1;
-  const int smem = gemv_smem_layout(a.w.cols, tpc).total;
+  const int smem = gemv_smem_layout(a.w.cols).total;
   if (smem > kGemvMaxSmem) throw Error(kErrCapacity, "GEMV inner dimension too large for shared memory");
+  if (a.epilogue == kEpiSiluPair && (a.w.tiles & 1)) throw Error(kErrArgument, "gate/up pairs need an even tile count");
   ensure_gemv_attributes();
-  dim3 grid((a.w.tiles + tpc - 1) / tpc, (a.frames + kGemvFrames - 1) / kGemvFrames);
+  dim3 grid((a.w.tiles + kGemvTiles - 1) / kGemvTiles, (a.frames + kGemvFrames - 1) / kGemvFrames);
   if (a.epilogue == kEpiArgmax && a.frames != 1) throw Error(kErrArgument, "argmax epilogue needs one frame");
   if (a.w.scale_f16) {
     gemv_kernel<true><<<grid, kGemvThreads, smem, stream>>>(a);

@@ -80,58 +80,53 @@ static void parallel_for(int64_t n, const std::function<void(int64_t, int64_t)>&
   for (auto& th : pool) th.join();
 }
 
-void pack_q8(const int8_t* q, const float* scales, int rows, int cols, bool f16, uint8_t* out_q,
-             uint8_t* out_s) {
+void pack_q8(const int8_t* q, const float* scales, int rows, int cols, bool f16, uint8_t* out) {
   const int tiles = (rows + kTileRows - 1) / kTileRows;
   const int blocks = cols / 32;
   const int chunks = cols / 16;
-  const int groups = q8_scale_groups(cols, f16);
-  const int per = f16 ? 8 : 4;
-  std::memset(out_q, 0, q8_bytes_q(rows, cols));
-  std::memset(out_s, 0, q8_bytes_s(rows, cols, f16));
+  const size_t tb = (size_t)q8_tile_bytes(cols, f16);
+  std::memset(out, 0, q8_bytes(rows, cols, f16));
   parallel_for(tiles, [&](int64_t t0, int64_t t1) {
-    for (int64_t t = t0; t < t1; ++t)
+    for (int64_t t = t0; t < t1; ++t) {
+      uint8_t* tile = out + (size_t)t * tb;
       for (int r = 0; r < kTileRows; ++r) {
         int64_t row = t * kTileRows + r;
         if (row >= rows) break;
-        uint8_t* tq = out_q + (size_t)t * kTileRows * cols;
         for (int c = 0; c < chunks; ++c)
-          std::memcpy(tq + (size_t)c * 512 + r * 16, q + (size_t)row * cols + c * 16, 16);
+          std::memcpy(tile + (size_t)c * 128 + r * 16, q + (size_t)row * cols + c * 16, 16);
         for (int b = 0; b < blocks; ++b) {
-          int g = b / per, slot = b % per;
-          uint8_t* dst = out_s + (((size_t)t * groups + g) * kTileRows + r) * 16;
           float s = scales[(size_t)row * blocks + b];
           if (f16) {
             uint16_t h = float_to_half_bits(s);
-            std::memcpy(dst + slot * 2, &h, 2);
+            std::memcpy(tile + (size_t)8 * cols + ((size_t)b * 8 + r) * 2, &h, 2);
           } else {
-            std::memcpy(dst + slot * 4, &s, 4);
+            std::memcpy(tile + (size_t)8 * cols + ((size_t)b * 8 + r) * 4, &s, 4);
           }
         }
       }
+    }
   });
 }
 
-void pack_q8_from_gguf(const uint8_t* blocks_in, int rows, int cols, uint8_t* out_q, uint8_t* out_s) {
+void pack_q8_from_gguf(const uint8_t* blocks_in, int rows, int cols, uint8_t* out) {
   const int tiles = (rows + kTileRows - 1) / kTileRows;
   const int blocks = cols / 32;
-  const int groups = q8_scale_groups(cols, true);
-  std::memset(out_q, 0, q8_bytes_q(rows, cols));
-  std::memset(out_s, 0, q8_bytes_s(rows, cols, true));
+  const size_t tb = (size_t)q8_tile_bytes(cols, true);
+  std::memset(out, 0, q8_bytes(rows, cols, true));
   parallel_for(tiles, [&](int64_t t0, int64_t t1) {
-    for (int64_t t = t0; t < t1; ++t)
+    for (int64_t t = t0; t < t1; ++t) {
+      uint8_t* tile = out + (size_t)t * tb;
       for (int r = 0; r < kTileRows; ++r) {
         int64_t row = t * kTileRows + r;
         if (row >= rows) break;
-        uint8_t* tq = out_q + (size_t)t * kTileRows * cols;
         for (int b = 0; b < blocks; ++b) {
           const uint8_t* blk = blocks_in + ((size_t)row * blocks + b) * 34;
-          std::memcpy(tq + (size_t)(2 * b) * 512 + r * 16, blk + 2, 16);
-          std::memcpy(tq + (size_t)(2 * b + 1) * 512 + r * 16, blk + 18, 16);
-          uint8_t* dst = out_s + (((size_t)t * groups + b / 8) * kTileRows + r) * 16;
-          std::memcpy(dst + (b % 8) * 2, blk, 2);  // f16 scale bits, little endian
+          std::memcpy(tile + (size_t)(2 * b) * 128 + r * 16, blk + 2, 16);
+          std::memcpy(tile + (size_t)(2 * b + 1) * 128 + r * 16, blk + 18, 16);
+          std::memcpy(tile + (size_t)8 * cols + ((size_t)b * 8 + r) * 2, blk, 2);  // f16 scale, LE
         }
       }
+    }
   });
 }
 

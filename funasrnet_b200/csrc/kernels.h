@@ -107,8 +107,8 @@ struct AttnArgs {
   float eps = 1e-6f;
   const float* rope_cos = nullptr;  // [capacity x head/2]
   const float* rope_sin = nullptr;
-  __half* k_cache = nullptr;        // [capacity x kv_width]
-  __half* v_cache = nullptr;
+  __half* k_cache = nullptr;        // [kv_heads x capacity x head] (head-major, K rows lane-permuted)
+  __half* v_cache = nullptr;        // [kv_heads x capacity x head]
   const int* pos = nullptr;         // device: KV length before this call
   int splits = 16;                  // partial CTAs per (frame, kv head)
   float* part = nullptr;            // [F x kv_heads x splits x (4 + 2*head)] (split-K mode)
@@ -118,7 +118,7 @@ struct AttnArgs {
   // arithmetic order (bit-identical results); 0: split-K online softmax.
   int exact = 1;
   float* scores = nullptr;          // [F x heads x capacity] (exact mode)
-  int capacity = 0;                 // KV capacity (rows of the caches)
+  int capacity = 0;                 // KV capacity (positions per head in the caches)
 };
 // Cache position of channel c in a K row (lane-permuted layout).
 int k_cache_pos(int c, int head_size);

@@ -80,7 +80,7 @@ struct fa_weight {
   fa_backend* owner = nullptr;
   int rows = 0, cols = 0;
   bool q8 = false;
-  DevBuf q, s, f32;
+  DevBuf q, f32;
   Q8View view;
   F32View fview;
 };
@@ -153,15 +153,14 @@ static void check_backend(fa_backend* b) {
   if (b->disposed) throw Error(kErrDisposed, "backend disposed");
 }
 
-static Q8View make_view(const void* q, const void* s, int rows, int cols, bool f16) {
+static Q8View make_view(const void* base, int rows, int cols, bool f16) {
   Q8View v;
-  v.q = static_cast<const uint8_t*>(q);
-  v.s = s;
+  v.base = static_cast<const uint8_t*>(base);
   v.rows = rows;
   v.cols = cols;
   v.tiles = (rows + kTileRows - 1) / kTileRows;
   v.scale_f16 = f16 ? 1 : 0;
-  v.scale_groups = q8_scale_groups(cols, f16);
+  v.tile_bytes = q8_tile_bytes(cols, f16);
   return v;
 }
 
@@ -226,18 +225,16 @@ int fa_weight_upload_q8(fa_backend* b, const int8_t* q, const float* scales, int
     DeviceGuard g(b->device);
     const size_t nscales = (size_t)rows * (cols / 32);
     const bool f16 = scales_fit_f16(scales, nscales);
-    std::vector<uint8_t> hq(q8_bytes_q(rows, cols)), hs(q8_bytes_s(rows, cols, f16));
-    pack_q8(q, scales, rows, cols, f16, hq.data(), hs.data());
+    std::vector<uint8_t> hq(q8_bytes(rows, cols, f16));
+    pack_q8(q, scales, rows, cols, f16, hq.data());
     auto w = std::make_unique<fa_weight>();
     w->owner = b;
     w->rows = rows;
     w->cols = cols;
     w->q8 = true;
     w->q.ensure(hq.size());
-    w->s.ensure(hs.size());
     FA_CUDA(cudaMemcpy(w->q.p, hq.data(), hq.size(), cudaMemcpyHostToDevice));
-    FA_CUDA(cudaMemcpy(w->s.p, hs.data(), hs.size(), cudaMemcpyHostToDevice));
-    w->view = make_view(w->q.p, w->s.p, rows, cols, f16);
+    w->view = make_view(w->q.p, rows, cols, f16);
     b->weights.insert(w.get());
     *out = w.release();
     return (int)kHandled;
@@ -466,9 +463,10 @@ int fa_op_attention_pair(fa_backend* b, const float* query, const float* keys, c
     // Device buffers: q (f32), k/v caches (f16), partials, attn, pos.
     std::vector<__half> hk((size_t)frames * kvw), hv((size_t)frames * kvw);
     for (size_t i = 0; i < hk.size(); ++i) {
-      const size_t row = i / size, c = i % size;  // K rows in the lane-permuted cache layout
-      hk[row * size + k_cache_pos((int)c, size)] = __float2half_rn(keys[i]);
-      hv[i] = __float2half_rn(values[i]);
+      // head-major cache [kv_head][t][size], K rows lane-permuted
+      const size_t t = i / kvw, h = (i % kvw) / size, c = i % size;
+      hk[(h * frames + t) * size + k_cache_pos((int)c, size)] = __float2half_rn(keys[i]);
+      hv[(h * frames + t) * size + c] = __float2half_rn(values[i]);
     }
     if ((size_t)frames * 4 > 200 * 1024) return (int)kDeclined;
     const size_t part_n = (size_t)kv_heads * kAttnSplits * (4 + 2 * size) + (size_t)2 * kv_heads * frames;
@@ -543,17 +541,17 @@ struct Arena {
   }
 };
 
-// Places tiles of one Q8 tensor into a combined tile-layout matrix:
+// Places the 8-row tiles of one Q8 tensor into a combined tile-layout matrix:
 // source tile i -> destination tile tile_offset + i * tile_step.
-void upload_q8_tensor(const GgufTensor& t, uint8_t* dq, uint8_t* ds, int tile_offset, int tile_step) {
+void upload_q8_tensor(const GgufTensor& t, uint8_t* dst, int tile_offset, int tile_step) {
   const int rows = t.rows(), cols = t.cols();
   if (t.type != kQ8_0) throw Error(kErrIo, t.name + ": expected Q8_0");
-  std::vector<uint8_t> hq(q8_bytes_q(rows, cols)), hs(q8_bytes_s(rows, cols, true));
-  pack_q8_from_gguf(t.data, rows, cols, hq.data(), hs.data());
-  const int tiles = (rows + kTileRows - 1) / kTileRows;
-  const size_t tq = (size_t)kTileRows * cols, ts = (size_t)q8_scale_groups(cols, true) * kTileRows * 16;
-  FA_CUDA(cudaMemcpy2D(dq + (size_t)tile_offset * tq, tq * tile_step, hq.data(), tq, tq, tiles, cudaMemcpyHostToDevice));
-  FA_CUDA(cudaMemcpy2D(ds + (size_t)tile_offset * ts, ts * tile_step, hs.data(), ts, ts, tiles, cudaMemcpyHostToDevice));
+  if (rows % kTileRows != 0) throw Error(kErrIo, t.name + ": rows must be a multiple of 8");
+  std::vector<uint8_t> h(q8_bytes(rows, cols, true));
+  pack_q8_from_gguf(t.data, rows, cols, h.data());
+  const int tiles = rows / kTileRows;
+  const size_t tb = (size_t)q8_tile_bytes(cols, true);
+  FA_CUDA(cudaMemcpy2D(dst + (size_t)tile_offset * tb, tb * tile_step, h.data(), tb, tb, tiles, cudaMemcpyHostToDevice));
 }
 
 std::vector<float> tensor_f32(const GgufTensor& t) {
@@ -611,11 +609,8 @@ int fa_model_load_gguf(fa_backend* b, const char* path, int capacity, fa_model**
 
     // ---- arena plan ----
     Arena ar;
-    struct QSlot { size_t q, s; int rows, cols; };
-    auto qslot = [&](int rows, int cols) {
-      QSlot s{ar.take(q8_bytes_q(rows, cols)), ar.take(q8_bytes_s(rows, cols, true)), rows, cols};
-      return s;
-    };
+    struct QSlot { size_t off; int rows, cols; };
+    auto qslot = [&](int rows, int cols) { return QSlot{ar.take(q8_bytes(rows, cols, true)), rows, cols}; };
     auto fslot = [&](int rows, int cols) { return ar.take((size_t)rows * cols * 4); };
     struct LayerPlan { QSlot qkv, o, gu, down; size_t fqkv, fo, fgu, fdown, an, qn, kn, fn; };
     std::vector<LayerPlan> plan(m->layers);
@@ -671,19 +666,18 @@ int fa_model_load_gguf(fa_backend* b, const char* path, int capacity, fa_model**
           to.rows() != W || tg.rows() != ffn || tu.rows() != ffn || td.cols() != ffn || td.rows() != W)
         throw Error(kErrIo, "layer " + std::to_string(l) + ": unexpected projection shapes");
       if (m->quantized) {
-        uint8_t *q0 = base + P.qkv.q, *s0 = base + P.qkv.s;
-        upload_q8_tensor(tq, q0, s0, 0, 1);
-        upload_q8_tensor(tk, q0, s0, qw / kTileRows, 1);
-        upload_q8_tensor(tv, q0, s0, (qw + kvw) / kTileRows, 1);
-        Ld.qkv = make_view(q0, s0, qw + 2 * kvw, W, true);
-        upload_q8_tensor(to, base + P.o.q, base + P.o.s, 0, 1);
-        Ld.o = make_view(base + P.o.q, base + P.o.s, W, qw, true);
-        upload_q8_tensor(tg, base + P.gu.q, base + P.gu.s, 0, 2);  // gate tile i -> 2i
-        upload_q8_tensor(tu, base + P.gu.q, base + P.gu.s, 1, 2);  // up tile i -> 2i + 1
-        Ld.gateup = make_view(base + P.gu.q, base + P.gu.s, 2 * ffn, W, true);
-        Ld.gateup.rows = ffn;  // epilogue rows per half of the pair
-        upload_q8_tensor(td, base + P.down.q, base + P.down.s, 0, 1);
-        Ld.down = make_view(base + P.down.q, base + P.down.s, W, ffn, true);
+        uint8_t* q0 = base + P.qkv.off;
+        upload_q8_tensor(tq, q0, 0, 1);
+        upload_q8_tensor(tk, q0, qw / kTileRows, 1);
+        upload_q8_tensor(tv, q0, (qw + kvw) / kTileRows, 1);
+        Ld.qkv = make_view(q0, qw + 2 * kvw, W, true);
+        upload_q8_tensor(to, base + P.o.off, 0, 1);
+        Ld.o = make_view(base + P.o.off, W, qw, true);
+        upload_q8_tensor(tg, base + P.gu.off, 0, 2);  // gate tile i -> 2i
+        upload_q8_tensor(tu, base + P.gu.off, 1, 2);  // up tile i -> 2i + 1
+        Ld.gateup = make_view(base + P.gu.off, 2 * ffn, W, true);
+        upload_q8_tensor(td, base + P.down.off, 0, 1);
+        Ld.down = make_view(base + P.down.off, W, ffn, true);
       } else {
         float* qkv0 = reinterpret_cast<float*>(base + P.fqkv);
         upload_f32_rows(tq, qkv0);
@@ -706,16 +700,16 @@ int fa_model_load_gguf(fa_backend* b, const char* path, int capacity, fa_model**
     }
     if (emb.cols() != W) throw Error(kErrIo, "token_embd.weight: unexpected width");
     if (emb_q8) {
-      upload_q8_tensor(emb, base + qemb.q, base + qemb.s, 0, 1);
-      m->embed = make_view(base + qemb.q, base + qemb.s, emb.rows(), W, true);
+      upload_q8_tensor(emb, base + qemb.off, 0, 1);
+      m->embed = make_view(base + qemb.off, emb.rows(), W, true);
     } else {
       upload_f32_rows(emb, reinterpret_cast<float*>(base + femb));
       m->fembed = F32View{reinterpret_cast<float*>(base + femb), emb.rows(), W};
     }
     if (outw) {
       if (outw->type == kQ8_0) {
-        upload_q8_tensor(*outw, base + qlm.q, base + qlm.s, 0, 1);
-        m->lm = make_view(base + qlm.q, base + qlm.s, outw->rows(), W, true);
+        upload_q8_tensor(*outw, base + qlm.off, 0, 1);
+        m->lm = make_view(base + qlm.off, outw->rows(), W, true);
       } else {
         upload_f32_rows(*outw, reinterpret_cast<float*>(base + flm));
         m->flm = F32View{reinterpret_cast<float*>(base + flm), outw->rows(), W};
@@ -724,7 +718,7 @@ int fa_model_load_gguf(fa_backend* b, const char* path, int capacity, fa_model**
       m->lm = m->embed;
       m->flm = m->fembed;
     }
-    if (m->quantized != (m->lm.q != nullptr))
+    if (m->quantized != (m->lm.base != nullptr))
       throw Error(kErrArgument, "mixed Q8/FP32 projection and lm_head types are not supported");
     m->out_norm = norm_up("output_norm.weight", onorm, W);
     // RoPE table exactly as QwenDecoder.cs:78-95 builds it (float pow/cos/sin).
@@ -1329,15 +1323,18 @@ int fa_session_kv(fa_session* s, int layer, float* keys, float* values) {
     fa_model* m = s->m;
     if (layer < 0 || layer >= m->layers || !keys || !values) throw Error(kErrArgument, "invalid layer");
     const size_t kvw = (size_t)m->kv_heads * m->head_size, n = (size_t)s->pos * kvw;
-    std::vector<__half> hk(n), hv(n);
-    const size_t off = (size_t)layer * m->capacity * kvw;
-    FA_CUDA(cudaMemcpy(hk.data(), s->k_cache.as<__half>() + off, n * 2, cudaMemcpyDeviceToHost));
-    FA_CUDA(cudaMemcpy(hv.data(), s->v_cache.as<__half>() + off, n * 2, cudaMemcpyDeviceToHost));
-    const size_t D = m->head_size;
-    for (size_t i = 0; i < n; ++i) {
-      keys[i] = __half2float(hk[(i / D) * D + k_cache_pos((int)(i % D), (int)D)]);
-      values[i] = __half2float(hv[i]);
+    const size_t per_layer = (size_t)m->capacity * kvw;
+    std::vector<__half> hk(per_layer), hv(per_layer);
+    const size_t off = (size_t)layer * per_layer;
+    FA_CUDA(cudaMemcpy(hk.data(), s->k_cache.as<__half>() + off, per_layer * 2, cudaMemcpyDeviceToHost));
+    FA_CUDA(cudaMemcpy(hv.data(), s->v_cache.as<__half>() + off, per_layer * 2, cudaMemcpyDeviceToHost));
+    const size_t D = m->head_size, P = s->pos, cap = m->capacity;
+    for (size_t i = 0; i < n; ++i) {  // head-major [kv_head][capacity][D] -> [t][kv_width]
+      const size_t t = i / kvw, h = (i % kvw) / D, c = i % D;
+      keys[i] = __half2float(hk[(h * cap + t) * D + k_cache_pos((int)c, (int)D)]);
+      values[i] = __half2float(hv[(h * cap + t) * D + c]);
     }
+    (void)P;
     return (int)kHandled;
   });
 }
