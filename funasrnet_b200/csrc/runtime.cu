@@ -6,6 +6,8 @@
 
 #include <algorithm>
 #include <cmath>
+#include <cstddef>
+#include <cstdlib>
 #include <cstring>
 #include <memory>
 #include <mutex>
@@ -17,6 +19,7 @@
 #include "fa_common.h"
 #include "gguf.h"
 #include "kernels.h"
+#include "mega.h"
 
 using namespace fa;
 
@@ -117,6 +120,8 @@ struct fa_model {
   const float* rope_sin = nullptr;
   int64_t weight_bytes = 0;
   int sessions = 0;
+  bool mega_ok = false;   // shape the persistent decode kernel is built for
+  DevBuf mega_layers;     // MegaLayer[layers] on the device
 };
 
 struct fa_session {
@@ -143,6 +148,10 @@ struct fa_session {
   bool debug = false;                        // keep layer-0 intermediates of decode calls
   int dbg_frames = 0;
   DevBuf dbg_q, dbg_attn, dbg_a, dbg_act, dbg_x;
+  // persistent decode kernel state
+  bool use_mega = false;
+  int mega_grid = 0;
+  DevBuf mx, mqkv, mattn, ma, mact, mpv, mpi, mctrl;
   int* d_int(int i) const { return ints.as<int>() + i; }
 };
 
@@ -721,6 +730,21 @@ int fa_model_load_gguf(fa_backend* b, const char* path, int capacity, fa_model**
     if (m->quantized != (m->lm.base != nullptr))
       throw Error(kErrArgument, "mixed Q8/FP32 projection and lm_head types are not supported");
     m->out_norm = norm_up("output_norm.weight", onorm, W);
+    // The persistent decode kernel covers the Qwen3-0.6B shape with Q8 weights.
+    m->mega_ok = m->quantized && W == kMegaWidth && m->heads == kMegaHeads && m->kv_heads == kMegaKvHeads &&
+                 D == kMegaHead && ffn == kMegaFfn && m->vocab % 8 == 0 && m->embed.base != nullptr &&
+                 m->embed.rows == m->vocab && m->capacity <= 8192 &&
+                 m->lm.base != nullptr && m->embed.scale_f16 && m->lm.scale_f16;
+    if (m->mega_ok) {
+      std::vector<MegaLayer> ml(m->layers);
+      for (int l = 0; l < m->layers; ++l) {
+        const LayerDev& Ld = m->L[l];
+        ml[l] = MegaLayer{Ld.qkv.base, Ld.o.base,       Ld.gateup.base, Ld.down.base,
+                          Ld.attn_norm, Ld.q_norm, Ld.k_norm, Ld.ffn_norm};
+      }
+      m->mega_layers.ensure(ml.size() * sizeof(MegaLayer));
+      FA_CUDA(cudaMemcpy(m->mega_layers.p, ml.data(), ml.size() * sizeof(MegaLayer), cudaMemcpyHostToDevice));
+    }
     // RoPE table exactly as QwenDecoder.cs:78-95 builds it (float pow/cos/sin).
     {
       const int half = D / 2;
@@ -1094,6 +1118,27 @@ int fa_session_create(fa_model* m, fa_session** out) {
     FA_CUDA(cudaEventCreate(&s->ev0));
     FA_CUDA(cudaEventCreate(&s->ev1));
     FA_CUDA(cudaMallocHost(&s->pinned, 64 * 4));
+    // Persistent decode kernel: one CTA per SM; opt out with FUNASR_CUDA_MEGA=0.
+    const char* env = std::getenv("FUNASR_CUDA_MEGA");
+    if (m->mega_ok && !(env && env[0] == '0')) {
+      s->mega_grid = mega_grid(s->device, m->capacity);
+      if (s->mega_grid > 0) {
+        s->mx.ensure((size_t)W * 8);
+        s->mqkv.ensure((size_t)(qw + 2 * kvw) * 8);
+        s->mattn.ensure((size_t)qw * 8);
+        s->ma.ensure((size_t)W * 8);
+        s->mact.ensure((size_t)m->ffn * 8);
+        s->mpv.ensure((size_t)s->mega_grid * 8);
+        s->mpi.ensure((size_t)s->mega_grid * 8);
+        s->mctrl.ensure(sizeof(MegaCtrl));
+        for (DevBuf* b : {&s->mx, &s->mqkv, &s->mattn, &s->ma, &s->mact, &s->mpv, &s->mpi})
+          FA_CUDA(cudaMemset(b->p, 0, b->bytes));  // tag 0 is never a valid tag
+        MegaCtrl c{};
+        c.epoch = 1;
+        FA_CUDA(cudaMemcpy(s->mctrl.p, &c, sizeof(c), cudaMemcpyHostToDevice));
+        s->use_mega = true;
+      }
+    }
     m->sessions++;
     *out = s.release();
     return (int)kHandled;
@@ -1190,11 +1235,78 @@ int fa_session_decode(fa_session* s, const float* embeddings, int frames, int ou
   });
 }
 
+// One persistent-kernel launch of `steps` decode steps (mega.cu).  The first
+// token is the host's (host_token >= 0) or the device argmax of the last
+// decode.  Returns the control block after the launch.
+static MegaCtrl run_mega(fa_session* s, int steps, int record, int n_end, int host_token, bool want_logits) {
+  fa_model* m = s->m;
+  MegaArgs a;
+  a.layers = s->m->mega_layers.as<MegaLayer>();
+  a.n_layers = m->layers;
+  a.lm = m->lm.base;
+  a.vocab = m->vocab;
+  a.emb = m->embed.base;
+  a.emb_rows = m->embed.rows;
+  a.out_norm = m->out_norm;
+  a.rope_cos = m->rope_cos;
+  a.rope_sin = m->rope_sin;
+  a.k_cache = s->k_cache.as<__half>();
+  a.v_cache = s->v_cache.as<__half>();
+  a.capacity = m->capacity;
+  a.eps = m->eps;
+  a.x_t = s->mx.as<unsigned long long>();
+  a.qkv_t = s->mqkv.as<unsigned long long>();
+  a.attn_t = s->mattn.as<unsigned long long>();
+  a.a_t = s->ma.as<unsigned long long>();
+  a.act_t = s->mact.as<unsigned long long>();
+  a.part_v = s->mpv.as<unsigned long long>();
+  a.part_i = s->mpi.as<unsigned long long>();
+  a.logits = want_logits ? s->logits.as<float>() : nullptr;
+  a.ctrl = s->mctrl.as<MegaCtrl>();
+  a.max_steps = steps;
+  a.record = record;
+  a.end_ids = s->end_ids.as<int>();
+  a.n_end = n_end;
+  a.log = s->log.as<int>();
+  a.log_cap = s->log_cap;
+  // control block: pos, token (host or last device argmax), counters cleared
+  s->pinned[8] = s->pos;
+  s->pinned[9] = host_token;
+  s->pinned[10] = 0;
+  s->pinned[11] = 0;
+  char* ctrl = static_cast<char*>(s->mctrl.p);
+  FA_CUDA(cudaMemcpyAsync(ctrl, s->pinned + 8, 16, cudaMemcpyHostToDevice, s->stream));
+  if (host_token < 0) FA_CUDA(cudaMemcpyAsync(ctrl + 4, s->d_int(1), 4, cudaMemcpyDeviceToDevice, s->stream));
+  FA_CUDA(cudaMemsetAsync(ctrl + offsetof(MegaCtrl, error), 0, 8, s->stream));
+  FA_CUDA(cudaEventRecord(s->ev0, s->stream));
+  launch_mega(a, s->mega_grid, s->stream);
+  FA_CUDA(cudaEventRecord(s->ev1, s->stream));
+  // keep the graph path's device words in step: pos, token
+  FA_CUDA(cudaMemcpyAsync(s->d_int(0), ctrl + offsetof(MegaCtrl, pos), 4, cudaMemcpyDeviceToDevice, s->stream));
+  FA_CUDA(cudaMemcpyAsync(s->d_int(1), ctrl + offsetof(MegaCtrl, token), 4, cudaMemcpyDeviceToDevice, s->stream));
+  FA_CUDA(cudaMemcpyAsync(s->pinned + 16, ctrl, sizeof(MegaCtrl), cudaMemcpyDeviceToHost, s->stream));
+  FA_CUDA(cudaStreamSynchronize(s->stream));
+  FA_CUDA(cudaEventElapsedTime(&s->last_ms, s->ev0, s->ev1));
+  MegaCtrl c;
+  std::memcpy(&c, s->pinned + 16, sizeof(c));
+  if (c.error != 0)
+    throw Error(kErrTimeout, "persistent decode kernel: a bounded wait gave up (code " + std::to_string(c.error) + ")");
+  s->pos = c.pos;
+  return c;
+}
+
 int fa_session_step(fa_session* s, int32_t token, float* logits, int32_t* next) {
   return with_session(s, [&] {
     fa_model* m = s->m;
     check_tokens(s, &token, 1);
     if (s->pos + 1 > m->capacity) throw Error(kErrArgument, "Decoder context exhausted or invalid embeddings");
+    if (s->use_mega && s->exact_attention) {
+      const MegaCtrl c = run_mega(s, 1, 0, 0, token, logits != nullptr);
+      if (logits) FA_CUDA(cudaMemcpy(logits, s->logits.p, (size_t)m->vocab * 4, cudaMemcpyDeviceToHost));
+      s->have_token = true;
+      if (next) *next = c.token;
+      return (int)kHandled;
+    }
     if (!s->step_graph) s->step_graph = capture(s, false, 0);
     s->pinned[0] = token;
     FA_CUDA(cudaMemcpyAsync(s->d_int(1), s->pinned, 4, cudaMemcpyHostToDevice, s->stream));
@@ -1221,6 +1333,18 @@ int fa_session_generate(fa_session* s, int max_tokens, const int32_t* end_ids, i
     if (max_tokens == 0) return (int)kHandled;
     const int steps = std::min(max_tokens, m->capacity - s->pos);
     if (n_end > 0) FA_CUDA(cudaMemcpyAsync(s->end_ids.p, end_ids, (size_t)n_end * 4, cudaMemcpyHostToDevice, s->stream));
+    if (s->use_mega && s->exact_attention) {
+      const MegaCtrl c = run_mega(s, steps, 1, n_end, -1, false);
+      const int count = c.log_count;
+      if (count > 0) FA_CUDA(cudaMemcpy(tokens, s->log.p, (size_t)count * 4, cudaMemcpyDeviceToHost));
+      *n_out = count;
+      if (!c.stopped && max_tokens > steps) {
+        bool is_end = false;
+        for (int i = 0; i < n_end; ++i) is_end |= end_ids[i] == c.token;
+        if (!is_end) throw Error(kErrCapacity, "Decoder context exhausted or invalid embeddings");
+      }
+      return (int)kHandled;
+    }
     if (!s->gen_graph || s->n_end_graph != n_end) {
       if (s->gen_graph) cudaGraphExecDestroy(s->gen_graph);
       s->gen_graph = nullptr;
@@ -1279,7 +1403,22 @@ int fa_session_restore_prefix(fa_session* s) {
   });
 }
 
-int fa_session_kernels_per_step(const fa_session* s) { return s ? s->gen_kernels : -1; }
+int fa_session_kernels_per_step(const fa_session* s) {
+  if (!s) return -1;
+  return (s->use_mega && s->exact_attention) ? 0 : s->gen_kernels;
+}
+
+int fa_session_uses_persistent_kernel(const fa_session* s) {
+  return s ? ((s->use_mega && s->exact_attention) ? s->mega_grid : 0) : -1;
+}
+
+int fa_session_set_persistent_kernel(fa_session* s, int on) {
+  return with_session(s, [&] {
+    if (on && s->mega_grid <= 0) return (int)kDeclined;
+    s->use_mega = on != 0;
+    return (int)kHandled;
+  });
+}
 
 int fa_session_set_debug(fa_session* s, int on) {
   return with_session(s, [&] {

@@ -126,6 +126,13 @@ class QwenDecoder:
         check(lib().fa_session_debug_layer0(self._h, name.encode(), ptr(out)))
         return out
 
+    def persistent_grid(self) -> int:
+        """CTAs of the persistent decode kernel (0: CUDA-graph step path)."""
+        return int(lib().fa_session_uses_persistent_kernel(self._h))
+
+    def set_persistent(self, on: bool = True) -> bool:
+        return check(lib().fa_session_set_persistent_kernel(self._h, 1 if on else 0)) == FA_OK
+
     def kernels_per_step(self) -> int:
         return int(lib().fa_session_kernels_per_step(self._h))
 

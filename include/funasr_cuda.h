@@ -175,6 +175,14 @@ int fa_session_debug_layer0(fa_session* session, const char* name, float* out);
  * logits bit-identical to the CPU decoder; 0 selects split-K online softmax,
  * faster at long contexts but reassociated (outside the reference's order). */
 int fa_session_set_exact_attention(fa_session* session, int on);
+/* Decode steps (fa_session_step / fa_session_generate) run as one persistent
+ * cooperative kernel per call (one CTA per SM, TMA-streamed weights) when the
+ * model has the Qwen3-0.6B Q8 shape; returns its grid size, 0 when the
+ * CUDA-graph path is used.  FUNASR_CUDA_MEGA=0 disables it at session creation. */
+int fa_session_uses_persistent_kernel(const fa_session* session);
+/* Selects the persistent kernel (1) or the CUDA-graph step (0); FA_DECLINED when
+ * the persistent kernel is unavailable for this model or device. */
+int fa_session_set_persistent_kernel(fa_session* session, int on);
 /* Number of kernel launches one generate iteration replays (kernel nodes of
  * its CUDA graph); 0 before the first fa_session_generate. */
 int fa_session_kernels_per_step(const fa_session* session);
