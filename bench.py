@@ -210,6 +210,7 @@ def main():
 
     from funasrnet_b200.backend import CudaFloatBackend
     from funasrnet_b200.decoder import CudaModel, QwenDecoder
+    from funasrnet_b200.shard import max_over_ranks
 
     path = ensure_model(quantized, rank, barrier)
     be = CudaFloatBackend(local)
@@ -229,12 +230,7 @@ def main():
         toks = dec.generate(steps, end_ids=())
     dev_ms = dec.last_generate_ms()
     assert len(toks) == steps
-    if dist is not None:
-        import torch
-
-        t = torch.tensor([dev_ms], dtype=torch.float64, device=f"cuda:{local}")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        dev_ms = float(t.item())
+    dev_ms = max_over_ranks(dev_ms, dist, f"cuda:{local}")
 
     # e2e: the same K steps through the public per-token API with host buffers
     # (FunAsr.Transcribe's loop: H2D token id, D2H next token id each step).
@@ -245,12 +241,7 @@ def main():
     for _ in range(steps):
         tok, _ = dec.step(tok)
     e2e_s = time.perf_counter() - t0
-    if dist is not None:
-        import torch
-
-        t = torch.tensor([e2e_s], dtype=torch.float64, device=f"cuda:{local}")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_s = float(t.item())
+    e2e_s = max_over_ranks(e2e_s, dist, f"cuda:{local}")
 
     # roofline of the decode step and of its largest single launch (lm_head GEMV)
     peak, peak_kind = measured_peak_hbm()
@@ -262,6 +253,10 @@ def main():
     lm_ms = dec.time_lm_head(20) if quantized else None
     lm_bytes = cm.vocab * cm.width // 32 * 34 + cm.width * 4 * 2
 
+    grid = dec.persistent_grid()
+    kernel_name = (f"decode_mega_kernel (persistent, {grid} CTAs, one launch for all {steps} steps)" if grid
+                   else "decode step (CUDA graph)")
+    launches = 1 if grid else dec.kernels_per_step() * steps
     line = {
         "metric": metric,
         "value": world * steps / (dev_ms * 1e-3),
@@ -278,10 +273,10 @@ def main():
         "config": config,
         "e2e": {"value": world * steps / e2e_s, "unit": "tokens/s", "h2d_bytes_per_step": 4,
                 "d2h_bytes_per_step": 4},
-        "roofline": {"bound": "hbm", "kernel": "decode step (CUDA graph)", "achieved": achieved, "peak": peak,
+        "roofline": {"bound": "hbm", "kernel": kernel_name, "achieved": achieved, "peak": peak,
                      "unit": "GB/s", "frac": achieved / peak, "traffic": None,
                      "bytes_per_step": step_bytes, "peak_source": peak_kind},
-        "gpu_launches": dec.kernels_per_step() * steps,
+        "gpu_launches": launches,
         "clocks": clocks.summary(),
     }
     if lm_ms:

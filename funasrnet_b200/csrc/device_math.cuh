@@ -78,7 +78,11 @@ __device__ __forceinline__ float silu_mul1(float g, float u) {
 
 // 1 / sqrt((float)(sumsq / width) + eps)  (TensorMath.Elementwise.cs:78)
 __device__ __forceinline__ float rms_inverse(double sumsq, int width, float eps) {
-  float ms = __double2float_rn(__ddiv_rn(sumsq, (double)width));
+  // sumsq / width: for a power-of-two width the product with the exact
+  // reciprocal is the same correctly rounded value as the division.
+  const double mean = (width & (width - 1)) == 0 ? __dmul_rn(sumsq, 1.0 / (double)width)
+                                                 : __ddiv_rn(sumsq, (double)width);
+  float ms = __double2float_rn(mean);
   return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(ms, eps)));
 }
 

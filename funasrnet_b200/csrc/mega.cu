@@ -1,28 +1,35 @@
 // Persistent decode kernel: whole greedy decode steps of the Qwen3-0.6B Q8
 // decoder in one cooperative launch (one CTA per SM).
 //
-// Per CTA: warp 15 is a TMA producer that streams the CTA's static share of
-// every projection (contiguous runs of 8-row weight tiles) through a 6-slot
-// shared-memory ring with cp.async.bulk + mbarriers, running ahead of the
-// compute across phases and layers; warps 0..14 compute.
+// Roles.  CTAs 0..15 are attention CTAs (one per query head); the others are
+// GEMV CTAs.  In every CTA, warp 15 is a TMA producer (one elected lane) that
+// streams data into shared-memory rings with cp.async.bulk + mbarriers and
+// runs ahead of the compute; warps 0..14 compute.
+//   GEMV CTAs stream their static share of every projection: contiguous runs
+//   of 8-row weight tiles, through a 6-slot ring, phase after phase, layer
+//   after layer, then their share of the lm_head.
+//   Attention CTAs stream their KV head's history: K in chunks of 60
+//   positions through a 6-slot ring, V through a 4-slot ring, issued as soon
+//   as a layer starts (the history does not depend on the current token).
 //
 // Phases of one step (QwenDecoder.Decode, QwenDecoder.cs:180-268):
-//   embed (every CTA computes the token's row itself)
-//   per layer: Q  (RMSNorm + quantise x, q/k/v GEMV)            all CTAs
-//              A  (QK-norm, RoPE, F16 KV, exact attention)     CTAs 0..15, one per query head
-//              O  (quantise attn, o GEMV + residual)           CTAs 16..
-//              GU (RMSNorm + quantise a, gate/up GEMV, SiLU*up) all CTAs
-//              D  (quantise act, down GEMV + residual)         all CTAs
-//   LM (final RMSNorm, lm_head GEMV, argmax; every CTA reduces all partials)
+//   embed (each GEMV CTA computes the token's row itself)
+//   per layer: Q  RMSNorm + quantise x, q/k/v rows                  GEMV CTAs
+//              A  QK-norm, RoPE, F16 KV write, exact attention       attention CTAs
+//              O  quantise attention output, o rows + residual       GEMV CTAs
+//              GU RMSNorm + quantise a, gate/up rows, SiLU*up        GEMV CTAs
+//              D  quantise act, down rows + residual                 GEMV CTAs
+//   LM final RMSNorm, lm_head rows, argmax; every CTA reduces all partials,
+//      so each knows the next token without another round trip.
 //
-// Cross-CTA activations are 64-bit words (tag << 32 | float bits): a reader
-// spins on the word itself until its tag is the expected one, so one L2 read
-// is both the synchronisation and the data (single-copy atomic 64-bit
-// accesses).  Tags are unique per (step, layer, buffer).  The only other data
-// crossing CTAs, the KV cache, is ordered by a release/acquire fence pair at
-// the step boundary (the argmax partial exchange).  Every wait is bounded: on
-// timeout the kernel records an error code in the control block, drains its
-// in-flight copies and returns.
+// Synchronisation.  Activations crossing CTAs are 64-bit words
+// (tag << 32 | float bits); a reader spins on the word until its tag is the
+// expected one, so one L2 read is both the wait and the data (aligned 64-bit
+// accesses are single-copy atomic).  Tags are unique per (step, layer,
+// buffer).  The KV cache, the only other data crossing CTAs, is ordered by a
+// release/acquire fence pair at the step boundary (the argmax exchange).
+// Every wait is bounded: on timeout the kernel records an error code in the
+// control block, drains its in-flight copies and returns.
 //
 // Arithmetic is the reference's, bit for bit, as in decoder_kernels.cu.
 #include <cuda_fp16.h>
@@ -45,26 +52,29 @@ constexpr int KVW = KH * D;              // 1024
 constexpr int QKV = QW + 2 * KVW;        // 4096
 constexpr int CWARPS = 15;               // compute warps
 constexpr int CTHREADS = CWARPS * 32;    // 480
-constexpr int NSLOT = 6;
 constexpr int TB_W = 8 * W + (W / 32) * 16;      // 8704: tile bytes, K = 1024
 constexpr int TB_Q = 8 * QW + (QW / 32) * 16;    // 17408: K = 2048
 constexpr int TB_F = 8 * FFN + (FFN / 32) * 16;  // 26112: K = 3072
-constexpr int SLOT = TB_F;                       // = 3 K=1024 tiles = 1.5 K=2048 tiles
+constexpr int WSLOTS = 6, WSLOT = TB_F;          // weight ring: 3 K=1024 tiles or 1 K=3072 tile per slot
+constexpr int CHUNK = 60;                        // KV positions per attention chunk (8 threads each)
+constexpr int CSLOT = CHUNK * D * 2;             // 15360 bytes
+constexpr int KSLOTS = 6, VSLOTS = 4;
 constexpr int ATT_CTAS = H;
 constexpr int PROD_FLOATS = 2048;
 constexpr unsigned kWaitLimit = 1u << 22;
+
+static_assert(KSLOTS * CSLOT + VSLOTS * CSLOT <= WSLOTS * WSLOT, "KV rings share the weight ring's memory");
 
 enum { kTagQkv = 1, kTagAttn = 2, kTagA = 3, kTagAct = 4, kTagX = 5, kTagPart = 6 };
 enum { kErrWaitData = 1, kErrWaitFull = 2, kErrWaitEmpty = 3, kErrWaitGo = 4, kErrWaitDrain = 5 };
 
 struct Shared {
-  volatile int quit;       // consumers stop the producer
-  volatile int go;         // steps the consumers have committed to
-  volatile int issued;     // pieces issued by the producer
-  volatile int prod_exit;  // producer left its loop
-  volatile int abort;      // a wait failed somewhere: drain and return
+  volatile int quit;        // consumers stop the producer
+  volatile int go;          // steps the consumers have committed to
+  volatile int issued[3];   // copies issued per ring (weights / K / V)
+  volatile int prod_exit;   // producer left its loop
+  volatile int abort;       // a wait failed somewhere: drain and return
   int token;
-  int stopped;
   float best_v[32];
   int best_i[32];
 };
@@ -82,8 +92,8 @@ __host__ __device__ inline Layout layout(int capacity) {
     o += bytes;
     return at;
   };
-  L.ring = take(NSLOT * SLOT, 128);
-  L.bars = take(2 * NSLOT * 8, 8);
+  L.ring = take(WSLOTS * WSLOT, 128);
+  L.bars = take(32 * 8, 8);
   L.xq = take(FFN, 16);
   L.xs = take(FFN / 32 * 4, 16);
   L.xres = take(W * 4, 16);
@@ -129,9 +139,6 @@ __device__ __forceinline__ void bulk_load(void* dst, const void* src, unsigned b
                "l"(src), "r"(bytes), "r"(saddr(bar))
                : "memory");
 }
-__device__ __forceinline__ void prefetch_l2(const void* src, unsigned bytes) {
-  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
-}
 __device__ __forceinline__ unsigned long long ld_word(const unsigned long long* p) {
   unsigned long long v;
   asm volatile("ld.relaxed.gpu.global.b64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
@@ -150,6 +157,12 @@ __device__ __forceinline__ unsigned long long pack(float v, unsigned tag) {
 }
 __device__ __forceinline__ void csync() { asm volatile("bar.sync 1, 480;" ::: "memory"); }
 
+__device__ __forceinline__ unsigned long long global_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
+
 __device__ __forceinline__ void raise_error(Shared* sh, MegaCtrl* ctrl, int code) {
   atomicCAS(&ctrl->error, 0, code);
   sh->abort = 1;
@@ -163,8 +176,8 @@ __device__ bool wait_word(const unsigned long long* p, unsigned tag, float& out,
       out = __uint_as_float((unsigned)v);
       return true;
     }
-    if (it >= 8) __nanosleep(it < 2048 ? 32 : 256);
-    if ((it & 255) == 255) {
+    if (it >= 4096) __nanosleep(128);  // spin first: the hop latency is the critical path
+    if ((it & 1023) == 1023) {
       if (sh->abort || ld_flag(&ctrl->error)) {
         sh->abort = 1;
         return false;
@@ -177,52 +190,39 @@ __device__ bool wait_word(const unsigned long long* p, unsigned tag, float& out,
   }
 }
 
-__device__ bool wait_full(uint64_t* bar, unsigned parity, Shared* sh, MegaCtrl* ctrl) {
-  for (unsigned it = 0;; ++it) {
-    if (mbar_try_wait(bar, parity)) return true;
-    if ((it & 63) == 63) {
-      if (sh->abort) return false;
-      if (it > kWaitLimit) {
-        raise_error(sh, ctrl, kErrWaitFull);
-        return false;
-      }
-    }
-  }
-}
-
 __device__ __forceinline__ void split(int total, int parts, int part, int& first, int& n) {
   first = (int)((long long)part * total / parts);
   n = (int)((long long)(part + 1) * total / parts) - first;
 }
 
-// Phase spans of CTA `cta` in units of tiles (GU: tile pairs).
+// GEMV spans of GEMV CTA `g` (0-based among GEMV CTAs) in tiles (GU: pairs).
 struct Spans {
   int q0, qn, o0, on, gu0, gun, d0, dn, lm0, lmn;
 };
-__device__ Spans spans(int cta, int grid, int lm_tiles) {
+__device__ Spans spans(int g, int n, int lm_tiles) {
   Spans s;
-  split(QKV / 8, grid, cta, s.q0, s.qn);
-  if (cta >= ATT_CTAS) split(W / 8, grid - ATT_CTAS, cta - ATT_CTAS, s.o0, s.on);
-  else s.o0 = s.on = 0;
-  split(FFN / 8, grid, cta, s.gu0, s.gun);
-  split(W / 8, grid, cta, s.d0, s.dn);
-  split(lm_tiles, grid, cta, s.lm0, s.lmn);
+  split(QKV / 8, n, g, s.q0, s.qn);
+  split(W / 8, n, g, s.o0, s.on);
+  split(FFN / 8, n, g, s.gu0, s.gun);
+  split(W / 8, n, g, s.d0, s.dn);
+  split(lm_tiles, n, g, s.lm0, s.lmn);
   return s;
 }
 
-// ------------------------------------------------------- producer ----
+// --------------------------------------------------------------- rings ----
 
 struct Ring {
   uint8_t* base;
   uint64_t* full;
   uint64_t* empty;
+  int nslot, slot_bytes, id;
 };
 
-// Issues one piece (a run of whole tiles) into the next ring slot.
-__device__ bool issue(const Ring& r, int& gp, const uint8_t* src, unsigned bytes, Shared* sh, MegaCtrl* ctrl) {
-  const int slot = gp % NSLOT;
-  if (gp >= NSLOT) {
-    const unsigned parity = (unsigned)((gp / NSLOT - 1) & 1);
+// Producer side: copies `bytes` from `src` into the ring's next slot.
+__device__ bool ring_issue(const Ring& r, int& n, const void* src, unsigned bytes, Shared* sh, MegaCtrl* ctrl) {
+  const int slot = n % r.nslot;
+  if (n >= r.nslot) {
+    const unsigned parity = (unsigned)((n / r.nslot - 1) & 1);
     for (unsigned it = 0;; ++it) {
       if (mbar_try_wait(&r.empty[slot], parity)) break;
       if ((it & 63) == 63) {
@@ -236,61 +236,125 @@ __device__ bool issue(const Ring& r, int& gp, const uint8_t* src, unsigned bytes
   }
   if (sh->abort) return false;
   mbar_expect_tx(&r.full[slot], bytes);
-  bulk_load(r.base + (size_t)slot * SLOT, src, bytes, &r.full[slot]);
-  ++gp;
-  sh->issued = gp;
+  bulk_load(r.base + (size_t)slot * r.slot_bytes, src, bytes, &r.full[slot]);
+  ++n;
+  sh->issued[r.id] = n;
   return true;
 }
 
-__device__ void producer(const MegaArgs& A, const Ring& r, Shared* sh, int pos0) {
-  const Spans sp = spans(blockIdx.x, gridDim.x, A.vocab / 8);
-  int gp = 0;
-  for (int step = 0; step < A.max_steps; ++step) {
-    for (unsigned it = 0;; ++it) {  // wait until the consumers commit to this step
-      if (sh->quit || sh->abort) goto done;
-      if (sh->go > step) break;
-      __nanosleep(64);
+// Consumer side (whole warps): waits for the ring's next slot.  The result is
+// warp-uniform, so the release's __syncwarp is reached by every lane.
+__device__ const uint8_t* ring_acquire(const Ring& r, int n, Shared* sh, MegaCtrl* ctrl) {
+  const int slot = n % r.nslot;
+  const unsigned parity = (unsigned)((n / r.nslot) & 1);
+  bool ok = false;
+  for (unsigned it = 0;; ++it) {
+    if (mbar_try_wait(&r.full[slot], parity)) {
+      ok = true;
+      break;
+    }
+    if ((it & 63) == 63) {
+      if (sh->abort) break;
       if (it > kWaitLimit) {
-        raise_error(sh, A.ctrl, kErrWaitGo);
-        goto done;
+        raise_error(sh, ctrl, kErrWaitFull);
+        break;
       }
-    }
-    for (int l = 0; l < A.n_layers; ++l) {
-      const MegaLayer& Lw = A.layers[l];
-      if (blockIdx.x < ATT_CTAS) {  // warm L2 with this head's K/V history
-        const int g = blockIdx.x / 2, pos = pos0 + step;
-        if (pos > 0) {
-          const size_t off = (((size_t)l * KH + g) * A.capacity) * D;
-          prefetch_l2(A.k_cache + off, (unsigned)pos * D * 2);
-          prefetch_l2(A.v_cache + off, (unsigned)pos * D * 2);
-        }
-      }
-      for (int t = 0; t < sp.qn; t += 3) {
-        const int n = min(3, sp.qn - t);
-        if (!issue(r, gp, Lw.qkv + (size_t)(sp.q0 + t) * TB_W, n * TB_W, sh, A.ctrl)) goto done;
-      }
-      for (int t = 0; t < sp.on; ++t)
-        if (!issue(r, gp, Lw.o + (size_t)(sp.o0 + t) * TB_Q, TB_Q, sh, A.ctrl)) goto done;
-      for (int t = 0; t < sp.gun; ++t)
-        if (!issue(r, gp, Lw.gu + (size_t)(sp.gu0 + t) * 2 * TB_W, 2 * TB_W, sh, A.ctrl)) goto done;
-      for (int t = 0; t < sp.dn; ++t)
-        if (!issue(r, gp, Lw.down + (size_t)(sp.d0 + t) * TB_F, TB_F, sh, A.ctrl)) goto done;
-    }
-    for (int t = 0; t < sp.lmn; t += 3) {
-      const int n = min(3, sp.lmn - t);
-      if (!issue(r, gp, A.lm + (size_t)(sp.lm0 + t) * TB_W, n * TB_W, sh, A.ctrl)) goto done;
     }
   }
-done:
-  sh->prod_exit = 1;
+  if (!__all_sync(0xffffffffu, ok)) return nullptr;
+  return r.base + (size_t)slot * r.slot_bytes;
+}
+__device__ __forceinline__ void ring_release(const Ring& r, int n, int lane) {
+  __syncwarp();
+  if (lane == 0) mbar_arrive(&r.empty[n % r.nslot]);
 }
 
-// ------------------------------------------------------- consumers ----
+// Waits (bounded) for every copy a ring issued to land: no TMA write may be in
+// flight when the CTA exits.
+__device__ void ring_drain(const Ring& r, int consumed, int issued, Shared* sh, MegaCtrl* ctrl) {
+  for (int n = consumed; n < issued; ++n) {
+    const int slot = n % r.nslot;
+    const unsigned parity = (unsigned)((n / r.nslot) & 1);
+    for (unsigned it = 0; !mbar_try_wait(&r.full[slot], parity); ++it)
+      if (it > kWaitLimit) {
+        raise_error(sh, ctrl, kErrWaitDrain);
+        return;
+      }
+  }
+}
+
+// ------------------------------------------------------------ producer ----
+
+__device__ bool wait_go(Shared* sh, MegaCtrl* ctrl, int step) {
+  for (unsigned it = 0;; ++it) {
+    if (sh->quit || sh->abort) return false;
+    if (sh->go > step) return true;
+    __nanosleep(64);
+    if (it > kWaitLimit) {
+      raise_error(sh, ctrl, kErrWaitGo);
+      return false;
+    }
+  }
+}
+
+__device__ void producer_gemv(const MegaArgs& A, const Ring& r, Shared* sh) {
+  const int n_gemv = gridDim.x - ATT_CTAS;
+  const Spans sp = spans(blockIdx.x - ATT_CTAS, n_gemv, A.vocab / 8);
+  int n = 0;
+  for (int step = 0; step < A.max_steps; ++step) {
+    if (!wait_go(sh, A.ctrl, step)) return;
+    for (int l = 0; l < A.n_layers; ++l) {
+      const MegaLayer& Lw = A.layers[l];
+      for (int t = 0; t < sp.qn; t += 3)
+        if (!ring_issue(r, n, Lw.qkv + (size_t)(sp.q0 + t) * TB_W, min(3, sp.qn - t) * TB_W, sh, A.ctrl)) return;
+      for (int t = 0; t < sp.on; ++t)
+        if (!ring_issue(r, n, Lw.o + (size_t)(sp.o0 + t) * TB_Q, TB_Q, sh, A.ctrl)) return;
+      for (int t = 0; t < sp.gun; ++t)
+        if (!ring_issue(r, n, Lw.gu + (size_t)(sp.gu0 + t) * 2 * TB_W, 2 * TB_W, sh, A.ctrl)) return;
+      for (int t = 0; t < sp.dn; ++t)
+        if (!ring_issue(r, n, Lw.down + (size_t)(sp.d0 + t) * TB_F, TB_F, sh, A.ctrl)) return;
+    }
+    for (int t = 0; t < sp.lmn; t += 3)
+      if (!ring_issue(r, n, A.lm + (size_t)(sp.lm0 + t) * TB_W, min(3, sp.lmn - t) * TB_W, sh, A.ctrl)) return;
+  }
+}
+
+// K/V history of this CTA's KV head, positions [0, pos), per layer: the first
+// K chunks, the first V chunks, then the rest of each as slots free up.
+__device__ void producer_attention(const MegaArgs& A, const Ring& kr, const Ring& vr, Shared* sh, int pos0) {
+  const int g = blockIdx.x >> 1;
+  int nk = 0, nv = 0;
+  for (int step = 0; step < A.max_steps; ++step) {
+    if (!wait_go(sh, A.ctrl, step)) return;
+    // The rows come from generic-proxy stores of earlier steps (ordered by the
+    // step boundary's fences); order them before this proxy's bulk reads.
+    __threadfence();
+    asm volatile("fence.proxy.async.global;" ::: "memory");
+    const int pos = pos0 + step, chunks = (pos + CHUNK - 1) / CHUNK;
+    for (int l = 0; l < A.n_layers; ++l) {
+      const size_t off = (((size_t)l * KH + g) * A.capacity) * D;
+      auto bytes = [&](int c) { return (unsigned)(min(CHUNK, pos - c * CHUNK) * D * 2); };
+      int ck = 0, cv = 0;
+      for (; ck < chunks && ck < KSLOTS; ++ck)
+        if (!ring_issue(kr, nk, A.k_cache + off + (size_t)ck * CHUNK * D, bytes(ck), sh, A.ctrl)) return;
+      for (; cv < chunks && cv < VSLOTS; ++cv)
+        if (!ring_issue(vr, nv, A.v_cache + off + (size_t)cv * CHUNK * D, bytes(cv), sh, A.ctrl)) return;
+      for (; ck < chunks; ++ck)
+        if (!ring_issue(kr, nk, A.k_cache + off + (size_t)ck * CHUNK * D, bytes(ck), sh, A.ctrl)) return;
+      for (; cv < chunks; ++cv)
+        if (!ring_issue(vr, nv, A.v_cache + off + (size_t)cv * CHUNK * D, bytes(cv), sh, A.ctrl)) return;
+    }
+  }
+}
+
+// ------------------------------------------------------------ consumers ----
 
 struct Ctx {
   const MegaArgs* A;
-  Ring r;
+  unsigned long long* trace;  // this CTA's row of phase stamps during a traced step, else nullptr
   Shared* sh;
+  Ring wr, kr, vr;
+  int nw, nk, nv;  // copies consumed per ring
   int8_t* xq;
   float* xs;
   float* xres;
@@ -302,21 +366,16 @@ struct Ctx {
   float* av;
   float* sc;
   double* red;
-  int gc;  // pieces consumed
   int tid, warp, lane;
 };
 
-// Products of one ring piece: `ntiles` tiles of K columns at `slot`, written to
-// prod[(tile_base + t) * pstride + b * 8 + row].
-__device__ void piece_products(Ctx& c, int ntiles, int K, int tb, int tile_base, int pstride) {
-  const int slot = c.gc % NSLOT;
-  const unsigned parity = (unsigned)((c.gc / NSLOT) & 1);
-  // Every lane waits on the slot; the warp proceeds only if all lanes saw it
-  // full (they differ only when the kernel is aborting), so the __syncwarp
-  // below is always reached by the whole warp.
-  const bool ok = wait_full(&c.r.full[slot], parity, c.sh, c.A->ctrl);
-  if (!__all_sync(0xffffffffu, ok)) return;  // abort: the drain waits for the copy
-  const uint8_t* base = c.r.base + (size_t)slot * SLOT;
+// Block products of one weight-ring piece of `ntiles` tiles (K columns) into
+// prod[(tile_base + t) * 8 * RS + row * RS + b] with RS = K/32 + 4: a row's
+// products are contiguous (read back as 16-byte vectors) and the padding keeps
+// both the writes and the reads free of bank conflicts.
+__device__ void piece_products(Ctx& c, int ntiles, int K, int tb, int tile_base) {
+  const uint8_t* base = ring_acquire(c.wr, c.nw, c.sh, c.A->ctrl);
+  if (base == nullptr) return;  // aborting: the drain waits for this copy
   const int B = K / 32, BP = B / 2;
   const int row = c.lane & 7, half = (c.lane >> 3) & 1, bsel = c.lane >> 4;
   const int units = ntiles * BP;
@@ -328,23 +387,34 @@ __device__ void piece_products(Ctx& c, int ntiles, int K, int tb, int tile_base,
     const int dot = part + __shfl_xor_sync(0xffffffffu, part, 8);
     if (half == 0) {
       const float ws = __half2float(reinterpret_cast<const __half*>(tile + (size_t)8 * K)[b * 8 + row]);
-      c.prod[(tile_base + t) * pstride + b * 8 + row] = __fmul_rn(__fmul_rn(__int2float_rn(dot), ws), c.xs[b]);
+      c.prod[((tile_base + t) * 8 + row) * (B + 4) + b] = __fmul_rn(__fmul_rn(__int2float_rn(dot), ws), c.xs[b]);
     }
   }
-  __syncwarp();
-  if (c.lane == 0) mbar_arrive(&c.r.empty[slot]);
-  ++c.gc;
+  ring_release(c.wr, c.nw, c.lane);
+  ++c.nw;
 }
 
-// Ordered block sum of one row: the reference's accumulation order.
-__device__ __forceinline__ float row_sum(const float* prod, int ti, int r, int B, int pstride) {
-  const float* p = prod + ti * pstride + r;
+// Ordered block sum of one row (the reference's accumulation order); the
+// products are fetched 32 at a time ahead of the dependent adds.
+__device__ __forceinline__ float row_sum(const float* prod, int ti, int r, int B) {
+  const float4* p = reinterpret_cast<const float4*>(prod + (ti * 8 + r) * (B + 4));
   float s = 0.0f;
-  for (int b = 0; b < B; ++b) s = __fadd_rn(s, p[b * 8]);
+  for (int k = 0; k < B / 4; k += 8) {
+    float4 v[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] = p[k + i];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      s = __fadd_rn(s, v[i].x);
+      s = __fadd_rn(s, v[i].y);
+      s = __fadd_rn(s, v[i].z);
+      s = __fadd_rn(s, v[i].w);
+    }
+  }
   return s;
 }
 
-// RMSNorm(v) * gamma then per-32-block quantisation into xq/xs (K = 1024).
+// RMSNorm(v) * gamma, then per-32-block quantisation into xq/xs (K = 1024).
 __device__ void norm_quant(Ctx& c, const float* v, const float* gamma, float eps) {
   double part = 0.0;
   for (int k = c.tid; k < W; k += CTHREADS) {
@@ -367,7 +437,7 @@ __device__ void norm_quant(Ctx& c, const float* v, const float* gamma, float eps
   csync();
 }
 
-// Per-32-block quantisation of a vector already in registers' reach (smem `v`, K values).
+// Per-32-block quantisation of K values in shared memory.
 __device__ void quant_only(Ctx& c, const float* v, int K) {
   for (int j = c.warp; j < K / 32; j += CWARPS) {
     const float y = v[j * 32 + c.lane];
@@ -379,7 +449,7 @@ __device__ void quant_only(Ctx& c, const float* v, int K) {
   csync();
 }
 
-// Loads n tagged words into dst (float); all consumer threads.
+// Loads n tagged words into dst (float), all consumer threads.
 __device__ void load_tagged(Ctx& c, const unsigned long long* src, int n, unsigned tag, float* dst) {
   for (int i = c.tid; i < n; i += CTHREADS) {
     float v;
@@ -389,37 +459,38 @@ __device__ void load_tagged(Ctx& c, const unsigned long long* src, int n, unsign
   csync();
 }
 
-// RMSNorm of one 128-wide head held by 4 warps (warp0..warp0+3), in place in v.
-__device__ __forceinline__ void head_norm(Ctx& c, float* v, const float* gamma, float eps, int warp0, int redslot) {
+// RMSNorm of one 128-wide head held by 4 warps (warp0..warp0+3) in place;
+// named barrier `bar` (128 threads).
+__device__ __forceinline__ void head_norm(Ctx& c, float* v, const float* gamma, float eps, int warp0, int bar) {
   const int i = c.tid - warp0 * 32;
   const float x = v[i];
-  double part = warp_sum_d(__dmul_rn((double)x, (double)x));
-  if (c.lane == 0) c.red[redslot + (c.warp - warp0)] = part;
-  asm volatile("bar.sync %0, 128;" ::"r"(2 + redslot / 4) : "memory");
+  const double part = warp_sum_d(__dmul_rn((double)x, (double)x));
+  double* red = c.red + 4 * (bar - 2);
+  if (c.lane == 0) red[c.warp - warp0] = part;
+  asm volatile("bar.sync %0, 128;" ::"r"(bar) : "memory");
   double var = 0.0;
-  for (int w = 0; w < 4; ++w) var = __dadd_rn(var, c.red[redslot + w]);
+  for (int w = 0; w < 4; ++w) var = __dadd_rn(var, red[w]);
   const float inv = rms_inverse(var, D, eps);
-  const float y = __fmul_rn(__fmul_rn(x, inv), gamma[i]);
-  asm volatile("bar.sync %0, 128;" ::"r"(2 + redslot / 4) : "memory");
-  v[i] = y;
-  asm volatile("bar.sync %0, 128;" ::"r"(2 + redslot / 4) : "memory");
+  v[i] = __fmul_rn(__fmul_rn(x, inv), gamma[i]);
+  asm volatile("bar.sync %0, 128;" ::"r"(bar) : "memory");
 }
 
-// RoPE on one head in place (TensorMath.Rope.cs:51-53), 128 threads of warp0..warp0+3.
-__device__ __forceinline__ void head_rope(Ctx& c, float* v, int pos, int warp0, int barid) {
+// RoPE on one head in place (TensorMath.Rope.cs:51-53), same 128 threads.
+__device__ __forceinline__ void head_rope(Ctx& c, float* v, int pos, int warp0, int bar) {
   const int i = c.tid - warp0 * 32, half = D / 2, k = i < half ? i : i - half;
   const float co = c.A->rope_cos[(size_t)pos * half + k], si = c.A->rope_sin[(size_t)pos * half + k];
   const float a = v[k], b = v[k + half];
   const float o = i < half ? __fsub_rn(__fmul_rn(a, co), __fmul_rn(b, si)) : __fadd_rn(__fmul_rn(a, si), __fmul_rn(b, co));
-  asm volatile("bar.sync %0, 128;" ::"r"(barid) : "memory");
+  asm volatile("bar.sync %0, 128;" ::"r"(bar) : "memory");
   v[i] = o;
 }
 
-// Exact paired-GQA attention of query head h = blockIdx.x at position pos.
+// Exact paired-GQA attention of query head h = blockIdx.x at position pos
+// (TensorMath.DecoderAttention.cs:17-52 in the order of TensorMath.AttentionAvx.cs
+// and TensorMath.SoftmaxAvx.cs), K/V history from the chunk rings.
 __device__ void attention(Ctx& c, int layer, int pos, unsigned tag_in, unsigned tag_out) {
   const MegaArgs& A = *c.A;
   const int h = blockIdx.x, g = h >> 1;
-  // q, k, v rows of this head (tagged by the Q phase)
   for (int i = c.tid; i < 3 * D; i += CTHREADS) {
     const int src = i < D ? h * D + i : (i < 2 * D ? QW + g * D + (i - D) : QW + KVW + g * D + (i - 2 * D));
     float v;
@@ -427,21 +498,22 @@ __device__ void attention(Ctx& c, int layer, int pos, unsigned tag_in, unsigned 
     (i < D ? c.aq : (i < 2 * D ? c.ak : c.av))[i % D] = v;
   }
   csync();
+  if (c.trace && c.tid == 0) c.trace[8 * layer + 2] = global_ns();
   if (c.sh->abort) return;
   const MegaLayer& Lw = A.layers[layer];
   if (c.warp < 4) {  // q: RMSNorm + RoPE (QwenDecoder.cs:188,193)
-    head_norm(c, c.aq, Lw.q_norm, A.eps, 0, 0);
+    head_norm(c, c.aq, Lw.q_norm, A.eps, 0, 2);
     head_rope(c, c.aq, pos, 0, 2);
-  } else if (c.warp < 8) {  // k: RMSNorm + RoPE + binary16 (QwenDecoder.cs:191,194,199)
-    head_norm(c, c.ak, Lw.k_norm, A.eps, 4, 4);
+  } else if (c.warp < 8) {  // k: RMSNorm + RoPE (QwenDecoder.cs:191,194)
+    head_norm(c, c.ak, Lw.k_norm, A.eps, 4, 3);
     head_rope(c, c.ak, pos, 4, 3);
   }
   csync();
   const size_t head_off = (((size_t)layer * KH + g) * A.capacity) * D;
-  if (c.tid < D) {
+  if (c.tid < D) {  // binary16 rounding of k and v (QwenDecoder.cs:199-200)
     const __half kh = __float2half_rn(c.ak[c.tid]);
     const __half vh = __float2half_rn(c.av[c.tid]);
-    if ((h & 1) == 0) {  // one CTA of the pair writes the cache row (QwenDecoder.cs:199-200)
+    if ((h & 1) == 0) {  // one CTA of the pair writes the cache row
       A.k_cache[head_off + (size_t)pos * D + (c.tid & 7) * (D / 8) + (c.tid >> 3)] = kh;
       A.v_cache[head_off + (size_t)pos * D + c.tid] = vh;
     }
@@ -449,34 +521,49 @@ __device__ void attention(Ctx& c, int layer, int pos, unsigned tag_in, unsigned 
     c.av[c.tid] = __half2float(vh);
   }
   csync();
-  // scores: 8 threads per position, lane j sums channels j, j+8, ... in order
-  const int len = pos + 1, j = c.lane & 7, slot = c.tid >> 3;
+  if (c.trace && c.tid == 0) c.trace[8 * layer + 3] = global_ns();
+  // Scores: one position per 8 threads, lane j sums channels j, j+8, ... in order.
+  const int j = c.lane & 7, slot = c.tid >> 3;
   float qj[D / 8];
 #pragma unroll
   for (int i = 0; i < D / 8; ++i) qj[i] = c.aq[j + 8 * i];
   const float divisor = __fsqrt_rn((float)D);
-  const __half* kc = A.k_cache + head_off;
-  for (int base = 0; base < len; base += CTHREADS / 8) {
-    const int t = base + slot;
+  const int chunks = (pos + CHUNK - 1) / CHUNK;
+  for (int ch = 0; ch < chunks; ++ch) {
+    const uint8_t* kb = ring_acquire(c.kr, c.nk, c.sh, A.ctrl);
+    if (kb == nullptr) return;
+    const int t = ch * CHUNK + slot;
     float acc = 0.0f;
     if (t < pos) {
-      const uint4* kr = reinterpret_cast<const uint4*>(kc + (size_t)t * D + j * (D / 8));
-      const uint4 ka = __ldcg(kr), kb = __ldcg(kr + 1);
+      const uint4* kr = reinterpret_cast<const uint4*>(kb + (size_t)slot * D * 2 + j * (D / 8) * 2);
+      const uint4 ka = kr[0], kc = kr[1];
       const __half* k0 = reinterpret_cast<const __half*>(&ka);
-      const __half* k1 = reinterpret_cast<const __half*>(&kb);
+      const __half* k1 = reinterpret_cast<const __half*>(&kc);
 #pragma unroll
       for (int i = 0; i < D / 8; ++i) acc = __fadd_rn(acc, __fmul_rn(qj[i], __half2float(i < 8 ? k0[i] : k1[i - 8])));
-    } else if (t == pos) {
+    }
+    acc = __fadd_rn(acc, __shfl_down_sync(0xffffffffu, acc, 4));
+    acc = __fadd_rn(acc, __shfl_down_sync(0xffffffffu, acc, 1));
+    acc = __fadd_rn(acc, __shfl_down_sync(0xffffffffu, acc, 2));
+    if (j == 0 && t < pos) c.sc[t] = __fdiv_rn(acc, divisor);
+    ring_release(c.kr, c.nk, c.lane);
+    ++c.nk;
+  }
+  if (c.warp == 0) {  // position pos from the fresh k
+    float acc = 0.0f;
+    if (slot == 0) {
 #pragma unroll
       for (int i = 0; i < D / 8; ++i) acc = __fadd_rn(acc, __fmul_rn(qj[i], c.ak[j + 8 * i]));
     }
     acc = __fadd_rn(acc, __shfl_down_sync(0xffffffffu, acc, 4));
     acc = __fadd_rn(acc, __shfl_down_sync(0xffffffffu, acc, 1));
     acc = __fadd_rn(acc, __shfl_down_sync(0xffffffffu, acc, 2));
-    if (j == 0 && t < len) c.sc[t] = __fdiv_rn(acc, divisor);
+    if (c.lane == 0) c.sc[pos] = __fdiv_rn(acc, divisor);
   }
   csync();
-  // softmax (TensorMath.SoftmaxAvx.cs:11-58)
+  if (c.trace && c.tid == 0) c.trace[8 * layer + 4] = global_ns();
+  // Softmax (TensorMath.SoftmaxAvx.cs:11-58).
+  const int len = pos + 1;
   float mx = -INFINITY;
   for (int t = c.tid; t < len; t += CTHREADS) mx = fmaxf(mx, c.sc[t]);
 #pragma unroll
@@ -506,54 +593,88 @@ __device__ void attention(Ctx& c, int layer, int pos, unsigned tag_in, unsigned 
   const float inv = redf[31];
   for (int t = c.tid; t < len; t += CTHREADS) c.sc[t] = __fmul_rn(c.sc[t], inv);
   csync();
-  // V sum per channel in position order (TensorMath.AttentionAvx.cs:188-213)
-  if (c.tid < D) {
-    const __half* vc = A.v_cache + head_off + c.tid;
+  if (c.trace && c.tid == 0) c.trace[8 * layer + 5] = global_ns();
+  // V sum per channel in position order (TensorMath.AttentionAvx.cs:188-213): warps 0..3.
+  if (c.warp < 4) {
     float acc = 0.0f;
-    int t = 0;
-    for (; t + 8 <= pos; t += 8) {
-      float v[8];
+    for (int ch = 0; ch < chunks; ++ch) {
+      const uint8_t* vb = ring_acquire(c.vr, c.nv, c.sh, A.ctrl);
+      if (vb == nullptr) return;
+      const __half* vv = reinterpret_cast<const __half*>(vb) + c.tid;
+      const int t0 = ch * CHUNK, n = min(CHUNK, pos - t0);
+      int t = 0;
+      for (; t + 8 <= n; t += 8) {
+        float v[8];
 #pragma unroll
-      for (int u = 0; u < 8; ++u) v[u] = __half2float(__ldcg(vc + (size_t)(t + u) * D));
+        for (int u = 0; u < 8; ++u) v[u] = __half2float(vv[(t + u) * D]);
 #pragma unroll
-      for (int u = 0; u < 8; ++u) acc = __fadd_rn(acc, __fmul_rn(v[u], c.sc[t + u]));
+        for (int u = 0; u < 8; ++u) acc = __fadd_rn(acc, __fmul_rn(v[u], c.sc[t0 + t + u]));
+      }
+      for (; t < n; ++t) acc = __fadd_rn(acc, __fmul_rn(__half2float(vv[t * D]), c.sc[t0 + t]));
+      ring_release(c.vr, c.nv, c.lane);
+      ++c.nv;
     }
-    for (; t < pos; ++t) acc = __fadd_rn(acc, __fmul_rn(__half2float(__ldcg(vc + (size_t)t * D)), c.sc[t]));
     acc = __fadd_rn(acc, __fmul_rn(c.av[c.tid], c.sc[pos]));
     st_word(A.attn_t + h * D + c.tid, pack(acc, tag_out));
   }
 }
 
+// Records a phase timestamp of the first step (thread 0 only; a no-op unless tracing).
+#define MEGA_TRACE(event)                                                                 \
+  do {                                                                                    \
+    if (A.trace != nullptr && step == 0 && tid == 0 && (event) < kTraceEvents)            \
+      A.trace[(size_t)blockIdx.x * kTraceEvents + (event)] = global_ns();                \
+  } while (0)
+
 __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(const MegaArgs A) {
   extern __shared__ __align__(128) uint8_t smem[];
   const Layout L = layout(A.capacity);
   Shared* sh = reinterpret_cast<Shared*>(smem + L.shared);
-  Ring ring{smem + L.ring, reinterpret_cast<uint64_t*>(smem + L.bars),
-            reinterpret_cast<uint64_t*>(smem + L.bars) + NSLOT};
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L.bars);
+  const Ring wr{smem + L.ring, bars, bars + WSLOTS, WSLOTS, WSLOT, 0};
+  const Ring kr{smem + L.ring, bars + 12, bars + 12 + KSLOTS, KSLOTS, CSLOT, 1};
+  const Ring vr{smem + L.ring + KSLOTS * CSLOT, bars + 24, bars + 24 + VSLOTS, VSLOTS, CSLOT, 2};
+  const bool att = blockIdx.x < ATT_CTAS;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   if (tid == 0) {
-    for (int i = 0; i < NSLOT; ++i) {
-      mbar_init(&ring.full[i], 1);
-      mbar_init(&ring.empty[i], CWARPS);
+    for (int i = 0; i < WSLOTS; ++i) {
+      mbar_init(&wr.full[i], 1);
+      mbar_init(&wr.empty[i], CWARPS);
+    }
+    for (int i = 0; i < KSLOTS; ++i) {
+      mbar_init(&kr.full[i], 1);
+      mbar_init(&kr.empty[i], CWARPS);
+    }
+    for (int i = 0; i < VSLOTS; ++i) {
+      mbar_init(&vr.full[i], 1);
+      mbar_init(&vr.empty[i], 4);  // the V sum runs on warps 0..3
     }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-    sh->quit = sh->go = sh->issued = sh->prod_exit = sh->abort = 0;
-    sh->stopped = 0;
+    sh->quit = sh->go = sh->prod_exit = sh->abort = 0;
+    sh->issued[0] = sh->issued[1] = sh->issued[2] = 0;
   }
   __syncthreads();
   MegaCtrl* ctrl = A.ctrl;
   const int pos0 = ctrl->pos;
   const unsigned epoch = ctrl->epoch;
   const unsigned tps = (unsigned)((A.n_layers + 1) * 8);
-  if (warp == CWARPS) {  // producer warp
-    if (lane == 0) producer(A, ring, sh, pos0);
+  if (warp == CWARPS) {  // producer warp: one elected lane issues every copy
+    if (lane == 0) {
+      if (att) producer_attention(A, kr, vr, sh, pos0);
+      else producer_gemv(A, wr, sh);
+      sh->prod_exit = 1;
+    }
     return;
   }
 
   Ctx c;
   c.A = &A;
-  c.r = ring;
   c.sh = sh;
+  c.wr = wr;
+  c.kr = kr;
+  c.vr = vr;
+  c.nw = c.nk = c.nv = 0;
+  c.trace = nullptr;
   c.xq = reinterpret_cast<int8_t*>(smem + L.xq);
   c.xs = reinterpret_cast<float*>(smem + L.xs);
   c.xres = reinterpret_cast<float*>(smem + L.xres);
@@ -565,11 +686,11 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(const Mega
   c.av = reinterpret_cast<float*>(smem + L.att_v);
   c.sc = reinterpret_cast<float*>(smem + L.sc);
   c.red = reinterpret_cast<double*>(smem + L.red);
-  c.gc = 0;
   c.tid = tid;
   c.warp = warp;
   c.lane = lane;
-  const Spans sp = spans(blockIdx.x, gridDim.x, A.vocab / 8);
+  const int n_gemv = gridDim.x - ATT_CTAS;
+  const Spans sp = spans(att ? 0 : blockIdx.x - ATT_CTAS, n_gemv, A.vocab / 8);
   int token = ctrl->token;
   int steps = 0;
   bool stopped = false;
@@ -588,108 +709,120 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(const Mega
     if (tid == 0) sh->go = step + 1;
     const int pos = pos0 + step;
     const unsigned tbase = epoch + (unsigned)step * tps;
-    // Embed (Weight.CopyRow, Gguf.cs:340-344): every CTA builds the row itself.
-    if (tid < W / 16) {
-      const int r = token & 7;
-      const uint8_t* tile = A.emb + (size_t)(token >> 3) * TB_W;
-      const uint4 q = *reinterpret_cast<const uint4*>(tile + (size_t)tid * 128 + r * 16);
-      const float s = __half2float(reinterpret_cast<const __half*>(tile + 8 * W)[(tid >> 1) * 8 + r]);
-      const int8_t* qb = reinterpret_cast<const int8_t*>(&q);
+    c.trace = (A.trace != nullptr && step == 0) ? A.trace + (size_t)blockIdx.x * kTraceEvents : nullptr;
+    if (!att) {  // Embed (Weight.CopyRow, Gguf.cs:340-344): each GEMV CTA builds the row itself
+      if (tid < W / 16) {
+        const int r = token & 7;
+        const uint8_t* tile = A.emb + (size_t)(token >> 3) * TB_W;
+        const uint4 q = *reinterpret_cast<const uint4*>(tile + (size_t)tid * 128 + r * 16);
+        const float s = __half2float(reinterpret_cast<const __half*>(tile + 8 * W)[(tid >> 1) * 8 + r]);
+        const int8_t* qb = reinterpret_cast<const int8_t*>(&q);
 #pragma unroll
-      for (int i = 0; i < 16; ++i) c.xres[tid * 16 + i] = __fmul_rn((float)qb[i], s);
+        for (int i = 0; i < 16; ++i) c.xres[tid * 16 + i] = __fmul_rn((float)qb[i], s);
+      }
+      csync();
     }
-    csync();
     for (int layer = 0; layer < A.n_layers; ++layer) {
-      const MegaLayer& Lw = A.layers[layer];
       const unsigned tl = tbase + (unsigned)(layer * 8);
+      if (att) {
+        MEGA_TRACE(8 * layer + 0);
+        attention(c, layer, pos, tl + kTagQkv, tl + kTagAttn);
+        csync();
+        MEGA_TRACE(8 * layer + 1);
+        if (sh->abort) goto drain;
+        continue;
+      }
+      const MegaLayer& Lw = A.layers[layer];
       // ---- Q: x -> RMSNorm -> quantise -> q/k/v rows ----
       if (layer > 0) load_tagged(c, A.x_t, W, tl - 8 + kTagX, c.xres);
       if (sh->abort) goto drain;
+      MEGA_TRACE(8 * layer + 0);
       norm_quant(c, c.xres, Lw.attn_norm, A.eps);
-      for (int t = 0; t < sp.qn; t += 3) piece_products(c, min(3, sp.qn - t), W, TB_W, t, 264);
+      for (int t = 0; t < sp.qn; t += 3) piece_products(c, min(3, sp.qn - t), W, TB_W, t);
       csync();
       if (sh->abort) goto drain;
       if (tid < sp.qn * 8) {
-        const float v = row_sum(c.prod, tid >> 3, tid & 7, W / 32, 264);
+        const float v = row_sum(c.prod, tid >> 3, tid & 7, W / 32);
         st_word(A.qkv_t + (sp.q0 * 8 + tid), pack(v, tl + kTagQkv));
       }
-      // ---- A: attention (CTAs 0..15) ----
-      if (blockIdx.x < ATT_CTAS) {
-        attention(c, layer, pos, tl + kTagQkv, tl + kTagAttn);
-        csync();
-        if (sh->abort) goto drain;
-      }
-      // ---- O: attn -> quantise -> o + x ----
+      MEGA_TRACE(8 * layer + 1);
+      // ---- O: attention output -> quantise -> o + x ----
       if (sp.on > 0) {
-        float* attn = c.vin;
-        load_tagged(c, A.attn_t, QW, tl + kTagAttn, attn);
+        load_tagged(c, A.attn_t, QW, tl + kTagAttn, c.vin);
         if (sh->abort) goto drain;
-        quant_only(c, attn, QW);
-        for (int t = 0; t < sp.on; ++t) piece_products(c, 1, QW, TB_Q, t, 520);
+        MEGA_TRACE(8 * layer + 2);
+        quant_only(c, c.vin, QW);
+        for (int t = 0; t < sp.on; ++t) piece_products(c, 1, QW, TB_Q, t);
         csync();
         if (sh->abort) goto drain;
         if (tid < sp.on * 8) {
           const int row = sp.o0 * 8 + tid;
-          const float v = __fadd_rn(row_sum(c.prod, tid >> 3, tid & 7, QW / 32, 520), c.xres[row]);
+          const float v = __fadd_rn(row_sum(c.prod, tid >> 3, tid & 7, QW / 32), c.xres[row]);
           st_word(A.a_t + row, pack(v, tl + kTagA));
         }
+        MEGA_TRACE(8 * layer + 3);
       }
       // ---- GU: a -> RMSNorm -> quantise -> SiLU(gate) * up ----
       load_tagged(c, A.a_t, W, tl + kTagA, c.ares);
       if (sh->abort) goto drain;
+      MEGA_TRACE(8 * layer + 4);
       norm_quant(c, c.ares, Lw.ffn_norm, A.eps);
-      for (int t = 0; t < sp.gun; ++t) piece_products(c, 2, W, TB_W, 2 * t, 264);
+      for (int t = 0; t < sp.gun; ++t) piece_products(c, 2, W, TB_W, 2 * t);
       csync();
       if (sh->abort) goto drain;
       if (tid < sp.gun * 8) {
         const int p = tid >> 3, r = tid & 7;
-        const float g = row_sum(c.prod, 2 * p, r, W / 32, 264), u = row_sum(c.prod, 2 * p + 1, r, W / 32, 264);
-        st_word(A.act_t + (sp.gu0 + p) * 8 + r, pack(silu_mul1(g, u), tl + kTagAct));
+        const float gg = row_sum(c.prod, 2 * p, r, W / 32), u = row_sum(c.prod, 2 * p + 1, r, W / 32);
+        st_word(A.act_t + (sp.gu0 + p) * 8 + r, pack(silu_mul1(gg, u), tl + kTagAct));
       }
+      MEGA_TRACE(8 * layer + 5);
       // ---- D: act -> quantise -> down + a ----
       if (sp.dn > 0) {
-        float* act = c.vin;
-        load_tagged(c, A.act_t, FFN, tl + kTagAct, act);
+        load_tagged(c, A.act_t, FFN, tl + kTagAct, c.vin);
         if (sh->abort) goto drain;
-        quant_only(c, act, FFN);
-        for (int t = 0; t < sp.dn; ++t) piece_products(c, 1, FFN, TB_F, t, 776);
+        MEGA_TRACE(8 * layer + 6);
+        quant_only(c, c.vin, FFN);
+        for (int t = 0; t < sp.dn; ++t) piece_products(c, 1, FFN, TB_F, t);
         csync();
         if (sh->abort) goto drain;
         if (tid < sp.dn * 8) {
           const int row = sp.d0 * 8 + tid;
-          const float v = __fadd_rn(row_sum(c.prod, tid >> 3, tid & 7, FFN / 32, 776), c.ares[row]);
+          const float v = __fadd_rn(row_sum(c.prod, tid >> 3, tid & 7, FFN / 32), c.ares[row]);
           st_word(A.x_t + row, pack(v, tl + kTagX));
         }
+        MEGA_TRACE(8 * layer + 7);
       }
     }
     {
       // ---- LM: final RMSNorm, lm_head rows, argmax (QwenDecoder.cs:262-268,278-326) ----
       const unsigned tlm = tbase + (unsigned)(A.n_layers * 8);
-      load_tagged(c, A.x_t, W, tlm - 8 + kTagX, c.xres);
-      if (sh->abort) goto drain;
-      norm_quant(c, c.xres, A.out_norm, A.eps);
       float best_v = __int_as_float(0x7fc00000);
       int best_i = INT_MAX;
       bool row0_nan = false;
-      int buf = 0;
-      for (int t = 0; t < sp.lmn; t += 3, buf ^= 1) {
-        const int n = min(3, sp.lmn - t);
-        piece_products(c, n, W, TB_W, buf * 3, 264);
-        csync();
+      if (!att) {
+        load_tagged(c, A.x_t, W, tlm - 8 + kTagX, c.xres);
         if (sh->abort) goto drain;
-        if (tid < n * 8) {
-          const int row = (sp.lm0 + t) * 8 + tid;
-          const float v = row_sum(c.prod, buf * 3 + (tid >> 3), tid & 7, W / 32, 264);
-          if (A.logits) A.logits[row] = v;
-          if (row == 0) row0_nan = isnan(v);
-          if (better(v, row, best_v, best_i)) {
-            best_v = v;
-            best_i = row;
+        MEGA_TRACE(8 * A.n_layers + 0);
+        norm_quant(c, c.xres, A.out_norm, A.eps);
+        int buf = 0;
+        for (int t = 0; t < sp.lmn; t += 3, buf ^= 1) {
+          const int n = min(3, sp.lmn - t);
+          piece_products(c, n, W, TB_W, buf * 3);
+          csync();
+          if (sh->abort) goto drain;
+          if (tid < n * 8) {
+            const int row = (sp.lm0 + t) * 8 + tid;
+            const float v = row_sum(c.prod, buf * 3 + (tid >> 3), tid & 7, W / 32);
+            if (A.logits) A.logits[row] = v;
+            if (row == 0) row0_nan = isnan(v);
+            if (better(v, row, best_v, best_i)) {
+              best_v = v;
+              best_i = row;
+            }
           }
         }
       }
-      // CTA-level argmax (threads 0..23 hold candidates; all in warp 0)
-      if (warp == 0) {
+      if (warp == 0) {  // CTA argmax (threads 0..23 hold the candidates)
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) {
           const float ov = __shfl_xor_sync(0xffffffffu, best_v, o);
@@ -706,6 +839,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(const Mega
         }
       }
       csync();
+      MEGA_TRACE(8 * A.n_layers + 1);
       if (tid == 0) {
         __threadfence();  // release this step's KV rows before the partials
         st_word(A.part_v + blockIdx.x, pack(sh->best_v[0], tlm + kTagPart));
@@ -757,6 +891,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(const Mega
         sh->token = (f0 || bi == INT_MAX || bi < 0) ? 0 : bi;
       }
       csync();
+      MEGA_TRACE(8 * A.n_layers + 2);
       token = sh->token;
       ++steps;
     }
@@ -774,16 +909,9 @@ drain:
         break;
       }
     }
-    const int issued = sh->issued;
-    for (int g = c.gc; g < issued; ++g) {
-      const int slot = g % NSLOT;
-      const unsigned parity = (unsigned)((g / NSLOT) & 1);
-      for (unsigned it = 0; !mbar_try_wait(&ring.full[slot], parity); ++it)
-        if (it > kWaitLimit) {
-          raise_error(sh, ctrl, kErrWaitDrain);
-          break;
-        }
-    }
+    ring_drain(wr, c.nw, sh->issued[0], sh, ctrl);
+    ring_drain(kr, c.nk, sh->issued[1], sh, ctrl);
+    ring_drain(vr, c.nv, sh->issued[2], sh, ctrl);
   }
   csync();
   if (blockIdx.x == 0 && tid == 0) {
@@ -808,7 +936,7 @@ int mega_grid(int device, int capacity) {
   FA_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, decode_mega_kernel, kMegaThreads, smem));
   int sms = 0;
   FA_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device));
-  if (per_sm < 1 || sms < ATT_CTAS + 16) return 0;
+  if (per_sm < 1 || sms < ATT_CTAS + 32) return 0;
   return sms;
 }
 

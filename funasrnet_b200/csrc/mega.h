@@ -61,7 +61,14 @@ struct MegaArgs {
   int n_end = 0;
   int* log = nullptr;
   int log_cap = 0;
+  // Optional phase timestamps of the first step (%globaltimer, ns):
+  // trace[cta * kTraceEvents + event]; events per layer l: 8*l + {0 inputs
+  // ready, 1 Q/A done, 2 O inputs ready, 3 O done, 4 GU inputs ready,
+  // 5 GU done, 6 D inputs ready, 7 D done}; then LM inputs ready, LM done,
+  // token known.
+  unsigned long long* trace = nullptr;
 };
+constexpr int kTraceEvents = 8 * 28 + 8;
 
 // Model shape the kernel is compiled for: hidden 1024, 16 query heads and 8 KV
 // heads of 128, FFN 3072 (Qwen3-0.6B).

@@ -152,6 +152,8 @@ struct fa_session {
   bool use_mega = false;
   int mega_grid = 0;
   DevBuf mx, mqkv, mattn, ma, mact, mpv, mpi, mctrl;
+  bool trace = false;
+  DevBuf trace_buf;                          // [grid x kTraceEvents] phase timestamps
   int* d_int(int i) const { return ints.as<int>() + i; }
 };
 
@@ -1269,6 +1271,12 @@ static MegaCtrl run_mega(fa_session* s, int steps, int record, int n_end, int ho
   a.n_end = n_end;
   a.log = s->log.as<int>();
   a.log_cap = s->log_cap;
+  if (s->trace) {
+    const size_t bytes = (size_t)s->mega_grid * kTraceEvents * 8;
+    s->trace_buf.ensure(bytes);
+    FA_CUDA(cudaMemsetAsync(s->trace_buf.p, 0, bytes, s->stream));
+    a.trace = s->trace_buf.as<unsigned long long>();
+  }
   // control block: pos, token (host or last device argmax), counters cleared
   s->pinned[8] = s->pos;
   s->pinned[9] = host_token;
@@ -1410,6 +1418,22 @@ int fa_session_kernels_per_step(const fa_session* s) {
 
 int fa_session_uses_persistent_kernel(const fa_session* s) {
   return s ? ((s->use_mega && s->exact_attention) ? s->mega_grid : 0) : -1;
+}
+
+int fa_session_set_trace(fa_session* s, int on) {
+  return with_session(s, [&] {
+    s->trace = on != 0;
+    return (int)kHandled;
+  });
+}
+
+int fa_session_get_trace(fa_session* s, uint64_t* out, int capacity) {
+  return with_session(s, [&] {
+    const int n = s->mega_grid * kTraceEvents;
+    if (!s->trace || !s->trace_buf.p) throw Error(kErrArgument, "no trace recorded");
+    if (out) FA_CUDA(cudaMemcpy(out, s->trace_buf.p, (size_t)std::min(n, capacity) * 8, cudaMemcpyDeviceToHost));
+    return n;
+  });
 }
 
 int fa_session_set_persistent_kernel(fa_session* s, int on) {

@@ -133,6 +133,16 @@ class QwenDecoder:
     def set_persistent(self, on: bool = True) -> bool:
         return check(lib().fa_session_set_persistent_kernel(self._h, 1 if on else 0)) == FA_OK
 
+    def trace_phases(self, on: bool = True) -> None:
+        check(lib().fa_session_set_trace(self._h, 1 if on else 0))
+
+    def phase_trace(self) -> np.ndarray:
+        """[grid x events] %globaltimer stamps (ns) of the last launch's first step."""
+        n = check(lib().fa_session_get_trace(self._h, None, 0))
+        out = np.zeros(n, np.uint64)
+        check(lib().fa_session_get_trace(self._h, ptr(out), n))
+        return out.reshape(self.persistent_grid(), -1)
+
     def kernels_per_step(self) -> int:
         return int(lib().fa_session_kernels_per_step(self._h))
 

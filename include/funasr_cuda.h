@@ -183,6 +183,13 @@ int fa_session_uses_persistent_kernel(const fa_session* session);
 /* Selects the persistent kernel (1) or the CUDA-graph step (0); FA_DECLINED when
  * the persistent kernel is unavailable for this model or device. */
 int fa_session_set_persistent_kernel(fa_session* session, int on);
+/* Profiling hook of the persistent kernel: when on, each launch records
+ * %globaltimer stamps (ns) of its first step's phases per CTA; get_trace copies
+ * [grid x events] stamps (events per layer l: 8l + {0 inputs ready, 1 Q or
+ * attention done, 2 O inputs, 3 O done, 4 GU inputs, 5 GU done, 6 D inputs,
+ * 7 D done}, then LM inputs, LM done, token known) and returns grid*events. */
+int fa_session_set_trace(fa_session* session, int on);
+int fa_session_get_trace(fa_session* session, uint64_t* out, int capacity);
 /* Number of kernel launches one generate iteration replays (kernel nodes of
  * its CUDA graph); 0 before the first fa_session_generate. */
 int fa_session_kernels_per_step(const fa_session* session);
