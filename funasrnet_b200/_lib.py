@@ -77,6 +77,7 @@ SIGNATURES = {
     "fa_session_set_exact_attention": (i32, [vp, i32]),
     "fa_session_debug_layer0": (i32, [vp, cp, vp]),
     "fa_session_time_lm_head": (i32, [vp, i32, P(f32)]),
+    "fa_lm_head_argmax_noalloc": (i32, [vp, vp, vp, vp, f32, vp, vp, vp]),
 }
 
 

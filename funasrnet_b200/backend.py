@@ -148,6 +148,28 @@ class CudaFloatBackend:
             return False, None
         return True, outs
 
+    def make_resident(self, w: Weight) -> None:
+        """Uploads ``w`` to the device now rather than on its first use."""
+        self._check()
+        with self._lock:
+            self._resident_handle(w)
+
+    # Allocation-free lm_head step (no counterpart in the reference).
+    def lm_head_argmax_noalloc(self, w: Weight, x: int, gamma: int | None, eps: float, logits: int | None,
+                               token: int, stream: int | None = None) -> bool:
+        """Enqueues RMSNorm (skipped when ``gamma`` is None) + the Q8 projection
+        by ``w`` + the greedy argmax of one frame on ``stream`` and returns
+        without waiting.  ``x``, ``gamma``, ``logits`` and ``token`` are device
+        addresses; ``w`` must be resident already (``make_resident``), so that
+        the call allocates nothing.  False when declined."""
+        self._check()
+        with self._lock:
+            h = self._resident.get(w)
+            if h is None:
+                raise ValueError(f"{w.name}: not resident; call make_resident first")
+            rc = check(lib().fa_lm_head_argmax_noalloc(self._h, h, x, gamma, eps, logits, token, stream))
+        return rc == FA_OK
+
     def dispose(self) -> None:
         if self._disposed:
             return

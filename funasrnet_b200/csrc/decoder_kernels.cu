@@ -802,6 +802,8 @@ int k_cache_pos(int c, int head_size) { return kpos(c, head_size); }
 
 int gemv_smem_bytes(int K, int) { return gemv_smem_layout(K).total; }
 
+int gemv_ctas(int tiles) { return (tiles + kGemvTiles - 1) / kGemvTiles; }
+
 void launch_gemv(const GemvArgs& a, cudaStream_t stream) {
   const int smem = gemv_smem_layout(a.w.cols).total;
   if (smem > kGemvMaxSmem) throw Error(kErrCapacity, "GEMV inner dimension too large for shared memory");

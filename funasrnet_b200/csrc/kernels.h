@@ -46,6 +46,9 @@ void launch_gemv(const GemvArgs& a, cudaStream_t stream);
 void prepare_kernels();
 // Dynamic shared memory one Q8 GEMV launch needs (<= 227 KB or the launch is refused).
 int gemv_smem_bytes(int K, int epilogue);
+// CTAs of one single-frame Q8 GEMV launch over `tiles` 8-row tiles (the number
+// of argmax partials its argmax epilogue writes).
+int gemv_ctas(int tiles);
 
 // FP32 weights ("F32 layout"): row-major rows whose columns are permuted inside
 // each 32-column group so that position 4j + m holds column j + 8m.  Thread j

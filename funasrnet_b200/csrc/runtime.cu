@@ -514,6 +514,83 @@ int fa_op_attention_pair(fa_backend* b, const float* query, const float* keys, c
   });
 }
 
+}  // extern "C"
+
+// ------------------------------------------------ allocation-free lm_head ----
+
+// Scratch of fa_lm_head_argmax_noalloc: the argmax epilogue's arrival counter
+// and per-CTA partials, held in module memory so that the call allocates
+// nothing.  Words: 0 arrival counter (zero before every launch; the launch's
+// last CTA also puts it back to zero), 1 row-0 NaN flag, then from word
+// kNoAllocHead the partial values [kNoAllocMaxCtas] and the partial indices
+// [kNoAllocMaxCtas]: 64 KB in all.
+constexpr int kNoAllocMaxCtas = 8192;
+constexpr int kNoAllocHead = 64;
+static_assert(FA_NOALLOC_MAX_ROWS == kNoAllocMaxCtas * 4 * kTileRows, "one GEMV CTA covers 4 tiles of 8 rows");
+static __device__ __align__(256) unsigned g_noalloc_scratch[kNoAllocHead + 2 * kNoAllocMaxCtas];
+
+namespace {
+
+constexpr int kNoAllocDevices = 64;
+std::mutex g_noalloc_mu;
+unsigned* g_noalloc_addr[kNoAllocDevices] = {};
+
+// Device address of the scratch on `device`, which must be current.  The first
+// call per device looks the address up, zeroes the block and sets the GEMV
+// kernels' shared-memory attribute; later calls only read the table.
+unsigned* noalloc_scratch(int device) {
+  if (device < 0 || device >= kNoAllocDevices) throw Error(kErrArgument, "device ordinal beyond the scratch table");
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  if (g_noalloc_addr[device] == nullptr) {
+    void* p = nullptr;
+    FA_CUDA(cudaGetSymbolAddress(&p, g_noalloc_scratch));
+    FA_CUDA(cudaMemset(p, 0, sizeof(g_noalloc_scratch)));
+    prepare_kernels();
+    g_noalloc_addr[device] = static_cast<unsigned*>(p);
+  }
+  return g_noalloc_addr[device];
+}
+
+}  // namespace
+
+extern "C" {
+
+int fa_lm_head_argmax_noalloc(fa_backend* b, const fa_weight* w, const float* x, const float* gamma, float eps,
+                              float* logits, int32_t* token, void* stream) {
+  return guarded([&] {
+    check_backend(b);
+    if (!x || !token) throw Error(kErrArgument, "null input or token");
+    std::lock_guard<std::mutex> lk(b->mu);
+    if (b->disposed) throw Error(kErrDisposed, "backend disposed");
+    if (!w || w->owner != b || !b->weights.count(const_cast<fa_weight*>(w)))
+      throw Error(kErrArgument, "weight not owned by this backend");
+    if (!w->q8 || gemv_smem_bytes(w->cols, kEpiArgmax) > 226 * 1024) return (int)kDeclined;
+    if (w->rows > FA_NOALLOC_MAX_ROWS || gemv_ctas(w->view.tiles) > kNoAllocMaxCtas)
+      throw Error(kErrCapacity, "weight rows beyond the allocation-free scratch (FA_NOALLOC_MAX_ROWS)");
+    DeviceGuard g(b->device);
+    unsigned* s = noalloc_scratch(b->device);
+    cudaStream_t st = stream != nullptr ? static_cast<cudaStream_t>(stream) : b->stream;
+    // The counter and the NaN flag start at zero even after a launch that
+    // failed part way.
+    FA_CUDA(cudaMemsetAsync(s, 0, 2 * sizeof(unsigned), st));
+    GemvArgs a;
+    a.x = x;
+    a.frames = 1;
+    a.gamma = gamma;
+    a.eps = eps;
+    a.w = w->view;
+    a.epilogue = kEpiArgmax;
+    a.logits = logits;
+    a.am.counter = s;
+    a.am.row0_nan = reinterpret_cast<int*>(s + 1);
+    a.am.part_value = reinterpret_cast<float*>(s + kNoAllocHead);
+    a.am.part_index = reinterpret_cast<int*>(s + kNoAllocHead + kNoAllocMaxCtas);
+    a.am.token = token;
+    launch_gemv(a, st);
+    return (int)kHandled;
+  });
+}
+
 int fa_synth_write_gguf(const char* path, uint64_t seed, int layers, int vocab, int width, int ffn, int quantized) {
   return guarded([&] {
     if (!path) throw Error(kErrArgument, "null path");

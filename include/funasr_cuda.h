@@ -198,6 +198,37 @@ int fa_session_kernels_per_step(const fa_session* session);
  * returns its mean CUDA-event duration in ms. */
 int fa_session_time_lm_head(fa_session* session, int iters, float* ms);
 
+/* ---------------------------------------------------------------------------
+ * Allocation-free lm_head step.  It has no counterpart in the reference, whose
+ * backends only take host arrays.
+ *
+ * Some callers cannot allocate device memory during their loop.  One kind is a
+ * host that hands the whole device to its own memory pool at start-up.
+ * Another is a latency-bound loop in which the device-wide synchronisation of
+ * a cudaFree would stall the work on its other streams.  The other entry
+ * points of this header may allocate: their staging buffers grow on demand.
+ * This one never does.
+ *
+ * One frame of RMSNorm (skipped when gamma is NULL), the Q8 projection by
+ * `weight`, and QwenDecoder.Greedy of the result (src/FunAsrNet/QwenDecoder.cs:
+ * 262-268,278-326).  All data pointers are device pointers on the backend's
+ * device: x [cols] and gamma [cols] float, logits [rows] float or NULL, and
+ * token, one int32 that receives the greedy token.  The call only enqueues the
+ * work on `stream` (a cudaStream_t; NULL selects the backend's own stream) and
+ * returns; the caller synchronises.  The results are bit-identical to
+ * fa_op_rmsnorm, then fa_try_quantized_linear, then fa_op_greedy.  An FP32
+ * weight, or cols too wide for one CTA's shared memory, gives FA_DECLINED.
+ *
+ * Limit: rows <= FA_NOALLOC_MAX_ROWS, else FA_ERR_CAPACITY.  The argmax
+ * partials live in a fixed 64 KB block of module memory, one per device.  The
+ * first call on a device sets that block up: make that first call before any
+ * stream capture.  All calls on one device share the block, so calls that
+ * overlap in time on one device race.  Serialise them, on one stream or with
+ * events between streams. */
+#define FA_NOALLOC_MAX_ROWS 262144
+int fa_lm_head_argmax_noalloc(fa_backend* backend, const fa_weight* weight, const float* x, const float* gamma,
+                              float eps, float* logits, int32_t* token, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
