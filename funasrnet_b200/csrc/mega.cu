@@ -9,8 +9,9 @@
 //   of 8-row weight tiles, through a 6-slot ring, phase after phase, layer
 //   after layer, then their share of the lm_head.
 //   Attention CTAs stream their KV head's history: K in chunks of 60
-//   positions through a 6-slot ring, V through a 4-slot ring, issued as soon
-//   as a layer starts (the history does not depend on the current token).
+//   positions through a 6-slot ring, V through a 4-slot ring; each ring takes
+//   its next chunk (of this or a later layer) as soon as a slot frees, since
+//   the history does not depend on the current token.
 //
 // Phases of one step (QwenDecoder.Decode, QwenDecoder.cs:180-268):
 //   embed (each GEMV CTA computes the token's row itself)
@@ -41,6 +42,8 @@
 #include "fa_common.h"
 #include "mega.h"
 
+extern __shared__ __align__(128) uint8_t fa_mega_smem[];
+
 namespace fa {
 namespace {
 
@@ -60,7 +63,6 @@ constexpr int CHUNK = 60;                        // KV positions per attention c
 constexpr int CSLOT = CHUNK * D * 2;             // 15360 bytes
 constexpr int KSLOTS = 6, VSLOTS = 4;
 constexpr int ATT_CTAS = H;
-constexpr int PROD_FLOATS = 2048;
 constexpr unsigned kWaitLimit = 1u << 22;
 
 static_assert(KSLOTS * CSLOT + VSLOTS * CSLOT <= WSLOTS * WSLOT, "KV rings share the weight ring's memory");
@@ -68,7 +70,12 @@ static_assert(KSLOTS * CSLOT + VSLOTS * CSLOT <= WSLOTS * WSLOT, "KV rings share
 enum { kTagQkv = 1, kTagAttn = 2, kTagA = 3, kTagAct = 4, kTagX = 5, kTagPart = 6 };
 enum { kErrWaitData = 1, kErrWaitFull = 2, kErrWaitEmpty = 3, kErrWaitGo = 4, kErrWaitDrain = 5 };
 
+struct Spans {
+  int q0, qn, o0, on, gb0, gbn, d0, dn, lm0, lmn;
+};
+
 struct Shared {
+  Spans sp;                 // this CTA's GEMV spans (kept here, not in registers)
   volatile int quit;        // consumers stop the producer
   volatile int go;          // steps the consumers have committed to
   volatile int issued[3];   // copies issued per ring (weights / K / V)
@@ -79,36 +86,36 @@ struct Shared {
   int best_i[32];
 };
 
-struct Layout {
-  int ring, bars, xq, xs, xres, ares, vin, prod, att_q, att_k, att_v, sc, red, shared, total;
-};
+// Shared memory: fixed-size regions at compile-time offsets (addresses fold
+// into the instructions instead of occupying registers), then the score row
+// of `capacity` floats.
+constexpr int align_up(int o, int a) { return (o + a - 1) / a * a; }
+constexpr int kOffRing = 0;                                        // weight ring / K and V rings
+constexpr int kOffBars = align_up(kOffRing + WSLOTS * WSLOT, 8);   // 32 mbarriers
+constexpr int kOffXq = align_up(kOffBars + 32 * 8, 16);            // quantised activations, skewed (xq_off)
+constexpr int kOffXs = align_up(kOffXq + FFN + FFN / 256 * 16, 16); // their block scales
+constexpr int kOffXres = align_up(kOffXs + FFN / 32 * 4, 16);      // x (residual of O)
+constexpr int kOffAres = kOffXres + W * 4;                         // a (residual of D)
+constexpr int kOffGFirst = kOffAres + W * 4;                       // layer 0 attn_norm
+constexpr int kOffGOut = kOffGFirst + W * 4;                       // output norm
+constexpr int kOffPart = kOffGOut + W * 4;                         // row sums crossing warps [32 x 8]
+constexpr int kOffAttQ = kOffPart + 32 * 8 * 4;
+constexpr int kOffAttK = kOffAttQ + D * 4;
+constexpr int kOffAttV = kOffAttK + D * 4;
+constexpr int kOffRed = kOffAttV + D * 4;                          // 64 doubles of reductions
+constexpr int kOffShared = align_up(kOffRed + 64 * 8, 16);
+constexpr int kOffScores = align_up(kOffShared + (int)sizeof(Shared), 16);
 
-__host__ __device__ inline Layout layout(int capacity) {
-  Layout L;
-  int o = 0;
-  auto take = [&](int bytes, int align) {
-    o = (o + align - 1) / align * align;
-    int at = o;
-    o += bytes;
-    return at;
-  };
-  L.ring = take(WSLOTS * WSLOT, 128);
-  L.bars = take(32 * 8, 8);
-  L.xq = take(FFN, 16);
-  L.xs = take(FFN / 32 * 4, 16);
-  L.xres = take(W * 4, 16);
-  L.ares = take(W * 4, 16);
-  L.vin = take(FFN * 4, 16);
-  L.prod = take(PROD_FLOATS * 4, 16);
-  L.att_q = take(D * 4, 16);
-  L.att_k = take(D * 4, 16);
-  L.att_v = take(D * 4, 16);
-  L.sc = take(capacity * 4, 16);
-  L.red = take(64 * 8, 16);
-  L.shared = take((int)sizeof(Shared), 16);
-  L.total = o;
-  return L;
+__host__ __device__ constexpr int smem_total(int capacity) { return kOffScores + capacity * 4; }
+
+template <typename T>
+__device__ __forceinline__ T* sm(int off) {
+  return reinterpret_cast<T*>(fa_mega_smem + off);
 }
+
+// Byte offset of quantised block b in xq: 16 bytes of skew every 8 blocks put
+// the four lane groups of a row warp (blocks 8 apart) on distinct banks.
+__device__ __forceinline__ int xq_off(int b) { return b * 32 + (b >> 3) * 16; }
 
 // ---------------------------------------------------------------- PTX ----
 
@@ -132,6 +139,16 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, unsigned parity) {
       : "memory");
   return ok != 0;
 }
+// Non-blocking probe of a phase (try_wait may suspend the thread a while).
+__device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, unsigned parity) {
+  unsigned ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(saddr(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
 // 1D bulk copy global -> this CTA's shared memory, completing on `bar`.
 __device__ __forceinline__ void bulk_load(void* dst, const void* src, unsigned bytes, uint64_t* bar) {
   asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
@@ -147,6 +164,14 @@ __device__ __forceinline__ unsigned long long ld_word(const unsigned long long* 
 __device__ __forceinline__ void st_word(unsigned long long* p, unsigned long long v) {
   asm volatile("st.relaxed.gpu.global.b64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
+__device__ __forceinline__ unsigned long long ld_word_acquire(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.acquire.gpu.global.b64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_word_release(unsigned long long* p, unsigned long long v) {
+  asm volatile("st.release.gpu.global.b64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
 __device__ __forceinline__ int ld_flag(const int* p) {
   int v;
   asm volatile("ld.relaxed.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
@@ -156,6 +181,17 @@ __device__ __forceinline__ unsigned long long pack(float v, unsigned tag) {
   return ((unsigned long long)tag << 32) | __float_as_uint(v);
 }
 __device__ __forceinline__ void csync() { asm volatile("bar.sync 1, 480;" ::: "memory"); }
+// Barrier over the compute warps returning the OR of `v` over their threads:
+// a CTA-uniform decision even while another warp may be raising the abort flag.
+__device__ __forceinline__ bool csync_or(bool v) {
+  int r;
+  asm volatile(
+      "{\n .reg .pred p, q;\n setp.ne.u32 p, %1, 0;\n bar.red.or.pred q, 1, 480, p;\n selp.s32 %0, 1, 0, q;\n}\n"
+      : "=r"(r)
+      : "r"((unsigned)v)
+      : "memory");
+  return r != 0;
+}
 
 __device__ __forceinline__ unsigned long long global_ns() {
   unsigned long long t;
@@ -169,9 +205,11 @@ __device__ __forceinline__ void raise_error(Shared* sh, MegaCtrl* ctrl, int code
 }
 
 // Spins until the tagged word carries `tag`; false when the kernel aborts.
+// ACQ: the load that sees the tag is an acquire.
+template <bool ACQ = false>
 __device__ bool wait_word(const unsigned long long* p, unsigned tag, float& out, Shared* sh, MegaCtrl* ctrl) {
   for (unsigned it = 0;; ++it) {
-    const unsigned long long v = ld_word(p);
+    const unsigned long long v = ACQ ? ld_word_acquire(p) : ld_word(p);
     if ((unsigned)(v >> 32) == tag) {
       out = __uint_as_float((unsigned)v);
       return true;
@@ -195,15 +233,14 @@ __device__ __forceinline__ void split(int total, int parts, int part, int& first
   n = (int)((long long)(part + 1) * total / parts) - first;
 }
 
-// GEMV spans of GEMV CTA `g` (0-based among GEMV CTAs) in tiles (GU: pairs).
-struct Spans {
-  int q0, qn, o0, on, gu0, gun, d0, dn, lm0, lmn;
-};
+// GEMV spans of GEMV CTA `g` (0-based among GEMV CTAs) in 8-row tiles; the
+// gate/up projection in 32-row activation blocks (4 gate/up tile pairs), so
+// that each block's SiLU*up values are quantised by the CTA that makes them.
 __device__ Spans spans(int g, int n, int lm_tiles) {
   Spans s;
   split(QKV / 8, n, g, s.q0, s.qn);
   split(W / 8, n, g, s.o0, s.on);
-  split(FFN / 8, n, g, s.gu0, s.gun);
+  split(FFN / 32, n, g, s.gb0, s.gbn);
   split(W / 8, n, g, s.d0, s.dn);
   split(lm_tiles, n, g, s.lm0, s.lmn);
   return s;
@@ -217,6 +254,20 @@ struct Ring {
   uint64_t* empty;
   int nslot, slot_bytes, id;
 };
+
+// The three rings over the same memory (a CTA uses either the weight ring or
+// the K and V rings).  Barriers: weights 0..11, K 12..23, V 24..31.
+__device__ __forceinline__ Ring ring_w() {
+  return Ring{sm<uint8_t>(kOffRing), sm<uint64_t>(kOffBars), sm<uint64_t>(kOffBars) + WSLOTS, WSLOTS, WSLOT, 0};
+}
+__device__ __forceinline__ Ring ring_k() {
+  return Ring{sm<uint8_t>(kOffRing), sm<uint64_t>(kOffBars) + 12, sm<uint64_t>(kOffBars) + 12 + KSLOTS, KSLOTS, CSLOT,
+              1};
+}
+__device__ __forceinline__ Ring ring_v() {
+  return Ring{sm<uint8_t>(kOffRing) + KSLOTS * CSLOT, sm<uint64_t>(kOffBars) + 24, sm<uint64_t>(kOffBars) + 24 + VSLOTS,
+              VSLOTS, CSLOT, 2};
+}
 
 // Producer side: copies `bytes` from `src` into the ring's next slot.
 __device__ bool ring_issue(const Ring& r, int& n, const void* src, unsigned bytes, Shared* sh, MegaCtrl* ctrl) {
@@ -301,16 +352,18 @@ __device__ void producer_gemv(const MegaArgs& A, const Ring& r, Shared* sh) {
   const int n_gemv = gridDim.x - ATT_CTAS;
   const Spans sp = spans(blockIdx.x - ATT_CTAS, n_gemv, A.vocab / 8);
   int n = 0;
+  // The weights do not depend on the step, so the stream runs ahead into the
+  // next step without waiting for it to start; after an early stop the
+  // consumers' drain waits for whatever was issued.
   for (int step = 0; step < A.max_steps; ++step) {
-    if (!wait_go(sh, A.ctrl, step)) return;
     for (int l = 0; l < A.n_layers; ++l) {
       const MegaLayer& Lw = A.layers[l];
       for (int t = 0; t < sp.qn; t += 3)
         if (!ring_issue(r, n, Lw.qkv + (size_t)(sp.q0 + t) * TB_W, min(3, sp.qn - t) * TB_W, sh, A.ctrl)) return;
       for (int t = 0; t < sp.on; ++t)
         if (!ring_issue(r, n, Lw.o + (size_t)(sp.o0 + t) * TB_Q, TB_Q, sh, A.ctrl)) return;
-      for (int t = 0; t < sp.gun; ++t)
-        if (!ring_issue(r, n, Lw.gu + (size_t)(sp.gu0 + t) * 2 * TB_W, 2 * TB_W, sh, A.ctrl)) return;
+      for (int t = 0; t < 4 * sp.gbn; ++t)  // one gate/up pair per piece
+        if (!ring_issue(r, n, Lw.gu + (size_t)(4 * sp.gb0 + t) * 2 * TB_W, 2 * TB_W, sh, A.ctrl)) return;
       for (int t = 0; t < sp.dn; ++t)
         if (!ring_issue(r, n, Lw.down + (size_t)(sp.d0 + t) * TB_F, TB_F, sh, A.ctrl)) return;
     }
@@ -319,8 +372,24 @@ __device__ void producer_gemv(const MegaArgs& A, const Ring& r, Shared* sh) {
   }
 }
 
-// K/V history of this CTA's KV head, positions [0, pos), per layer: the first
-// K chunks, the first V chunks, then the rest of each as slots free up.
+// Producer side, non-blocking: true when the ring's next slot is free.
+__device__ __forceinline__ bool ring_free(const Ring& r, int n) {
+  if (n < r.nslot) return true;
+  return mbar_test_wait(&r.empty[n % r.nslot], (unsigned)((n / r.nslot - 1) & 1));
+}
+// Producer side: copies into the ring's next slot, which must be free.
+__device__ __forceinline__ void ring_put(const Ring& r, int& n, const void* src, unsigned bytes, Shared* sh) {
+  const int slot = n % r.nslot;
+  mbar_expect_tx(&r.full[slot], bytes);
+  bulk_load(r.base + (size_t)slot * r.slot_bytes, src, bytes, &r.full[slot]);
+  ++n;
+  sh->issued[r.id] = n;
+}
+
+// K/V history of this CTA's KV head, positions [0, pos), layer after layer,
+// in chunks of CHUNK positions.  The K and V rings advance independently:
+// whichever has a free slot gets its next chunk, so the next layer's K
+// chunks stream in while this layer's V sum still holds the V ring.
 __device__ void producer_attention(const MegaArgs& A, const Ring& kr, const Ring& vr, Shared* sh, int pos0) {
   const int g = blockIdx.x >> 1;
   int nk = 0, nv = 0;
@@ -331,18 +400,35 @@ __device__ void producer_attention(const MegaArgs& A, const Ring& kr, const Ring
     __threadfence();
     asm volatile("fence.proxy.async.global;" ::: "memory");
     const int pos = pos0 + step, chunks = (pos + CHUNK - 1) / CHUNK;
-    for (int l = 0; l < A.n_layers; ++l) {
-      const size_t off = (((size_t)l * KH + g) * A.capacity) * D;
-      auto bytes = [&](int c) { return (unsigned)(min(CHUNK, pos - c * CHUNK) * D * 2); };
-      int ck = 0, cv = 0;
-      for (; ck < chunks && ck < KSLOTS; ++ck)
-        if (!ring_issue(kr, nk, A.k_cache + off + (size_t)ck * CHUNK * D, bytes(ck), sh, A.ctrl)) return;
-      for (; cv < chunks && cv < VSLOTS; ++cv)
-        if (!ring_issue(vr, nv, A.v_cache + off + (size_t)cv * CHUNK * D, bytes(cv), sh, A.ctrl)) return;
-      for (; ck < chunks; ++ck)
-        if (!ring_issue(kr, nk, A.k_cache + off + (size_t)ck * CHUNK * D, bytes(ck), sh, A.ctrl)) return;
-      for (; cv < chunks; ++cv)
-        if (!ring_issue(vr, nv, A.v_cache + off + (size_t)cv * CHUNK * D, bytes(cv), sh, A.ctrl)) return;
+    if (chunks == 0) continue;
+    auto src = [&](const __half* cache, int l, int ch) {
+      return cache + (((size_t)l * KH + g) * A.capacity + (size_t)ch * CHUNK) * D;
+    };
+    auto bytes = [&](int ch) { return (unsigned)(min(CHUNK, pos - ch * CHUNK) * D * 2); };
+    int kl = 0, kc = 0, vl = 0, vc = 0;  // next (layer, chunk) of each ring
+    for (unsigned idle = 0; kl < A.n_layers || vl < A.n_layers;) {
+      bool moved = false;
+      if (kl < A.n_layers && ring_free(kr, nk)) {
+        ring_put(kr, nk, src(A.k_cache, kl, kc), bytes(kc), sh);
+        if (++kc == chunks) kc = 0, ++kl;
+        moved = true;
+      }
+      if (vl < A.n_layers && ring_free(vr, nv)) {
+        ring_put(vr, nv, src(A.v_cache, vl, vc), bytes(vc), sh);
+        if (++vc == chunks) vc = 0, ++vl;
+        moved = true;
+      }
+      if (moved) {
+        idle = 0;
+        continue;
+      }
+      if ((++idle & 63) == 0) {
+        if (sh->abort || sh->quit) return;
+        if (idle > kWaitLimit) {
+          raise_error(sh, A.ctrl, kErrWaitEmpty);
+          return;
+        }
+      }
     }
   }
 }
@@ -352,133 +438,298 @@ __device__ void producer_attention(const MegaArgs& A, const Ring& kr, const Ring
 struct Ctx {
   const MegaArgs* A;
   unsigned long long* trace;  // this CTA's row of phase stamps during a traced step, else nullptr
-  Shared* sh;
-  Ring wr, kr, vr;
-  int nw, nk, nv;  // copies consumed per ring
-  int8_t* xq;
-  float* xs;
-  float* xres;
-  float* ares;
-  float* vin;  // attention output (O) / SiLU*up activation (D) inputs
-  float* prod;
-  float* aq;
-  float* ak;
-  float* av;
-  float* sc;
-  double* red;
+  int nw, nk, nv;             // copies consumed per ring
   int tid, warp, lane;
+  __device__ Shared* sh() const { return sm<Shared>(kOffShared); }
+  __device__ int8_t* xq() const { return sm<int8_t>(kOffXq); }
+  __device__ float* xs() const { return sm<float>(kOffXs); }
+  __device__ float* xres() const { return sm<float>(kOffXres); }
+  __device__ float* ares() const { return sm<float>(kOffAres); }
+  __device__ float* part() const { return sm<float>(kOffPart); }
+  __device__ float* aq() const { return sm<float>(kOffAttQ); }
+  __device__ float* ak() const { return sm<float>(kOffAttK); }
+  __device__ float* av() const { return sm<float>(kOffAttV); }
+  __device__ float* sc() const { return sm<float>(kOffScores); }
+  __device__ double* red() const { return sm<double>(kOffRed); }
 };
 
-// Block products of one weight-ring piece of `ntiles` tiles (K columns) into
-// prod[(tile_base + t) * 8 * RS + row * RS + b] with RS = K/32 + 4: a row's
-// products are contiguous (read back as 16-byte vectors) and the padding keeps
-// both the writes and the reads free of bank conflicts.
-__device__ void piece_products(Ctx& c, int ntiles, int K, int tb, int tile_base) {
-  const uint8_t* base = ring_acquire(c.wr, c.nw, c.sh, c.A->ctrl);
-  if (base == nullptr) return;  // aborting: the drain waits for this copy
-  const int B = K / 32, BP = B / 2;
-  const int row = c.lane & 7, half = (c.lane >> 3) & 1, bsel = c.lane >> 4;
-  const int units = ntiles * BP;
-  for (int u = c.warp; u < units; u += CWARPS) {
-    const int t = u / BP, b = 2 * (u - t * BP) + bsel;
-    const uint8_t* tile = base + (size_t)t * tb;
-    const uint4 w = *reinterpret_cast<const uint4*>(tile + (size_t)(2 * b + half) * 128 + row * 16);
-    const int part = dot16(w, *reinterpret_cast<const int4*>(c.xq + b * 32 + half * 16));
-    const int dot = part + __shfl_xor_sync(0xffffffffu, part, 8);
-    if (half == 0) {
-      const float ws = __half2float(reinterpret_cast<const __half*>(tile + (size_t)8 * K)[b * 8 + row]);
-      c.prod[((tile_base + t) * 8 + row) * (B + 4) + b] = __fmul_rn(__fmul_rn(__int2float_rn(dot), ws), c.xs[b]);
-    }
-  }
-  ring_release(c.wr, c.nw, c.lane);
-  ++c.nw;
+// ------------------------------------------------------------ W8A8 rows ----
+// A warp computes whole rows of an 8-row tile: lane (r, g) = (lane & 7,
+// lane >> 3) forms the block products of row r for blocks 8g..8g+7 of the
+// tile's 32-block segment, p_b = ((float)dot_b * ws) * xs
+// (TensorMath.QuantizedRowsAvx.cs:30-41).  The row sum then runs through the
+// four lane groups in block order, so it is the reference's strictly
+// sequential sum.  Tiles with K > 1024 are split into 1024-column segments on
+// consecutive warps; the running sums cross warps through shared memory,
+// ordered by named barriers (ids 4..15).
+
+__device__ __forceinline__ void named_sync(int id, int threads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+__device__ __forceinline__ void named_arrive(int id, int threads) {
+  asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_count(uint64_t* bar, unsigned count) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0], %1;" ::"r"(saddr(bar)), "r"(count) : "memory");
 }
 
-// Ordered block sum of one row (the reference's accumulation order); the
-// products are fetched 32 at a time ahead of the dependent adds.
-__device__ __forceinline__ float row_sum(const float* prod, int ti, int r, int B) {
-  const float4* p = reinterpret_cast<const float4*>(prod + (ti * 8 + r) * (B + 4));
-  float s = 0.0f;
-  for (int k = 0; k < B / 4; k += 8) {
-    float4 v[8];
+template <int K>
+__device__ __forceinline__ void row_products(const uint8_t* tile, const int8_t* xq, const float* xs, int r, int b0,
+                                             float (&p)[8]) {
 #pragma unroll
-    for (int i = 0; i < 8; ++i) v[i] = p[k + i];
+  for (int i = 0; i < 8; ++i) {
+    // at most four blocks' loads in flight: keeps the live registers in budget
+    if (i == 4) asm volatile("" ::: "memory");
+    const int b = b0 + i;
+    const uint4 w0 = *reinterpret_cast<const uint4*>(tile + (size_t)(2 * b) * 128 + r * 16);
+    const uint4 w1 = *reinterpret_cast<const uint4*>(tile + (size_t)(2 * b + 1) * 128 + r * 16);
+    const int4 x0 = *reinterpret_cast<const int4*>(xq + xq_off(b));
+    const int4 x1 = *reinterpret_cast<const int4*>(xq + xq_off(b) + 16);
+    const int dot = dot16(w0, x0) + dot16(w1, x1);
+    const float ws = __half2float(reinterpret_cast<const __half*>(tile + (size_t)8 * K)[b * 8 + r]);
+    p[i] = __fmul_rn(__fmul_rn(__int2float_rn(dot), ws), xs[b]);
+  }
+}
+
+// Ordered sum through the lane groups: `s` enters as the sum before the
+// segment (used by group 0) and the row's running sum leaves in group 3.
+__device__ __forceinline__ float chain_groups(const float (&p)[8], int g, float s) {
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      s = __fadd_rn(s, v[i].x);
-      s = __fadd_rn(s, v[i].y);
-      s = __fadd_rn(s, v[i].z);
-      s = __fadd_rn(s, v[i].w);
+  for (int stage = 0; stage < 4; ++stage) {
+    if (g == stage) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) s = __fadd_rn(s, p[i]);
     }
+    const float up = __shfl_up_sync(0xffffffffu, s, 8);
+    if (g == stage + 1) s = up;
   }
   return s;
 }
 
-// RMSNorm(v) * gamma, then per-32-block quantisation into xq/xs (K = 1024).
-__device__ void norm_quant(Ctx& c, const float* v, const float* gamma, float eps) {
-  double part = 0.0;
-  for (int k = c.tid; k < W; k += CTHREADS) {
-    const double z = (double)v[k];
-    part = __dadd_rn(part, __dmul_rn(z, z));
+// Segment s of tile t: continues the previous segment's sums (named barrier
+// 4 + t * (NS - 1) + s - 1) and hands its own on unless it is the last.
+template <int K>
+__device__ __forceinline__ float tile_segment(Ctx& c, const uint8_t* tile, int t, int s) {
+  constexpr int NS = K / 1024;
+  const int r = c.lane & 7, g = c.lane >> 3;
+  float p[8];
+  row_products<K>(tile, c.xq(), c.xs(), r, s * 32 + g * 8, p);
+  float start = 0.0f;
+  if (NS > 1 && s > 0) {
+    named_sync(4 + t * (NS - 1) + s - 1, 64);
+    start = c.part()[t * 8 + r];
   }
+  const float sum = chain_groups(p, g, start);
+  if (NS > 1 && s < NS - 1) {
+    if (g == 3) c.part()[t * 8 + r] = sum;
+    named_arrive(4 + t * (NS - 1) + s, 64);
+  }
+  return sum;
+}
+
+// One projection phase over this CTA's nt tiles of K columns, streamed in ring
+// pieces of `per` tiles.  epi(t, r, sum) runs in the lanes that hold the sum
+// of row r of tile t.  False when the kernel aborts.
+template <int K, typename Epi>
+__device__ __forceinline__ bool w8a8_phase(Ctx& c, int nt, int per, Epi epi) {
+  constexpr int NS = K / 1024, TB = 8 * K + (K / 32) * 16;
+  const int np = (nt + per - 1) / per;
+  bool failed = false;
+  for (int p = 0; p < np && !failed; ++p) failed = ring_acquire(ring_w(), c.nw + p, c.sh(), c.A->ctrl) == nullptr;
+  // Every warp takes the same branch: the jobs below wait on each other at
+  // named barriers, which have no time limit.  (On failure the drain waits
+  // for the copies in flight.)
+  if (csync_or(failed)) return false;
+  for (int j = c.warp; j < nt * NS; j += CWARPS) {  // warp-uniform
+    const int t = j / NS, s = j - t * NS, piece = t / per;
+    const uint8_t* tile = ring_w().base + (size_t)((c.nw + piece) % WSLOTS) * WSLOT + (size_t)(t - piece * per) * TB;
+    const float sum = tile_segment<K>(c, tile, t, s);
+    if (s == NS - 1 && (c.lane >> 3) == 3) epi(t, c.lane & 7, sum);
+  }
+  for (int p = 0; p < np; ++p) ring_release(ring_w(), c.nw + p, c.lane);
+  c.nw += np;
+  csync();  // the next phase rewrites xq/xs and part
+  return true;
+}
+
+// Quantised activations crossing CTAs: word i < n/4 holds values 4i..4i+3 as
+// int8 bytes, word n/4 + j the scale of block j (both tagged).  Quantises the
+// 32-block held one value per lane and publishes it as block j.
+__device__ __forceinline__ void publish_block(unsigned long long* dst, int n, int j, float v, unsigned tag, int lane) {
+  float d, id;
+  block_scale(v, d, id);
+  const unsigned byte = (unsigned)(quant1(v, id) & 0xff) << (8 * (lane & 3));
+  const unsigned w = byte | __shfl_down_sync(0xffffffffu, byte, 1) | __shfl_down_sync(0xffffffffu, byte, 2) |
+                     __shfl_down_sync(0xffffffffu, byte, 3);
+  if ((lane & 3) == 0) st_word(dst + j * 8 + (lane >> 2), ((unsigned long long)tag << 32) | w);
+  if (lane == 0) st_word(dst + n / 4 + j, pack(d, tag));
+}
+
+// Waits for n quantised values in that format and unpacks them into xq/xs.
+__device__ __forceinline__ void gather_q8(Ctx& c, const unsigned long long* src, int n, unsigned tag) {
+  const int total = n / 4 + n / 32;  // <= 2 * CTHREADS
+  unsigned pending = 0;
+#pragma unroll
+  for (int k = 0; k < 2; ++k)
+    if (c.tid + k * CTHREADS < total) pending |= 1u << k;
+  for (unsigned it = 0; pending != 0; ++it) {
+    unsigned long long w[2];
+#pragma unroll
+    for (int k = 0; k < 2; ++k) w[k] = (pending >> k) & 1u ? ld_word(src + c.tid + k * CTHREADS) : 0ull;
+#pragma unroll
+    for (int k = 0; k < 2; ++k)
+      if (((pending >> k) & 1u) && (unsigned)(w[k] >> 32) == tag) {
+        const int i = c.tid + k * CTHREADS;
+        if (i < n / 4) *reinterpret_cast<unsigned*>(c.xq() + xq_off(i >> 3) + (i & 7) * 4) = (unsigned)w[k];
+        else c.xs()[i - n / 4] = __uint_as_float((unsigned)w[k]);
+        pending &= ~(1u << k);
+      }
+    if (pending == 0) break;
+    if (it >= 4096) __nanosleep(128);
+    if ((it & 1023) == 1023) {
+      if (c.sh()->abort || ld_flag(&c.A->ctrl->error)) {
+        c.sh()->abort = 1;
+        break;
+      }
+      if (it > kWaitLimit) {
+        raise_error(c.sh(), c.A->ctrl, kErrWaitData);
+        break;
+      }
+    }
+  }
+  csync();
+}
+
+// This thread's RMSNorm weights in norm_quant's block mapping (block
+// j = warp + 15 i, element 32 j + lane), requested ahead of the phase's wait
+// so that their DRAM latency overlaps it.
+struct Gamma {
+  float g[3];
+};
+__device__ __forceinline__ Gamma load_gamma(const Ctx& c, const float* gamma) {
+  Gamma r;
+#pragma unroll
+  for (int i = 0; i < 3; ++i) {
+    const int j = c.warp + i * CWARPS;
+    r.g[i] = j < W / 32 ? gamma[j * 32 + c.lane] : 0.0f;
+  }
+  return r;
+}
+
+// Waits for the tagged words src[0, n) (n <= NW * CTHREADS) and leaves word
+// tid + k * CTHREADS in v[k] (0 beyond n): element `lane` of block
+// warp + 15 k, which is the quantiser's block mapping.  Each pass requests
+// every word still pending, so a hop costs one L2 round trip per pass rather
+// than one per word.  On abort it returns with sh->abort set.
+template <int NW>
+__device__ __forceinline__ void gather(Ctx& c, const unsigned long long* src, int n, unsigned tag, float (&v)[NW]) {
+  unsigned pending = 0;
+#pragma unroll
+  for (int k = 0; k < NW; ++k) {
+    v[k] = 0.0f;
+    if (c.tid + k * CTHREADS < n) pending |= 1u << k;
+  }
+  for (unsigned it = 0; pending != 0; ++it) {
+    unsigned long long w[NW];
+#pragma unroll
+    for (int k = 0; k < NW; ++k) w[k] = (pending >> k) & 1u ? ld_word(src + c.tid + k * CTHREADS) : 0ull;
+#pragma unroll
+    for (int k = 0; k < NW; ++k)
+      if (((pending >> k) & 1u) && (unsigned)(w[k] >> 32) == tag) {
+        v[k] = __uint_as_float((unsigned)w[k]);
+        pending &= ~(1u << k);
+      }
+    if (pending == 0) break;
+    if (it >= 4096) __nanosleep(128);
+    if ((it & 1023) == 1023) {
+      if (c.sh()->abort || ld_flag(&c.A->ctrl->error)) {
+        c.sh()->abort = 1;
+        break;
+      }
+      if (it > kWaitLimit) {
+        raise_error(c.sh(), c.A->ctrl, kErrWaitData);
+        break;
+      }
+    }
+  }
+}
+
+// Per-32-block quantisation of K values held in gather's mapping into xq/xs
+// (TensorMath.QuantizeAvx.cs:145-150): d = amax / 127, inv = 1 / d.  A warp
+// first reduces the maxima of all its blocks; lane k then divides for block
+// k, so one division pair serves every block at once, and the lanes read the
+// scales back by shuffle.
+template <int NW>
+__device__ __forceinline__ void quant_regs(Ctx& c, const float (&y)[NW], int K) {
+  static_assert(NW <= 32, "one lane per block");
+  unsigned mb[NW];
+#pragma unroll
+  for (int k = 0; k < NW; ++k) mb[k] = __reduce_max_sync(0xffffffffu, __float_as_uint(y[k]) & 0x7fffffffu);
+  // mine = mb[lane] as register selects (an indexed read would go through local memory)
+  unsigned mine = 0;
+#pragma unroll
+  for (int k = 0; k < NW; ++k)
+    asm("{\n .reg .pred p;\n setp.eq.s32 p, %1, %2;\n selp.b32 %0, %3, %0, p;\n}\n"
+        : "+r"(mine)
+        : "r"(c.lane), "r"(k), "r"(mb[k]));
+  const float d = __fdiv_rn(__uint_as_float(mine), 127.0f);
+  const float id = d == 0.0f ? 0.0f : __fdiv_rn(1.0f, d);
+#pragma unroll
+  for (int k = 0; k < NW; ++k) {
+    const float dk = __shfl_sync(0xffffffffu, d, k), ik = __shfl_sync(0xffffffffu, id, k);
+    const int j = c.warp + k * CWARPS;
+    if (j < K / 32) {
+      c.xq()[xq_off(j) + c.lane] = (int8_t)quant1(y[k], ik);
+      if (c.lane == 0) c.xs()[j] = dk;
+    }
+  }
+}
+
+// RMSNorm(v) * gamma then quantisation (K = W), v in gather's mapping.  The
+// sum of squares runs over this thread's elements tid, tid + 480, ... in
+// order, then over the warps in order.  keep: optional shared copy of v.
+__device__ __forceinline__ void norm_quant(Ctx& c, const float (&v)[3], const Gamma& gamma, float eps, float* keep) {
+  double part = 0.0;
+#pragma unroll
+  for (int k = 0; k < 3; ++k)
+    if (c.tid + k * CTHREADS < W) {
+      const double z = (double)v[k];
+      part = __dadd_rn(part, __dmul_rn(z, z));
+      if (keep) keep[c.tid + k * CTHREADS] = v[k];
+    }
   part = warp_sum_d(part);
-  if (c.lane == 0) c.red[c.warp] = part;
+  if (c.lane == 0) c.red()[c.warp] = part;
   csync();
   double var = 0.0;
-  for (int w = 0; w < CWARPS; ++w) var = __dadd_rn(var, c.red[w]);
+  for (int w = 0; w < CWARPS; ++w) var = __dadd_rn(var, c.red()[w]);
   const float inv = rms_inverse(var, W, eps);
-  for (int j = c.warp; j < W / 32; j += CWARPS) {
-    const float y = __fmul_rn(__fmul_rn(v[j * 32 + c.lane], inv), gamma[j * 32 + c.lane]);
-    float d, id;
-    block_scale(y, d, id);
-    c.xq[j * 32 + c.lane] = (int8_t)quant1(y, id);
-    if (c.lane == 0) c.xs[j] = d;
-  }
+  float y[3];
+#pragma unroll
+  for (int k = 0; k < 3; ++k) y[k] = __fmul_rn(__fmul_rn(v[k], inv), gamma.g[k]);
+  quant_regs<3>(c, y, W);
   csync();
 }
 
-// Per-32-block quantisation of K values in shared memory.
-__device__ void quant_only(Ctx& c, const float* v, int K) {
-  for (int j = c.warp; j < K / 32; j += CWARPS) {
-    const float y = v[j * 32 + c.lane];
-    float d, id;
-    block_scale(y, d, id);
-    c.xq[j * 32 + c.lane] = (int8_t)quant1(y, id);
-    if (c.lane == 0) c.xs[j] = d;
-  }
-  csync();
-}
-
-// Loads n tagged words into dst (float), all consumer threads.
-__device__ void load_tagged(Ctx& c, const unsigned long long* src, int n, unsigned tag, float* dst) {
-  for (int i = c.tid; i < n; i += CTHREADS) {
-    float v;
-    if (!wait_word(src + i, tag, v, c.sh, c.A->ctrl)) break;
-    dst[i] = v;
-  }
-  csync();
-}
-
-// RMSNorm of one 128-wide head held by 4 warps (warp0..warp0+3) in place;
-// named barrier `bar` (128 threads).
-__device__ __forceinline__ void head_norm(Ctx& c, float* v, const float* gamma, float eps, int warp0, int bar) {
+// RMSNorm of one 128-wide head held by 4 warps (warp0..warp0+3) in place, g
+// this thread's norm weight; named barrier `bar` (128 threads).
+__device__ __forceinline__ void head_norm(Ctx& c, float* v, float g, float eps, int warp0, int bar) {
   const int i = c.tid - warp0 * 32;
   const float x = v[i];
   const double part = warp_sum_d(__dmul_rn((double)x, (double)x));
-  double* red = c.red + 4 * (bar - 2);
+  double* red = c.red() + 4 * (bar - 2);
   if (c.lane == 0) red[c.warp - warp0] = part;
   asm volatile("bar.sync %0, 128;" ::"r"(bar) : "memory");
   double var = 0.0;
   for (int w = 0; w < 4; ++w) var = __dadd_rn(var, red[w]);
   const float inv = rms_inverse(var, D, eps);
-  v[i] = __fmul_rn(__fmul_rn(x, inv), gamma[i]);
+  v[i] = __fmul_rn(__fmul_rn(x, inv), g);
   asm volatile("bar.sync %0, 128;" ::"r"(bar) : "memory");
 }
 
-// RoPE on one head in place (TensorMath.Rope.cs:51-53), same 128 threads.
-__device__ __forceinline__ void head_rope(Ctx& c, float* v, int pos, int warp0, int bar) {
+// RoPE on one head in place (TensorMath.Rope.cs:51-53), same 128 threads; co
+// and si are this thread's table entries at the position.
+__device__ __forceinline__ void head_rope(Ctx& c, float* v, float co, float si, int warp0, int bar) {
   const int i = c.tid - warp0 * 32, half = D / 2, k = i < half ? i : i - half;
-  const float co = c.A->rope_cos[(size_t)pos * half + k], si = c.A->rope_sin[(size_t)pos * half + k];
   const float a = v[k], b = v[k + half];
   const float o = i < half ? __fsub_rn(__fmul_rn(a, co), __fmul_rn(b, si)) : __fadd_rn(__fmul_rn(a, si), __fmul_rn(b, co));
   asm volatile("bar.sync %0, 128;" ::"r"(bar) : "memory");
@@ -488,49 +739,53 @@ __device__ __forceinline__ void head_rope(Ctx& c, float* v, int pos, int warp0, 
 // Exact paired-GQA attention of query head h = blockIdx.x at position pos
 // (TensorMath.DecoderAttention.cs:17-52 in the order of TensorMath.AttentionAvx.cs
 // and TensorMath.SoftmaxAvx.cs), K/V history from the chunk rings.
-__device__ void attention(Ctx& c, int layer, int pos, unsigned tag_in, unsigned tag_out) {
+// co/si: this thread's RoPE entries at pos (threads 0..255).
+__device__ void attention(Ctx& c, int layer, int pos, unsigned tag_in, unsigned tag_out, float co, float si) {
   const MegaArgs& A = *c.A;
   const int h = blockIdx.x, g = h >> 1;
+  // norm weight of this thread's q (warps 0..3) or k (warps 4..7) channel,
+  // requested before the wait for q/k/v
+  float gn = 0.0f;
+  if (c.warp < 8) gn = __ldg((c.warp < 4 ? A.layers[layer].q_norm : A.layers[layer].k_norm) + (c.tid & (D - 1)));
   for (int i = c.tid; i < 3 * D; i += CTHREADS) {
     const int src = i < D ? h * D + i : (i < 2 * D ? QW + g * D + (i - D) : QW + KVW + g * D + (i - 2 * D));
     float v;
-    if (!wait_word(A.qkv_t + src, tag_in, v, c.sh, A.ctrl)) break;
-    (i < D ? c.aq : (i < 2 * D ? c.ak : c.av))[i % D] = v;
+    if (!wait_word(A.qkv_t + src, tag_in, v, c.sh(), A.ctrl)) break;
+    (i < D ? c.aq() : (i < 2 * D ? c.ak() : c.av()))[i % D] = v;
   }
   csync();
-  if (c.trace && c.tid == 0) c.trace[8 * layer + 2] = global_ns();
-  if (c.sh->abort) return;
-  const MegaLayer& Lw = A.layers[layer];
+  if (c.trace && c.tid == 0) c.trace[kTraceLayerEvents * layer + 1] = global_ns();
+  if (c.sh()->abort) return;
   if (c.warp < 4) {  // q: RMSNorm + RoPE (QwenDecoder.cs:188,193)
-    head_norm(c, c.aq, Lw.q_norm, A.eps, 0, 2);
-    head_rope(c, c.aq, pos, 0, 2);
+    head_norm(c, c.aq(), gn, A.eps, 0, 2);
+    head_rope(c, c.aq(), co, si, 0, 2);
   } else if (c.warp < 8) {  // k: RMSNorm + RoPE (QwenDecoder.cs:191,194)
-    head_norm(c, c.ak, Lw.k_norm, A.eps, 4, 3);
-    head_rope(c, c.ak, pos, 4, 3);
+    head_norm(c, c.ak(), gn, A.eps, 4, 3);
+    head_rope(c, c.ak(), co, si, 4, 3);
   }
   csync();
   const size_t head_off = (((size_t)layer * KH + g) * A.capacity) * D;
   if (c.tid < D) {  // binary16 rounding of k and v (QwenDecoder.cs:199-200)
-    const __half kh = __float2half_rn(c.ak[c.tid]);
-    const __half vh = __float2half_rn(c.av[c.tid]);
+    const __half kh = __float2half_rn(c.ak()[c.tid]);
+    const __half vh = __float2half_rn(c.av()[c.tid]);
     if ((h & 1) == 0) {  // one CTA of the pair writes the cache row
       A.k_cache[head_off + (size_t)pos * D + (c.tid & 7) * (D / 8) + (c.tid >> 3)] = kh;
       A.v_cache[head_off + (size_t)pos * D + c.tid] = vh;
     }
-    c.ak[c.tid] = __half2float(kh);
-    c.av[c.tid] = __half2float(vh);
+    c.ak()[c.tid] = __half2float(kh);
+    c.av()[c.tid] = __half2float(vh);
   }
   csync();
-  if (c.trace && c.tid == 0) c.trace[8 * layer + 3] = global_ns();
+  if (c.trace && c.tid == 0) c.trace[kTraceLayerEvents * layer + 2] = global_ns();
   // Scores: one position per 8 threads, lane j sums channels j, j+8, ... in order.
   const int j = c.lane & 7, slot = c.tid >> 3;
   float qj[D / 8];
 #pragma unroll
-  for (int i = 0; i < D / 8; ++i) qj[i] = c.aq[j + 8 * i];
+  for (int i = 0; i < D / 8; ++i) qj[i] = c.aq()[j + 8 * i];
   const float divisor = __fsqrt_rn((float)D);
   const int chunks = (pos + CHUNK - 1) / CHUNK;
   for (int ch = 0; ch < chunks; ++ch) {
-    const uint8_t* kb = ring_acquire(c.kr, c.nk, c.sh, A.ctrl);
+    const uint8_t* kb = ring_acquire(ring_k(), c.nk, c.sh(), A.ctrl);
     if (kb == nullptr) return;
     const int t = ch * CHUNK + slot;
     float acc = 0.0f;
@@ -545,77 +800,92 @@ __device__ void attention(Ctx& c, int layer, int pos, unsigned tag_in, unsigned 
     acc = __fadd_rn(acc, __shfl_down_sync(0xffffffffu, acc, 4));
     acc = __fadd_rn(acc, __shfl_down_sync(0xffffffffu, acc, 1));
     acc = __fadd_rn(acc, __shfl_down_sync(0xffffffffu, acc, 2));
-    if (j == 0 && t < pos) c.sc[t] = __fdiv_rn(acc, divisor);
-    ring_release(c.kr, c.nk, c.lane);
+    if (j == 0 && t < pos) c.sc()[t] = __fdiv_rn(acc, divisor);
+    ring_release(ring_k(), c.nk, c.lane);
     ++c.nk;
   }
   if (c.warp == 0) {  // position pos from the fresh k
     float acc = 0.0f;
     if (slot == 0) {
 #pragma unroll
-      for (int i = 0; i < D / 8; ++i) acc = __fadd_rn(acc, __fmul_rn(qj[i], c.ak[j + 8 * i]));
+      for (int i = 0; i < D / 8; ++i) acc = __fadd_rn(acc, __fmul_rn(qj[i], c.ak()[j + 8 * i]));
     }
     acc = __fadd_rn(acc, __shfl_down_sync(0xffffffffu, acc, 4));
     acc = __fadd_rn(acc, __shfl_down_sync(0xffffffffu, acc, 1));
     acc = __fadd_rn(acc, __shfl_down_sync(0xffffffffu, acc, 2));
-    if (c.lane == 0) c.sc[pos] = __fdiv_rn(acc, divisor);
+    if (c.lane == 0) c.sc()[pos] = __fdiv_rn(acc, divisor);
   }
   csync();
-  if (c.trace && c.tid == 0) c.trace[8 * layer + 4] = global_ns();
+  if (c.trace && c.tid == 0) c.trace[kTraceLayerEvents * layer + 3] = global_ns();
   // Softmax (TensorMath.SoftmaxAvx.cs:11-58).
   const int len = pos + 1;
   float mx = -INFINITY;
-  for (int t = c.tid; t < len; t += CTHREADS) mx = fmaxf(mx, c.sc[t]);
+  for (int t = c.tid; t < len; t += CTHREADS) mx = fmaxf(mx, c.sc()[t]);
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-  float* redf = reinterpret_cast<float*>(c.red + 32);
+  float* redf = reinterpret_cast<float*>(c.red() + 32);
   if (c.lane == 0) redf[c.warp] = mx;
   csync();
   mx = redf[0];
   for (int w = 1; w < CWARPS; ++w) mx = fmaxf(mx, redf[w]);
-  for (int t = c.tid; t < len; t += CTHREADS) c.sc[t] = exp_ref(__fsub_rn(c.sc[t], mx));
+  for (int t = c.tid; t < len; t += CTHREADS) c.sc()[t] = exp_ref(__fsub_rn(c.sc()[t], mx));
   csync();
   const int full = len & ~7;
   if (c.tid < 8) {
     double acc = 0.0;
-    for (int t = c.tid; t < full; t += 8) acc = __dadd_rn(acc, (double)c.sc[t]);
-    c.red[48 + c.tid] = acc;
+    for (int t = c.tid; t < full; t += 8) acc = __dadd_rn(acc, (double)c.sc()[t]);
+    c.red()[48 + c.tid] = acc;
   }
   csync();
   if (c.tid == 0) {
-    const double s0 = __dadd_rn(c.red[48], c.red[52]), s1 = __dadd_rn(c.red[49], c.red[53]);
-    const double s2 = __dadd_rn(c.red[50], c.red[54]), s3 = __dadd_rn(c.red[51], c.red[55]);
+    const double s0 = __dadd_rn(c.red()[48], c.red()[52]), s1 = __dadd_rn(c.red()[49], c.red()[53]);
+    const double s2 = __dadd_rn(c.red()[50], c.red()[54]), s3 = __dadd_rn(c.red()[51], c.red()[55]);
     double sum = __dadd_rn(__dadd_rn(s0, s2), __dadd_rn(s1, s3));
-    for (int t = full; t < len; ++t) sum = __dadd_rn(sum, (double)c.sc[t]);
+    for (int t = full; t < len; ++t) sum = __dadd_rn(sum, (double)c.sc()[t]);
     redf[31] = __double2float_rn(__ddiv_rn(1.0, sum));
   }
   csync();
   const float inv = redf[31];
-  for (int t = c.tid; t < len; t += CTHREADS) c.sc[t] = __fmul_rn(c.sc[t], inv);
+  for (int t = c.tid; t < len; t += CTHREADS) c.sc()[t] = __fmul_rn(c.sc()[t], inv);
   csync();
-  if (c.trace && c.tid == 0) c.trace[8 * layer + 5] = global_ns();
+  if (c.trace && c.tid == 0) c.trace[kTraceLayerEvents * layer + 4] = global_ns();
   // V sum per channel in position order (TensorMath.AttentionAvx.cs:188-213): warps 0..3.
   if (c.warp < 4) {
     float acc = 0.0f;
     for (int ch = 0; ch < chunks; ++ch) {
-      const uint8_t* vb = ring_acquire(c.vr, c.nv, c.sh, A.ctrl);
+      const uint8_t* vb = ring_acquire(ring_v(), c.nv, c.sh(), A.ctrl);
       if (vb == nullptr) return;
       const __half* vv = reinterpret_cast<const __half*>(vb) + c.tid;
-      const int t0 = ch * CHUNK, n = min(CHUNK, pos - t0);
+      const float* pr = c.sc() + ch * CHUNK;
+      const int n = min(CHUNK, pos - ch * CHUNK);
+      // Software pipeline: the products of the next G positions are formed
+      // while the dependent adds of the current G run.
+      constexpr int G = 12;
       int t = 0;
-      for (; t + 8 <= n; t += 8) {
-        float v[8];
+      if (n >= G) {
+        float cur[G];
 #pragma unroll
-        for (int u = 0; u < 8; ++u) v[u] = __half2float(vv[(t + u) * D]);
+        for (int u = 0; u < G; ++u) cur[u] = __fmul_rn(__half2float(vv[u * D]), pr[u]);
+        for (t = G; t + G <= n; t += G) {
+          float nxt[G];
 #pragma unroll
-        for (int u = 0; u < 8; ++u) acc = __fadd_rn(acc, __fmul_rn(v[u], c.sc[t0 + t + u]));
+          for (int u = 0; u < G; ++u) nxt[u] = __fmul_rn(__half2float(vv[(t + u) * D]), pr[t + u]);
+#pragma unroll
+          for (int u = 0; u < G; ++u) acc = __fadd_rn(acc, cur[u]);
+#pragma unroll
+          for (int u = 0; u < G; ++u) cur[u] = nxt[u];
+        }
+#pragma unroll
+        for (int u = 0; u < G; ++u) acc = __fadd_rn(acc, cur[u]);
       }
-      for (; t < n; ++t) acc = __fadd_rn(acc, __fmul_rn(__half2float(vv[t * D]), c.sc[t0 + t]));
-      ring_release(c.vr, c.nv, c.lane);
+      for (; t < n; ++t) acc = __fadd_rn(acc, __fmul_rn(__half2float(vv[t * D]), pr[t]));
+      ring_release(ring_v(), c.nv, c.lane);
       ++c.nv;
     }
-    acc = __fadd_rn(acc, __fmul_rn(c.av[c.tid], c.sc[pos]));
-    st_word(A.attn_t + h * D + c.tid, pack(acc, tag_out));
+    acc = __fadd_rn(acc, __fmul_rn(c.av()[c.tid], c.sc()[pos]));
+    // The O projection's input quantisation of this head's four blocks
+    // (block 4h + warp), done once here instead of in every GEMV CTA.
+    publish_block(A.attn_t, QW, h * 4 + c.warp, acc, tag_out, c.lane);
   }
 }
 
@@ -627,13 +897,8 @@ __device__ void attention(Ctx& c, int layer, int pos, unsigned tag_in, unsigned 
   } while (0)
 
 __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(const MegaArgs A) {
-  extern __shared__ __align__(128) uint8_t smem[];
-  const Layout L = layout(A.capacity);
-  Shared* sh = reinterpret_cast<Shared*>(smem + L.shared);
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L.bars);
-  const Ring wr{smem + L.ring, bars, bars + WSLOTS, WSLOTS, WSLOT, 0};
-  const Ring kr{smem + L.ring, bars + 12, bars + 12 + KSLOTS, KSLOTS, CSLOT, 1};
-  const Ring vr{smem + L.ring + KSLOTS * CSLOT, bars + 24, bars + 24 + VSLOTS, VSLOTS, CSLOT, 2};
+  Shared* sh = sm<Shared>(kOffShared);
+  const Ring wr = ring_w(), kr = ring_k(), vr = ring_v();
   const bool att = blockIdx.x < ATT_CTAS;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   if (tid == 0) {
@@ -669,31 +934,30 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(const Mega
 
   Ctx c;
   c.A = &A;
-  c.sh = sh;
-  c.wr = wr;
-  c.kr = kr;
-  c.vr = vr;
   c.nw = c.nk = c.nv = 0;
   c.trace = nullptr;
-  c.xq = reinterpret_cast<int8_t*>(smem + L.xq);
-  c.xs = reinterpret_cast<float*>(smem + L.xs);
-  c.xres = reinterpret_cast<float*>(smem + L.xres);
-  c.ares = reinterpret_cast<float*>(smem + L.ares);
-  c.vin = reinterpret_cast<float*>(smem + L.vin);
-  c.prod = reinterpret_cast<float*>(smem + L.prod);
-  c.aq = reinterpret_cast<float*>(smem + L.att_q);
-  c.ak = reinterpret_cast<float*>(smem + L.att_k);
-  c.av = reinterpret_cast<float*>(smem + L.att_v);
-  c.sc = reinterpret_cast<float*>(smem + L.sc);
-  c.red = reinterpret_cast<double*>(smem + L.red);
   c.tid = tid;
   c.warp = warp;
   c.lane = lane;
-  const int n_gemv = gridDim.x - ATT_CTAS;
-  const Spans sp = spans(att ? 0 : blockIdx.x - ATT_CTAS, n_gemv, A.vocab / 8);
+  if (tid == 0) sh->sp = spans(att ? 0 : blockIdx.x - ATT_CTAS, gridDim.x - ATT_CTAS, A.vocab / 8);
+  csync();
+  const Spans& sp = sh->sp;
   int token = ctrl->token;
   int steps = 0;
   bool stopped = false;
+
+  // RMSNorm weights are requested ahead of the waits that precede their use;
+  // layer 0's attn_norm and the output norm stay in shared memory for the launch.
+  Gamma g_attn{}, g_ffn{};
+  float* s_first = sm<float>(kOffGFirst);
+  float* s_out = sm<float>(kOffGOut);
+  if (!att) {
+    for (int k = tid; k < W; k += CTHREADS) {
+      s_first[k] = __ldg(A.layers[0].attn_norm + k);
+      s_out[k] = __ldg(A.out_norm + k);
+    }
+    csync();
+  }
 
   for (int step = 0; step < A.max_steps; ++step) {
     // FunAsr.Transcribe (FunAsr.cs:169-176): stop before an end token, else record it.
@@ -706,10 +970,20 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(const Mega
       }
       if (blockIdx.x == 0 && tid == 0 && step < A.log_cap) A.log[step] = token;
     }
-    if (tid == 0) sh->go = step + 1;
+    if (tid == 0) {
+      // The producer's TMA reads of the KV history follow its read of `go`:
+      // this fence orders the partial exchange's acquires before the flag.
+      __threadfence();
+      sh->go = step + 1;
+    }
     const int pos = pos0 + step;
     const unsigned tbase = epoch + (unsigned)step * tps;
     c.trace = (A.trace != nullptr && step == 0) ? A.trace + (size_t)blockIdx.x * kTraceEvents : nullptr;
+    float rope_co = 0.0f, rope_si = 0.0f;  // this thread's RoPE entries at pos (q and k threads)
+    if (att && tid < 2 * D) {
+      rope_co = __ldg(A.rope_cos + (size_t)pos * (D / 2) + (tid & (D / 2 - 1)));
+      rope_si = __ldg(A.rope_sin + (size_t)pos * (D / 2) + (tid & (D / 2 - 1)));
+    }
     if (!att) {  // Embed (Weight.CopyRow, Gguf.cs:340-344): each GEMV CTA builds the row itself
       if (tid < W / 16) {
         const int r = token & 7;
@@ -718,111 +992,152 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(const Mega
         const float s = __half2float(reinterpret_cast<const __half*>(tile + 8 * W)[(tid >> 1) * 8 + r]);
         const int8_t* qb = reinterpret_cast<const int8_t*>(&q);
 #pragma unroll
-        for (int i = 0; i < 16; ++i) c.xres[tid * 16 + i] = __fmul_rn((float)qb[i], s);
+        for (int i = 0; i < 16; ++i) c.xres()[tid * 16 + i] = __fmul_rn((float)qb[i], s);
       }
       csync();
     }
     for (int layer = 0; layer < A.n_layers; ++layer) {
       const unsigned tl = tbase + (unsigned)(layer * 8);
+      const int ev = kTraceLayerEvents * layer;
       if (att) {
-        MEGA_TRACE(8 * layer + 0);
-        attention(c, layer, pos, tl + kTagQkv, tl + kTagAttn);
+        MEGA_TRACE(ev + 0);
+        attention(c, layer, pos, tl + kTagQkv, tl + kTagAttn, rope_co, rope_si);
         csync();
-        MEGA_TRACE(8 * layer + 1);
+        MEGA_TRACE(ev + 5);
         if (sh->abort) goto drain;
         continue;
       }
-      const MegaLayer& Lw = A.layers[layer];
+      g_ffn = load_gamma(c, A.layers[layer].ffn_norm);  // used after the attention round trip
+      if (layer == 0) g_attn = load_gamma(c, s_first);
       // ---- Q: x -> RMSNorm -> quantise -> q/k/v rows ----
-      if (layer > 0) load_tagged(c, A.x_t, W, tl - 8 + kTagX, c.xres);
-      if (sh->abort) goto drain;
-      MEGA_TRACE(8 * layer + 0);
-      norm_quant(c, c.xres, Lw.attn_norm, A.eps);
-      for (int t = 0; t < sp.qn; t += 3) piece_products(c, min(3, sp.qn - t), W, TB_W, t);
-      csync();
-      if (sh->abort) goto drain;
-      if (tid < sp.qn * 8) {
-        const float v = row_sum(c.prod, tid >> 3, tid & 7, W / 32);
-        st_word(A.qkv_t + (sp.q0 * 8 + tid), pack(v, tl + kTagQkv));
+      {
+        float v[3];
+        if (layer > 0) {
+          gather<3>(c, A.x_t, W, tl - 8 + kTagX, v);
+        } else {  // the embedding row this CTA built
+#pragma unroll
+          for (int k = 0; k < 3; ++k) v[k] = c.tid + k * CTHREADS < W ? c.xres()[c.tid + k * CTHREADS] : 0.0f;
+        }
+        MEGA_TRACE(ev + 0);
+        norm_quant(c, v, g_attn, A.eps, layer > 0 ? c.xres() : nullptr);
       }
-      MEGA_TRACE(8 * layer + 1);
-      // ---- O: attention output -> quantise -> o + x ----
+      if (sh->abort) goto drain;
+      MEGA_TRACE(ev + 1);
+      {
+        const unsigned tag = tl + kTagQkv;
+        const int q0 = sp.q0;
+        if (!w8a8_phase<W>(c, sp.qn, 3, [&](int t, int r, float v) { st_word(A.qkv_t + (q0 + t) * 8 + r, pack(v, tag)); }))
+          goto drain;
+      }
+      MEGA_TRACE(ev + 3);
+      // ---- O: quantised attention output -> o + x ----
       if (sp.on > 0) {
-        load_tagged(c, A.attn_t, QW, tl + kTagAttn, c.vin);
+        gather_q8(c, A.attn_t, QW, tl + kTagAttn);
         if (sh->abort) goto drain;
-        MEGA_TRACE(8 * layer + 2);
-        quant_only(c, c.vin, QW);
-        for (int t = 0; t < sp.on; ++t) piece_products(c, 1, QW, TB_Q, t);
-        csync();
-        if (sh->abort) goto drain;
-        if (tid < sp.on * 8) {
-          const int row = sp.o0 * 8 + tid;
-          const float v = __fadd_rn(row_sum(c.prod, tid >> 3, tid & 7, QW / 32), c.xres[row]);
-          st_word(A.a_t + row, pack(v, tl + kTagA));
+        MEGA_TRACE(ev + 4);
+        const unsigned tag = tl + kTagA;
+        const int o0 = sp.o0;
+        if (!w8a8_phase<QW>(c, sp.on, 1, [&](int t, int r, float v) {
+              const int row = (o0 + t) * 8 + r;
+              st_word(A.a_t + row, pack(__fadd_rn(v, c.xres()[row]), tag));
+            }))
+          goto drain;
+        MEGA_TRACE(ev + 7);
+      }
+      // ---- GU: a -> RMSNorm -> quantise -> SiLU(gate) * up -> quantised act ----
+      {
+        float v[3];
+        gather<3>(c, A.a_t, W, tl + kTagA, v);
+        MEGA_TRACE(ev + 8);
+        if (sp.gbn > 0) {
+          norm_quant(c, v, g_ffn, A.eps, c.ares());
+        } else {  // no gate/up block here: keep a for the down projection's residual
+#pragma unroll
+          for (int k = 0; k < 3; ++k)
+            if (tid + k * CTHREADS < W) c.ares()[tid + k * CTHREADS] = v[k];
+          csync();
         }
-        MEGA_TRACE(8 * layer + 3);
       }
-      // ---- GU: a -> RMSNorm -> quantise -> SiLU(gate) * up ----
-      load_tagged(c, A.a_t, W, tl + kTagA, c.ares);
       if (sh->abort) goto drain;
-      MEGA_TRACE(8 * layer + 4);
-      norm_quant(c, c.ares, Lw.ffn_norm, A.eps);
-      for (int t = 0; t < sp.gun; ++t) piece_products(c, 2, W, TB_W, 2 * t);
-      csync();
-      if (sh->abort) goto drain;
-      if (tid < sp.gun * 8) {
-        const int p = tid >> 3, r = tid & 7;
-        const float gg = row_sum(c.prod, 2 * p, r, W / 32), u = row_sum(c.prod, 2 * p + 1, r, W / 32);
-        st_word(A.act_t + (sp.gu0 + p) * 8 + r, pack(silu_mul1(gg, u), tl + kTagAct));
+      MEGA_TRACE(ev + 9);
+      for (int bj = 0; bj < sp.gbn; ++bj) {
+        if (!w8a8_phase<W>(c, 8, 2, [&](int t, int r, float v) { c.part()[t * 8 + r] = v; })) goto drain;
+        if (warp == 0) {  // lane = 8 * pair + row: the block's 32 SiLU(gate) * up values
+          const float act = silu_mul1(c.part()[(lane >> 3) * 16 + (lane & 7)], c.part()[(lane >> 3) * 16 + 8 + (lane & 7)]);
+          publish_block(A.act_t, FFN, sp.gb0 + bj, act, tl + kTagAct, lane);
+        }
+        csync();  // part is rewritten by the next block
       }
-      MEGA_TRACE(8 * layer + 5);
-      // ---- D: act -> quantise -> down + a ----
+      MEGA_TRACE(ev + 11);
+      if (layer + 1 < A.n_layers) g_attn = load_gamma(c, A.layers[layer + 1].attn_norm);
+      // ---- D: quantised act -> down + a ----
       if (sp.dn > 0) {
-        load_tagged(c, A.act_t, FFN, tl + kTagAct, c.vin);
+        gather_q8(c, A.act_t, FFN, tl + kTagAct);
         if (sh->abort) goto drain;
-        MEGA_TRACE(8 * layer + 6);
-        quant_only(c, c.vin, FFN);
-        for (int t = 0; t < sp.dn; ++t) piece_products(c, 1, FFN, TB_F, t);
-        csync();
-        if (sh->abort) goto drain;
-        if (tid < sp.dn * 8) {
-          const int row = sp.d0 * 8 + tid;
-          const float v = __fadd_rn(row_sum(c.prod, tid >> 3, tid & 7, FFN / 32), c.ares[row]);
-          st_word(A.x_t + row, pack(v, tl + kTagX));
-        }
-        MEGA_TRACE(8 * layer + 7);
+        MEGA_TRACE(ev + 12);
+        const unsigned tag = tl + kTagX;
+        const int d0 = sp.d0;
+        if (!w8a8_phase<FFN>(c, sp.dn, 1, [&](int t, int r, float v) {
+              const int row = (d0 + t) * 8 + r;
+              st_word(A.x_t + row, pack(__fadd_rn(v, c.ares()[row]), tag));
+            }))
+          goto drain;
+        MEGA_TRACE(ev + 15);
       }
     }
     {
       // ---- LM: final RMSNorm, lm_head rows, argmax (QwenDecoder.cs:262-268,278-326) ----
       const unsigned tlm = tbase + (unsigned)(A.n_layers * 8);
+      const int ev = kTraceLayerEvents * A.n_layers;
       float best_v = __int_as_float(0x7fc00000);
       int best_i = INT_MAX;
       bool row0_nan = false;
       if (!att) {
-        load_tagged(c, A.x_t, W, tlm - 8 + kTagX, c.xres);
+        {
+          float v[3];
+          gather<3>(c, A.x_t, W, tlm - 8 + kTagX, v);
+          MEGA_TRACE(ev + 0);
+          norm_quant(c, v, load_gamma(c, s_out), A.eps, nullptr);
+        }
         if (sh->abort) goto drain;
-        MEGA_TRACE(8 * A.n_layers + 0);
-        norm_quant(c, c.xres, A.out_norm, A.eps);
-        int buf = 0;
-        for (int t = 0; t < sp.lmn; t += 3, buf ^= 1) {
-          const int n = min(3, sp.lmn - t);
-          piece_products(c, n, W, TB_W, buf * 3);
-          csync();
-          if (sh->abort) goto drain;
-          if (tid < n * 8) {
-            const int row = (sp.lm0 + t) * 8 + tid;
-            const float v = row_sum(c.prod, buf * 3 + (tid >> 3), tid & 7, W / 32);
-            if (A.logits) A.logits[row] = v;
-            if (row == 0) row0_nan = isnan(v);
-            if (better(v, row, best_v, best_i)) {
-              best_v = v;
-              best_i = row;
+        MEGA_TRACE(ev + 1);
+        // Rounds of 15 tiles (5 ring pieces of 3 tiles), one tile per warp,
+        // closed by a barrier: the pieces in use at any time are those of one
+        // round, so no two share a ring slot.  Each warp releases its tile's
+        // share of a piece (arrival counts summing to 15) as soon as it is done.
+        const int r = lane & 7, g = lane >> 3;
+        for (int T0 = 0; T0 < sp.lmn; T0 += CWARPS) {
+          const int T = T0 + warp;
+          bool failed = false;
+          if (T < sp.lmn) {
+            const int piece = T / 3, off = T - piece * 3, nt = min(3, sp.lmn - piece * 3);
+            const uint8_t* base = ring_acquire(ring_w(), c.nw + piece, sh, ctrl);
+            failed = base == nullptr;
+            if (!failed) {
+              float p[8];
+              row_products<W>(base + (size_t)off * TB_W, c.xq(), c.xs(), r, g * 8, p);
+              const float v = chain_groups(p, g, 0.0f);
+              __syncwarp();
+              if (lane == 0)
+                mbar_arrive_count(&ring_w().empty[(c.nw + piece) % WSLOTS],
+                                  nt == 3 ? 5u : (nt == 2 ? (off == 0 ? 8u : 7u) : 15u));
+              if (g == 3) {
+                const int row = (sp.lm0 + T) * 8 + r;
+                if (A.logits) A.logits[row] = v;
+                if (row == 0) row0_nan = isnan(v);
+                if (better(v, row, best_v, best_i)) {
+                  best_v = v;
+                  best_i = row;
+                }
+              }
             }
           }
+          if (csync_or(failed)) goto drain;
         }
+        c.nw += (sp.lmn + 2) / 3;
+        MEGA_TRACE(ev + 2);
       }
-      if (warp == 0) {  // CTA argmax (threads 0..23 hold the candidates)
+      {  // CTA argmax: within each warp, then across the warps
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) {
           const float ov = __shfl_xor_sync(0xffffffffu, best_v, o);
@@ -834,16 +1149,30 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(const Mega
         }
         const bool nan0 = __any_sync(0xffffffffu, row0_nan);
         if (lane == 0) {
-          sh->best_v[0] = best_v;
-          sh->best_i[0] = nan0 ? -2 : best_i;
+          sh->best_v[warp] = best_v;
+          sh->best_i[warp] = nan0 ? -2 : best_i;
+        }
+        csync();
+        if (tid == 0) {
+          float bv = __int_as_float(0x7fc00000);
+          int bi = INT_MAX;
+          bool f0 = false;
+          for (int w = 0; w < CWARPS; ++w) {
+            if (sh->best_i[w] == -2) f0 = true;
+            else if (better(sh->best_v[w], sh->best_i[w], bv, bi)) {
+              bv = sh->best_v[w];
+              bi = sh->best_i[w];
+            }
+          }
+          sh->best_v[0] = bv;
+          sh->best_i[0] = f0 ? -2 : bi;
         }
       }
       csync();
-      MEGA_TRACE(8 * A.n_layers + 1);
-      if (tid == 0) {
-        __threadfence();  // release this step's KV rows before the partials
-        st_word(A.part_v + blockIdx.x, pack(sh->best_v[0], tlm + kTagPart));
-        st_word(A.part_i + blockIdx.x, pack(__int_as_float(sh->best_i[0]), tlm + kTagPart));
+      MEGA_TRACE(ev + 3);
+      if (tid == 0) {  // release: this CTA's KV rows (ordered by the barrier above) precede the partials
+        st_word_release(A.part_v + blockIdx.x, pack(sh->best_v[0], tlm + kTagPart));
+        st_word_release(A.part_i + blockIdx.x, pack(__int_as_float(sh->best_i[0]), tlm + kTagPart));
       }
       // every CTA reduces every partial: the same token everywhere
       float pv = __int_as_float(0x7fc00000);
@@ -851,8 +1180,9 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(const Mega
       bool force0 = false;
       for (int i = tid; i < (int)gridDim.x; i += CTHREADS) {
         float v, vi;
-        if (!wait_word(A.part_v + i, tlm + kTagPart, v, sh, ctrl)) break;
-        if (!wait_word(A.part_i + i, tlm + kTagPart, vi, sh, ctrl)) break;
+        // acquire: the next step's KV reads see every CTA's rows
+        if (!wait_word<true>(A.part_v + i, tlm + kTagPart, v, sh, ctrl)) break;
+        if (!wait_word<true>(A.part_i + i, tlm + kTagPart, vi, sh, ctrl)) break;
         const int idx = __float_as_int(vi);
         if (idx == -2) force0 = true;
         if (better(v, idx, pv, pi)) {
@@ -860,7 +1190,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(const Mega
           pi = idx;
         }
       }
-      __threadfence();  // acquire: later KV reads see every CTA's rows
+      MEGA_TRACE(ev + 5);
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) {
         const float ov = __shfl_xor_sync(0xffffffffu, pv, o);
@@ -891,7 +1221,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(const Mega
         sh->token = (f0 || bi == INT_MAX || bi < 0) ? 0 : bi;
       }
       csync();
-      MEGA_TRACE(8 * A.n_layers + 2);
+      MEGA_TRACE(ev + 4);
       token = sh->token;
       ++steps;
     }
@@ -926,7 +1256,7 @@ drain:
 
 }  // namespace
 
-int mega_smem_bytes(int capacity) { return layout(capacity).total; }
+int mega_smem_bytes(int capacity) { return smem_total(capacity); }
 
 int mega_grid(int device, int capacity) {
   const int smem = mega_smem_bytes(capacity);

@@ -62,13 +62,17 @@ struct MegaArgs {
   int* log = nullptr;
   int log_cap = 0;
   // Optional phase timestamps of the first step (%globaltimer, ns):
-  // trace[cta * kTraceEvents + event]; events per layer l: 8*l + {0 inputs
-  // ready, 1 Q/A done, 2 O inputs ready, 3 O done, 4 GU inputs ready,
-  // 5 GU done, 6 D inputs ready, 7 D done}; then LM inputs ready, LM done,
-  // token known.
+  // trace[cta * kTraceEvents + event].  Events of layer l are 16*l + e.
+  // GEMV CTAs: per phase p (0 Q, 1 O, 2 GU, 3 D) e = 4p + {0 inputs ready,
+  // 1 activations quantised, 2 block products done, 3 outputs stored}.
+  // Attention CTAs: e = {0 layer start, 1 q/k/v loaded, 2 norm + RoPE + KV
+  // write, 3 scores, 4 softmax, 5 output stored}.  Then 16*layers + {0 LM
+  // inputs ready, 1 quantised, 2 lm_head rows done, 3 partials published,
+  // 4 token known, 5 all partials read}.
   unsigned long long* trace = nullptr;
 };
-constexpr int kTraceEvents = 8 * 28 + 8;
+constexpr int kTraceLayerEvents = 16;
+constexpr int kTraceEvents = kTraceLayerEvents * 28 + 8;
 
 // Model shape the kernel is compiled for: hidden 1024, 16 query heads and 8 KV
 // heads of 128, FFN 3072 (Qwen3-0.6B).

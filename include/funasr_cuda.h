@@ -185,9 +185,13 @@ int fa_session_uses_persistent_kernel(const fa_session* session);
 int fa_session_set_persistent_kernel(fa_session* session, int on);
 /* Profiling hook of the persistent kernel: when on, each launch records
  * %globaltimer stamps (ns) of its first step's phases per CTA; get_trace copies
- * [grid x events] stamps (events per layer l: 8l + {0 inputs ready, 1 Q or
- * attention done, 2 O inputs, 3 O done, 4 GU inputs, 5 GU done, 6 D inputs,
- * 7 D done}, then LM inputs, LM done, token known) and returns grid*events. */
+ * [grid x events] stamps and returns grid*events.  Layer l owns events
+ * 16l + e.  GEMV CTAs: for phase p (0 q/k/v, 1 o, 2 gate/up, 3 down)
+ * e = 4p + {0 inputs ready, 1 activations quantised, 2 block products done,
+ * 3 outputs stored}.  Attention CTAs: e = {0 layer start, 1 q/k/v loaded,
+ * 2 norm + RoPE + KV write, 3 scores, 4 softmax, 5 output stored}.  After the
+ * layers: {0 lm_head inputs ready, 1 quantised, 2 rows done, 3 partials
+ * published, 4 token known, 5 all partials read}. */
 int fa_session_set_trace(fa_session* session, int on);
 int fa_session_get_trace(fa_session* session, uint64_t* out, int capacity);
 /* Number of kernel launches one generate iteration replays (kernel nodes of
