@@ -75,6 +75,7 @@ struct Spans {
 };
 
 struct Shared {
+  MegaArgs args;            // the launch arguments (functions reach them through Ctx)
   Spans sp;                 // this CTA's GEMV spans (kept here, not in registers)
   volatile int quit;        // consumers stop the producer
   volatile int go;          // steps the consumers have committed to
@@ -96,8 +97,9 @@ constexpr int kOffXq = align_up(kOffBars + 32 * 8, 16);            // quantised 
 constexpr int kOffXs = align_up(kOffXq + FFN + FFN / 256 * 16, 16); // their block scales
 constexpr int kOffXres = align_up(kOffXs + FFN / 32 * 4, 16);      // x (residual of O)
 constexpr int kOffAres = kOffXres + W * 4;                         // a (residual of D)
-constexpr int kOffGFirst = kOffAres + W * 4;                       // layer 0 attn_norm
-constexpr int kOffGOut = kOffGFirst + W * 4;                       // output norm
+constexpr int kOffGAttn = kOffAres + W * 4;                        // attn_norm of the coming Q phase
+constexpr int kOffGFfn = kOffGAttn + W * 4;                        // ffn_norm of the coming GU phase
+constexpr int kOffGOut = kOffGFfn + W * 4;                         // output norm
 constexpr int kOffPart = kOffGOut + W * 4;                         // row sums crossing warps [32 x 8]
 constexpr int kOffAttQ = kOffPart + 32 * 8 * 4;
 constexpr int kOffAttK = kOffAttQ + D * 4;
@@ -298,8 +300,9 @@ __device__ bool ring_issue(const Ring& r, int& n, const void* src, unsigned byte
 __device__ const uint8_t* ring_acquire(const Ring& r, int n, Shared* sh, MegaCtrl* ctrl) {
   const int slot = n % r.nslot;
   const unsigned parity = (unsigned)((n / r.nslot) & 1);
-  bool ok = false;
-  for (unsigned it = 0;; ++it) {
+  // A non-blocking probe first; try_wait may suspend the thread for a while.
+  bool ok = mbar_test_wait(&r.full[slot], parity);
+  for (unsigned it = 0; !ok; ++it) {
     if (mbar_try_wait(&r.full[slot], parity)) {
       ok = true;
       break;
@@ -318,6 +321,17 @@ __device__ const uint8_t* ring_acquire(const Ring& r, int n, Shared* sh, MegaCtr
 __device__ __forceinline__ void ring_release(const Ring& r, int n, int lane) {
   __syncwarp();
   if (lane == 0) mbar_arrive(&r.empty[n % r.nslot]);
+}
+
+// Whole warps: waits for copies n0 .. n0 + count - 1 (count <= nslot) with the
+// probes of all their slots in flight together; false when the kernel aborts.
+__device__ bool ring_acquire_all(const Ring& r, int n0, int count, Shared* sh, MegaCtrl* ctrl) {
+  bool ok = true;
+  for (int i = 0; i < count; ++i) ok &= mbar_test_wait(&r.full[(n0 + i) % r.nslot], (unsigned)(((n0 + i) / r.nslot) & 1));
+  if (__all_sync(0xffffffffu, ok)) return true;
+  for (int i = 0; i < count; ++i)
+    if (ring_acquire(r, n0 + i, sh, ctrl) == nullptr) return false;
+  return true;
 }
 
 // Waits (bounded) for every copy a ring issued to land: no TMA write may be in
@@ -534,8 +548,7 @@ template <int K, typename Epi>
 __device__ __forceinline__ bool w8a8_phase(Ctx& c, int nt, int per, Epi epi) {
   constexpr int NS = K / 1024, TB = 8 * K + (K / 32) * 16;
   const int np = (nt + per - 1) / per;
-  bool failed = false;
-  for (int p = 0; p < np && !failed; ++p) failed = ring_acquire(ring_w(), c.nw + p, c.sh(), c.A->ctrl) == nullptr;
+  const bool failed = !ring_acquire_all(ring_w(), c.nw, np, c.sh(), c.A->ctrl);
   // Every warp takes the same branch: the jobs below wait on each other at
   // named barriers, which have no time limit.  (On failure the drain waits
   // for the copies in flight.)
@@ -736,11 +749,31 @@ __device__ __forceinline__ void head_rope(Ctx& c, float* v, float co, float si, 
   v[i] = o;
 }
 
+// Products p_t * v_t of 12 consecutive positions of one channel (weights
+// 16-byte aligned, the channel's column at stride D halves), and their
+// ordered sum into acc.
+__device__ __forceinline__ void vprod12(const __half* vv, const float* pr, int t, float (&x)[12]) {
+#pragma unroll
+  for (int q = 0; q < 3; ++q) {
+    const float4 p = *reinterpret_cast<const float4*>(pr + t + 4 * q);
+    x[4 * q + 0] = __fmul_rn(__half2float(vv[(t + 4 * q + 0) * D]), p.x);
+    x[4 * q + 1] = __fmul_rn(__half2float(vv[(t + 4 * q + 1) * D]), p.y);
+    x[4 * q + 2] = __fmul_rn(__half2float(vv[(t + 4 * q + 2) * D]), p.z);
+    x[4 * q + 3] = __fmul_rn(__half2float(vv[(t + 4 * q + 3) * D]), p.w);
+  }
+}
+__device__ __forceinline__ void add12(float& acc, const float (&x)[12]) {
+#pragma unroll
+  for (int u = 0; u < 12; ++u) acc = __fadd_rn(acc, x[u]);
+}
+
 // Exact paired-GQA attention of query head h = blockIdx.x at position pos
 // (TensorMath.DecoderAttention.cs:17-52 in the order of TensorMath.AttentionAvx.cs
 // and TensorMath.SoftmaxAvx.cs), K/V history from the chunk rings.
 // co/si: this thread's RoPE entries at pos (threads 0..255).
-__device__ void attention(Ctx& c, int layer, int pos, unsigned tag_in, unsigned tag_out, float co, float si) {
+// Kept out of line (its registers are its own); returns the updated K and V
+// ring counts.
+__device__ __noinline__ int2 attention(Ctx c, int layer, int pos, unsigned tag_in, unsigned tag_out, float co, float si) {
   const MegaArgs& A = *c.A;
   const int h = blockIdx.x, g = h >> 1;
   // norm weight of this thread's q (warps 0..3) or k (warps 4..7) channel,
@@ -755,7 +788,7 @@ __device__ void attention(Ctx& c, int layer, int pos, unsigned tag_in, unsigned 
   }
   csync();
   if (c.trace && c.tid == 0) c.trace[kTraceLayerEvents * layer + 1] = global_ns();
-  if (c.sh()->abort) return;
+  if (c.sh()->abort) return make_int2(c.nk, c.nv);
   if (c.warp < 4) {  // q: RMSNorm + RoPE (QwenDecoder.cs:188,193)
     head_norm(c, c.aq(), gn, A.eps, 0, 2);
     head_rope(c, c.aq(), co, si, 0, 2);
@@ -782,25 +815,29 @@ __device__ void attention(Ctx& c, int layer, int pos, unsigned tag_in, unsigned 
   float qj[D / 8];
 #pragma unroll
   for (int i = 0; i < D / 8; ++i) qj[i] = c.aq()[j + 8 * i];
-  const float divisor = __fsqrt_rn((float)D);
   const int chunks = (pos + CHUNK - 1) / CHUNK;
   for (int ch = 0; ch < chunks; ++ch) {
     const uint8_t* kb = ring_acquire(ring_k(), c.nk, c.sh(), A.ctrl);
-    if (kb == nullptr) return;
+    if (kb == nullptr) return make_int2(c.nk, c.nv);
     const int t = ch * CHUNK + slot;
     float acc = 0.0f;
     if (t < pos) {
-      const uint4* kr = reinterpret_cast<const uint4*>(kb + (size_t)slot * D * 2 + j * (D / 8) * 2);
-      const uint4 ka = kr[0], kc = kr[1];
-      const __half* k0 = reinterpret_cast<const __half*>(&ka);
-      const __half* k1 = reinterpret_cast<const __half*>(&kc);
+      // lane j's channels j, j+8, ... are contiguous in the lane-permuted row
+      const __half2* kr = reinterpret_cast<const __half2*>(kb + (size_t)slot * D * 2 + j * (D / 8) * 2);
+      __half2 kh[D / 16];
 #pragma unroll
-      for (int i = 0; i < D / 8; ++i) acc = __fadd_rn(acc, __fmul_rn(qj[i], __half2float(i < 8 ? k0[i] : k1[i - 8])));
+      for (int i = 0; i < D / 16; ++i) kh[i] = kr[i];
+#pragma unroll
+      for (int i = 0; i < D / 16; ++i) {
+        const float2 kv = __half22float2(kh[i]);
+        acc = __fadd_rn(acc, __fmul_rn(qj[2 * i], kv.x));
+        acc = __fadd_rn(acc, __fmul_rn(qj[2 * i + 1], kv.y));
+      }
     }
     acc = __fadd_rn(acc, __shfl_down_sync(0xffffffffu, acc, 4));
     acc = __fadd_rn(acc, __shfl_down_sync(0xffffffffu, acc, 1));
     acc = __fadd_rn(acc, __shfl_down_sync(0xffffffffu, acc, 2));
-    if (j == 0 && t < pos) c.sc()[t] = __fdiv_rn(acc, divisor);
+    if (j == 0 && t < pos) c.sc()[t] = acc;  // raw dot: divided by sqrt(D) in the softmax pass
     ring_release(ring_k(), c.nk, c.lane);
     ++c.nk;
   }
@@ -813,14 +850,19 @@ __device__ void attention(Ctx& c, int layer, int pos, unsigned tag_in, unsigned 
     acc = __fadd_rn(acc, __shfl_down_sync(0xffffffffu, acc, 4));
     acc = __fadd_rn(acc, __shfl_down_sync(0xffffffffu, acc, 1));
     acc = __fadd_rn(acc, __shfl_down_sync(0xffffffffu, acc, 2));
-    if (c.lane == 0) c.sc()[pos] = __fdiv_rn(acc, divisor);
+    if (c.lane == 0) c.sc()[pos] = acc;
   }
   csync();
   if (c.trace && c.tid == 0) c.trace[kTraceLayerEvents * layer + 3] = global_ns();
   // Softmax (TensorMath.SoftmaxAvx.cs:11-58).
   const int len = pos + 1;
+  const float divisor = __fsqrt_rn((float)D);
   float mx = -INFINITY;
-  for (int t = c.tid; t < len; t += CTHREADS) mx = fmaxf(mx, c.sc()[t]);
+  for (int t = c.tid; t < len; t += CTHREADS) {  // scores = dot / sqrt(D), then the max
+    const float sv = __fdiv_rn(c.sc()[t], divisor);
+    c.sc()[t] = sv;
+    mx = fmaxf(mx, sv);
+  }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
   float* redf = reinterpret_cast<float*>(c.red() + 32);
@@ -854,31 +896,27 @@ __device__ void attention(Ctx& c, int layer, int pos, unsigned tag_in, unsigned 
     float acc = 0.0f;
     for (int ch = 0; ch < chunks; ++ch) {
       const uint8_t* vb = ring_acquire(ring_v(), c.nv, c.sh(), A.ctrl);
-      if (vb == nullptr) return;
+      if (vb == nullptr) return make_int2(c.nk, c.nv);
       const __half* vv = reinterpret_cast<const __half*>(vb) + c.tid;
       const float* pr = c.sc() + ch * CHUNK;
       const int n = min(CHUNK, pos - ch * CHUNK);
-      // Software pipeline: the products of the next G positions are formed
-      // while the dependent adds of the current G run.
-      constexpr int G = 12;
-      int t = 0;
-      if (n >= G) {
-        float cur[G];
-#pragma unroll
-        for (int u = 0; u < G; ++u) cur[u] = __fmul_rn(__half2float(vv[u * D]), pr[u]);
-        for (t = G; t + G <= n; t += G) {
-          float nxt[G];
-#pragma unroll
-          for (int u = 0; u < G; ++u) nxt[u] = __fmul_rn(__half2float(vv[(t + u) * D]), pr[t + u]);
-#pragma unroll
-          for (int u = 0; u < G; ++u) acc = __fadd_rn(acc, cur[u]);
-#pragma unroll
-          for (int u = 0; u < G; ++u) cur[u] = nxt[u];
-        }
-#pragma unroll
-        for (int u = 0; u < G; ++u) acc = __fadd_rn(acc, cur[u]);
+      if (n == CHUNK) {
+        // Five groups of 12: a group's products form while the previous
+        // group's dependent adds run.
+        float x[12], y[12];
+        vprod12(vv, pr, 0, x);
+        vprod12(vv, pr, 12, y);
+        add12(acc, x);
+        vprod12(vv, pr, 24, x);
+        add12(acc, y);
+        vprod12(vv, pr, 36, y);
+        add12(acc, x);
+        vprod12(vv, pr, 48, x);
+        add12(acc, y);
+        add12(acc, x);
+      } else {
+        for (int t = 0; t < n; ++t) acc = __fadd_rn(acc, __fmul_rn(__half2float(vv[t * D]), pr[t]));
       }
-      for (; t < n; ++t) acc = __fadd_rn(acc, __fmul_rn(__half2float(vv[t * D]), pr[t]));
       ring_release(ring_v(), c.nv, c.lane);
       ++c.nv;
     }
@@ -887,6 +925,7 @@ __device__ void attention(Ctx& c, int layer, int pos, unsigned tag_in, unsigned 
     // (block 4h + warp), done once here instead of in every GEMV CTA.
     publish_block(A.attn_t, QW, h * 4 + c.warp, acc, tag_out, c.lane);
   }
+  return make_int2(c.nk, c.nv);
 }
 
 // Records a phase timestamp of the first step (thread 0 only; a no-op unless tracing).
@@ -932,8 +971,10 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(const Mega
     return;
   }
 
+  if (tid == 0) sh->args = A;
+  csync();
   Ctx c;
-  c.A = &A;
+  c.A = &sh->args;
   c.nw = c.nk = c.nv = 0;
   c.trace = nullptr;
   c.tid = tid;
@@ -946,14 +987,15 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(const Mega
   int steps = 0;
   bool stopped = false;
 
-  // RMSNorm weights are requested ahead of the waits that precede their use;
-  // layer 0's attn_norm and the output norm stay in shared memory for the launch.
-  Gamma g_attn{}, g_ffn{};
-  float* s_first = sm<float>(kOffGFirst);
+  // RMSNorm weights live in shared memory: the output norm for the launch,
+  // each layer's attn_norm / ffn_norm staged while the CTA waits for the
+  // attention round trip (nothing stays in registers across phases).
+  float* s_attn = sm<float>(kOffGAttn);
+  float* s_ffn = sm<float>(kOffGFfn);
   float* s_out = sm<float>(kOffGOut);
   if (!att) {
     for (int k = tid; k < W; k += CTHREADS) {
-      s_first[k] = __ldg(A.layers[0].attn_norm + k);
+      s_attn[k] = __ldg(A.layers[0].attn_norm + k);
       s_out[k] = __ldg(A.out_norm + k);
     }
     csync();
@@ -1001,14 +1043,14 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(const Mega
       const int ev = kTraceLayerEvents * layer;
       if (att) {
         MEGA_TRACE(ev + 0);
-        attention(c, layer, pos, tl + kTagQkv, tl + kTagAttn, rope_co, rope_si);
+        const int2 n = attention(c, layer, pos, tl + kTagQkv, tl + kTagAttn, rope_co, rope_si);
+        c.nk = n.x;
+        c.nv = n.y;
         csync();
         MEGA_TRACE(ev + 5);
         if (sh->abort) goto drain;
         continue;
       }
-      g_ffn = load_gamma(c, A.layers[layer].ffn_norm);  // used after the attention round trip
-      if (layer == 0) g_attn = load_gamma(c, s_first);
       // ---- Q: x -> RMSNorm -> quantise -> q/k/v rows ----
       {
         float v[3];
@@ -1019,7 +1061,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(const Mega
           for (int k = 0; k < 3; ++k) v[k] = c.tid + k * CTHREADS < W ? c.xres()[c.tid + k * CTHREADS] : 0.0f;
         }
         MEGA_TRACE(ev + 0);
-        norm_quant(c, v, g_attn, A.eps, layer > 0 ? c.xres() : nullptr);
+        norm_quant(c, v, load_gamma(c, s_attn), A.eps, layer > 0 ? c.xres() : nullptr);
       }
       if (sh->abort) goto drain;
       MEGA_TRACE(ev + 1);
@@ -1030,6 +1072,14 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(const Mega
           goto drain;
       }
       MEGA_TRACE(ev + 3);
+      {  // stage ffn_norm and the next Q phase's attn_norm during the attention round trip
+        const float* fsrc = A.layers[layer].ffn_norm;
+        const float* asrc = A.layers[layer + 1 < A.n_layers ? layer + 1 : 0].attn_norm;
+        for (int k = tid; k < W; k += CTHREADS) {
+          s_ffn[k] = __ldg(fsrc + k);
+          s_attn[k] = __ldg(asrc + k);
+        }
+      }
       // ---- O: quantised attention output -> o + x ----
       if (sp.on > 0) {
         gather_q8(c, A.attn_t, QW, tl + kTagAttn);
@@ -1050,7 +1100,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(const Mega
         gather<3>(c, A.a_t, W, tl + kTagA, v);
         MEGA_TRACE(ev + 8);
         if (sp.gbn > 0) {
-          norm_quant(c, v, g_ffn, A.eps, c.ares());
+          norm_quant(c, v, load_gamma(c, s_ffn), A.eps, c.ares());
         } else {  // no gate/up block here: keep a for the down projection's residual
 #pragma unroll
           for (int k = 0; k < 3; ++k)
@@ -1069,7 +1119,6 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(const Mega
         csync();  // part is rewritten by the next block
       }
       MEGA_TRACE(ev + 11);
-      if (layer + 1 < A.n_layers) g_attn = load_gamma(c, A.layers[layer + 1].attn_norm);
       // ---- D: quantised act -> down + a ----
       if (sp.dn > 0) {
         gather_q8(c, A.act_t, FFN, tl + kTagAct);
