@@ -151,6 +151,14 @@ def oracle_decode_rate(path: Path, cfg, steps: int, warmup: int, threads: int):
     return steps / dt, dt
 
 
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per decode step of
+# the persistent kernel on the bs1_400 workload: `ncu --set full` of one
+# 3-step launch read 2.043 GB and wrote 7.0 MB (profiles/
+# decode_mega_kernel_bs1_prefix408.md).  Algorithmic bytes at prefix 408:
+# 0.681 GB per step.
+MEASURED_TRAFFIC_PER_STEP = {"bs1_400": 0.6833e9}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -245,6 +253,7 @@ def main():
 
     # roofline of the decode step and of its largest single launch (lm_head GEMV)
     peak, peak_kind = measured_peak_hbm()
+    traffic = MEASURED_TRAFFIC_PER_STEP.get(args.config) if dec.persistent_grid() else None
     kv_bytes_per_pos = cm.layers * 2 * cm.kv_heads * cm.head_size * 2
     mean_pos = frames + (steps - 1) / 2.0
     step_bytes = cm.weight_bytes + 1088 + kv_bytes_per_pos * (mean_pos + 1)
@@ -274,7 +283,8 @@ def main():
         "e2e": {"value": world * steps / e2e_s, "unit": "tokens/s", "h2d_bytes_per_step": 4,
                 "d2h_bytes_per_step": 4},
         "roofline": {"bound": "hbm", "kernel": kernel_name, "achieved": achieved, "peak": peak,
-                     "unit": "GB/s", "frac": achieved / peak, "traffic": None,
+                     "unit": "GB/s", "frac": achieved / peak, "traffic": traffic,
+                     "traffic_unit": "DRAM bytes per decode step (ncu capture of this workload)",
                      "bytes_per_step": step_bytes, "peak_source": peak_kind},
         "gpu_launches": launches,
         "clocks": clocks.summary(),
