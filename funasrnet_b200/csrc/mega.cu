@@ -58,14 +58,15 @@ constexpr int CTHREADS = CWARPS * 32;    // 480
 constexpr int TB_W = 8 * W + (W / 32) * 16;      // 8704: tile bytes, K = 1024
 constexpr int TB_Q = 8 * QW + (QW / 32) * 16;    // 17408: K = 2048
 constexpr int TB_F = 8 * FFN + (FFN / 32) * 16;  // 26112: K = 3072
-constexpr int WSLOTS = 6, WSLOT = TB_F;          // weight ring: 3 K=1024 tiles or 1 K=3072 tile per slot
+constexpr int WSLOTS = 7, WSLOT = TB_F;          // weight ring: 3 K=1024 tiles or 1 K=3072 tile per slot
 constexpr int CHUNK = 60;                        // KV positions per attention chunk (8 threads each)
 constexpr int CSLOT = CHUNK * D * 2;             // 15360 bytes
-constexpr int KSLOTS = 6, VSLOTS = 4;
+constexpr int KSLOTS = 6, VSLOTS = 5;
 constexpr int ATT_CTAS = H;
 constexpr unsigned kWaitLimit = 1u << 22;
 
 static_assert(KSLOTS * CSLOT + VSLOTS * CSLOT <= WSLOTS * WSLOT, "KV rings share the weight ring's memory");
+static_assert(2 * WSLOTS <= 16 && 16 + 2 * KSLOTS <= 32 && 32 + 2 * VSLOTS <= 48, "disjoint mbarrier ranges");
 
 enum { kTagQkv = 1, kTagAttn = 2, kTagA = 3, kTagAct = 4, kTagX = 5, kTagPart = 6 };
 enum { kErrWaitData = 1, kErrWaitFull = 2, kErrWaitEmpty = 3, kErrWaitGo = 4, kErrWaitDrain = 5 };
@@ -79,6 +80,7 @@ struct Shared {
   Spans sp;                 // this CTA's GEMV spans (kept here, not in registers)
   volatile int quit;        // consumers stop the producer
   volatile int go;          // steps the consumers have committed to
+  volatile int window;      // weight-issue windows opened (one per layer, at its attention)
   volatile int issued[3];   // copies issued per ring (weights / K / V)
   volatile int prod_exit;   // producer left its loop
   volatile int abort;       // a wait failed somewhere: drain and return
@@ -92,8 +94,15 @@ struct Shared {
 // of `capacity` floats.
 constexpr int align_up(int o, int a) { return (o + a - 1) / a * a; }
 constexpr int kOffRing = 0;                                        // weight ring / K and V rings
-constexpr int kOffBars = align_up(kOffRing + WSLOTS * WSLOT, 8);   // 32 mbarriers
-constexpr int kOffXq = align_up(kOffBars + 32 * 8, 16);            // quantised activations, skewed (xq_off)
+constexpr int kOffBars = align_up(kOffRing + WSLOTS * WSLOT, 8);   // 48 mbarriers
+constexpr int kOffAttQ = kOffBars + 48 * 8;
+constexpr int kOffAttK = kOffAttQ + D * 4;
+constexpr int kOffAttV = kOffAttK + D * 4;
+constexpr int kOffRed = kOffAttV + D * 4;                          // 64 doubles of reductions
+constexpr int kOffShared = align_up(kOffRed + 64 * 8, 16);
+constexpr int kOffRole = align_up(kOffShared + (int)sizeof(Shared), 16);
+// The last region depends on the role.  GEMV CTAs:
+constexpr int kOffXq = kOffRole;                                   // quantised activations, skewed (xq_off)
 constexpr int kOffXs = align_up(kOffXq + FFN + FFN / 256 * 16, 16); // their block scales
 constexpr int kOffXres = align_up(kOffXs + FFN / 32 * 4, 16);      // x (residual of O)
 constexpr int kOffAres = kOffXres + W * 4;                         // a (residual of D)
@@ -101,14 +110,13 @@ constexpr int kOffGAttn = kOffAres + W * 4;                        // attn_norm 
 constexpr int kOffGFfn = kOffGAttn + W * 4;                        // ffn_norm of the coming GU phase
 constexpr int kOffGOut = kOffGFfn + W * 4;                         // output norm
 constexpr int kOffPart = kOffGOut + W * 4;                         // row sums crossing warps [32 x 8]
-constexpr int kOffAttQ = kOffPart + 32 * 8 * 4;
-constexpr int kOffAttK = kOffAttQ + D * 4;
-constexpr int kOffAttV = kOffAttK + D * 4;
-constexpr int kOffRed = kOffAttV + D * 4;                          // 64 doubles of reductions
-constexpr int kOffShared = align_up(kOffRed + 64 * 8, 16);
-constexpr int kOffScores = align_up(kOffShared + (int)sizeof(Shared), 16);
+constexpr int kGemvEnd = kOffPart + 32 * 8 * 4;
+// Attention CTAs: the score row of the query head.
+constexpr int kOffScores = kOffRole;                               // [capacity]
 
-__host__ __device__ constexpr int smem_total(int capacity) { return kOffScores + capacity * 4; }
+__host__ __device__ constexpr int smem_total(int capacity) {
+  return kGemvEnd > kOffScores + capacity * 4 ? kGemvEnd : kOffScores + capacity * 4;
+}
 
 template <typename T>
 __device__ __forceinline__ T* sm(int off) {
@@ -258,16 +266,16 @@ struct Ring {
 };
 
 // The three rings over the same memory (a CTA uses either the weight ring or
-// the K and V rings).  Barriers: weights 0..11, K 12..23, V 24..31.
+// the K and V rings).  Barriers: weights 0..13, K 16..27, V 32..41.
 __device__ __forceinline__ Ring ring_w() {
   return Ring{sm<uint8_t>(kOffRing), sm<uint64_t>(kOffBars), sm<uint64_t>(kOffBars) + WSLOTS, WSLOTS, WSLOT, 0};
 }
 __device__ __forceinline__ Ring ring_k() {
-  return Ring{sm<uint8_t>(kOffRing), sm<uint64_t>(kOffBars) + 12, sm<uint64_t>(kOffBars) + 12 + KSLOTS, KSLOTS, CSLOT,
+  return Ring{sm<uint8_t>(kOffRing), sm<uint64_t>(kOffBars) + 16, sm<uint64_t>(kOffBars) + 16 + KSLOTS, KSLOTS, CSLOT,
               1};
 }
 __device__ __forceinline__ Ring ring_v() {
-  return Ring{sm<uint8_t>(kOffRing) + KSLOTS * CSLOT, sm<uint64_t>(kOffBars) + 24, sm<uint64_t>(kOffBars) + 24 + VSLOTS,
+  return Ring{sm<uint8_t>(kOffRing) + KSLOTS * CSLOT, sm<uint64_t>(kOffBars) + 32, sm<uint64_t>(kOffBars) + 32 + VSLOTS,
               VSLOTS, CSLOT, 2};
 }
 
@@ -362,27 +370,60 @@ __device__ bool wait_go(Shared* sh, MegaCtrl* ctrl, int step) {
   }
 }
 
+// Bounded wait (producer) until the consumers have opened weight window w.
+__device__ bool wait_window(Shared* sh, MegaCtrl* ctrl, int w) {
+  for (unsigned it = 0;; ++it) {
+    if (sh->quit || sh->abort) return false;
+    if (sh->window > w) return true;
+    __nanosleep(64);
+    if (it > kWaitLimit) {
+      raise_error(sh, ctrl, kErrWaitGo);
+      return false;
+    }
+  }
+}
+
+// Weight stream of this GEMV CTA.  Layer l's o, gate/up and down pieces and
+// layer l+1's q/k/v pieces are issued while layer l's attention runs (the
+// consumers open window l when they finish its q/k/v phase): HBM is otherwise
+// idle then, so the other phases' cross-CTA hand-offs never queue behind
+// weight bursts, and the 7-slot ring holds the CTA's share of a whole layer.
+// The lm_head streams as slots free, and the next step's first q/k/v pieces
+// follow it.  The weights do not depend on the step, so the stream runs ahead
+// into the next step; after an early stop the consumers' drain waits for
+// whatever was issued.
 __device__ void producer_gemv(const MegaArgs& A, const Ring& r, Shared* sh) {
   const int n_gemv = gridDim.x - ATT_CTAS;
   const Spans sp = spans(blockIdx.x - ATT_CTAS, n_gemv, A.vocab / 8);
   int n = 0;
-  // The weights do not depend on the step, so the stream runs ahead into the
-  // next step without waiting for it to start; after an early stop the
-  // consumers' drain waits for whatever was issued.
+  auto issue_q = [&](int l) {
+    for (int t = 0; t < sp.qn; t += 3)
+      if (!ring_issue(r, n, A.layers[l].qkv + (size_t)(sp.q0 + t) * TB_W, min(3, sp.qn - t) * TB_W, sh, A.ctrl))
+        return false;
+    return true;
+  };
+  auto issue_rest = [&](int l) {
+    const MegaLayer& Lw = A.layers[l];
+    for (int t = 0; t < sp.on; ++t)
+      if (!ring_issue(r, n, Lw.o + (size_t)(sp.o0 + t) * TB_Q, TB_Q, sh, A.ctrl)) return false;
+    for (int b = 0; b < sp.gbn; ++b)  // a block's 8 gate/up tiles in pieces of 3, 3 and 2
+      for (int t = 0; t < 8; t += 3)
+        if (!ring_issue(r, n, Lw.gu + (size_t)(8 * (sp.gb0 + b) + t) * TB_W, min(3, 8 - t) * TB_W, sh, A.ctrl))
+          return false;
+    for (int t = 0; t < sp.dn; ++t)
+      if (!ring_issue(r, n, Lw.down + (size_t)(sp.d0 + t) * TB_F, TB_F, sh, A.ctrl)) return false;
+    return true;
+  };
+  if (!issue_q(0)) return;
   for (int step = 0; step < A.max_steps; ++step) {
     for (int l = 0; l < A.n_layers; ++l) {
-      const MegaLayer& Lw = A.layers[l];
-      for (int t = 0; t < sp.qn; t += 3)
-        if (!ring_issue(r, n, Lw.qkv + (size_t)(sp.q0 + t) * TB_W, min(3, sp.qn - t) * TB_W, sh, A.ctrl)) return;
-      for (int t = 0; t < sp.on; ++t)
-        if (!ring_issue(r, n, Lw.o + (size_t)(sp.o0 + t) * TB_Q, TB_Q, sh, A.ctrl)) return;
-      for (int t = 0; t < 4 * sp.gbn; ++t)  // one gate/up pair per piece
-        if (!ring_issue(r, n, Lw.gu + (size_t)(4 * sp.gb0 + t) * 2 * TB_W, 2 * TB_W, sh, A.ctrl)) return;
-      for (int t = 0; t < sp.dn; ++t)
-        if (!ring_issue(r, n, Lw.down + (size_t)(sp.d0 + t) * TB_F, TB_F, sh, A.ctrl)) return;
+      if (!wait_window(sh, A.ctrl, step * A.n_layers + l)) return;
+      if (!issue_rest(l)) return;
+      if (l + 1 < A.n_layers && !issue_q(l + 1)) return;
     }
     for (int t = 0; t < sp.lmn; t += 3)
       if (!ring_issue(r, n, A.lm + (size_t)(sp.lm0 + t) * TB_W, min(3, sp.lmn - t) * TB_W, sh, A.ctrl)) return;
+    if (step + 1 < A.max_steps && !issue_q(0)) return;
   }
 }
 
@@ -579,7 +620,33 @@ __device__ __forceinline__ void publish_block(unsigned long long* dst, int n, in
 }
 
 // Waits for n quantised values in that format and unpacks them into xq/xs.
+// SENTINEL: warp 0 alone first waits for the n/32 scale words, a light poll
+// while the producers still compute.  That pays where consumers start waiting
+// long before the data (the down projection: CTAs without a gate/up block
+// would otherwise hammer the same lines for the whole gate/up phase) and costs
+// a round trip where they do not.
+template <bool SENTINEL>
 __device__ __forceinline__ void gather_q8(Ctx& c, const unsigned long long* src, int n, unsigned tag) {
+  if (SENTINEL) {
+    if (c.warp == 0) {
+      for (unsigned it = 0;; ++it) {
+        bool all = true;
+        for (int j = c.lane; j < n / 32; j += 32) all &= (unsigned)(ld_word(src + n / 4 + j) >> 32) == tag;
+        if (__all_sync(0xffffffffu, all)) break;
+        if ((it & 1023) == 1023) {
+          if (c.sh()->abort || ld_flag(&c.A->ctrl->error)) {
+            c.sh()->abort = 1;
+            break;
+          }
+          if (it > kWaitLimit) {
+            raise_error(c.sh(), c.A->ctrl, kErrWaitData);
+            break;
+          }
+        }
+      }
+    }
+    csync();
+  }
   const int total = n / 4 + n / 32;  // <= 2 * CTHREADS
   unsigned pending = 0;
 #pragma unroll
@@ -954,7 +1021,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(const Mega
       mbar_init(&vr.empty[i], 4);  // the V sum runs on warps 0..3
     }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-    sh->quit = sh->go = sh->prod_exit = sh->abort = 0;
+    sh->quit = sh->go = sh->window = sh->prod_exit = sh->abort = 0;
     sh->issued[0] = sh->issued[1] = sh->issued[2] = 0;
   }
   __syncthreads();
@@ -1072,6 +1139,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(const Mega
           goto drain;
       }
       MEGA_TRACE(ev + 3);
+      if (tid == 0) sh->window = step * A.n_layers + layer + 1;  // the weight stream may refill now
       {  // stage ffn_norm and the next Q phase's attn_norm during the attention round trip
         const float* fsrc = A.layers[layer].ffn_norm;
         const float* asrc = A.layers[layer + 1 < A.n_layers ? layer + 1 : 0].attn_norm;
@@ -1082,7 +1150,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(const Mega
       }
       // ---- O: quantised attention output -> o + x ----
       if (sp.on > 0) {
-        gather_q8(c, A.attn_t, QW, tl + kTagAttn);
+        gather_q8<false>(c, A.attn_t, QW, tl + kTagAttn);
         if (sh->abort) goto drain;
         MEGA_TRACE(ev + 4);
         const unsigned tag = tl + kTagA;
@@ -1111,7 +1179,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(const Mega
       if (sh->abort) goto drain;
       MEGA_TRACE(ev + 9);
       for (int bj = 0; bj < sp.gbn; ++bj) {
-        if (!w8a8_phase<W>(c, 8, 2, [&](int t, int r, float v) { c.part()[t * 8 + r] = v; })) goto drain;
+        if (!w8a8_phase<W>(c, 8, 3, [&](int t, int r, float v) { c.part()[t * 8 + r] = v; })) goto drain;
         if (warp == 0) {  // lane = 8 * pair + row: the block's 32 SiLU(gate) * up values
           const float act = silu_mul1(c.part()[(lane >> 3) * 16 + (lane & 7)], c.part()[(lane >> 3) * 16 + 8 + (lane & 7)]);
           publish_block(A.act_t, FFN, sp.gb0 + bj, act, tl + kTagAct, lane);
@@ -1121,7 +1189,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(const Mega
       MEGA_TRACE(ev + 11);
       // ---- D: quantised act -> down + a ----
       if (sp.dn > 0) {
-        gather_q8(c, A.act_t, FFN, tl + kTagAct);
+        gather_q8<true>(c, A.act_t, FFN, tl + kTagAct);
         if (sh->abort) goto drain;
         MEGA_TRACE(ev + 12);
         const unsigned tag = tl + kTagX;
