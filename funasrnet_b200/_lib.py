@@ -78,6 +78,12 @@ SIGNATURES = {
     "fa_session_debug_layer0": (i32, [vp, cp, vp]),
     "fa_session_time_lm_head": (i32, [vp, i32, P(f32)]),
     "fa_lm_head_argmax_noalloc": (i32, [vp, vp, vp, vp, f32, vp, vp, vp]),
+    "fa_batch_create": (i32, [vp, i32, P(vp)]),
+    "fa_batch_free": (i32, [vp]),
+    "fa_batch_size": (i32, [vp]),
+    "fa_batch_step": (i32, [vp, vp, vp, vp]),
+    "fa_batch_generate": (i32, [vp, i32, vp]),
+    "fa_batch_last_ms": (i32, [vp, P(f32)]),
 }
 
 

@@ -16,6 +16,7 @@
 #include <vector>
 
 #include "../../include/funasr_cuda.h"
+#include "batch.h"
 #include "fa_common.h"
 #include "gguf.h"
 #include "kernels.h"
@@ -27,6 +28,9 @@ namespace {
 
 constexpr int kMaxChunkFrames = 64;   // prefill frames per kernel sequence
 constexpr int kAttnSplits = 16;       // split-K CTAs per (frame, KV head)
+constexpr int kBmmMinFrames = 16;     // frames from which projections run on the tensor cores
+constexpr int kSessionInts = 128;     // device words of a session (tokens staged at 16..79)
+constexpr int kErrWord = 100;         // session int word: error code of the batched kernels
 
 struct DevBuf {
   void* p = nullptr;
@@ -97,6 +101,7 @@ struct fa_backend {
   std::set<fa_weight*> weights;
   int models = 0;
   DevBuf in, out, aux, aux2;
+  DevBuf bxq, bxs, berr;  // frame-tile operands of multi-frame projections
   std::vector<float> staging;
 };
 
@@ -121,6 +126,7 @@ struct fa_model {
   int64_t weight_bytes = 0;
   int sessions = 0;
   bool mega_ok = false;   // shape the persistent decode kernel is built for
+  bool bmm_ok = false;    // every Q8 projection fits the tensor-core path (batch.cu)
   DevBuf mega_layers;     // MegaLayer[layers] on the device
 };
 
@@ -154,6 +160,7 @@ struct fa_session {
   DevBuf mx, mqkv, mattn, ma, mact, mpv, mpi, mctrl;
   bool trace = false;
   DevBuf trace_buf;                          // [grid x kTraceEvents] phase timestamps
+  DevBuf bxq, bxs;                           // frame-tile operands of tensor-core prefill projections
   int* d_int(int i) const { return ints.as<int>() + i; }
 };
 
@@ -291,6 +298,43 @@ int fa_weight_release(fa_backend* b, fa_weight* w) {
   });
 }
 
+namespace {
+
+// [RMSNorm] + quantisation of `frames` activation rows into the frame-tile
+// operand, then the tensor-core projection with epilogue `epi` (batch.cu).
+void enqueue_bmm(cudaStream_t st, const Q8View& w, const float* x, int x_stride, int frames, const float* gamma,
+                 float eps, int8_t* xq, float* xs, int epi, float* out, int out_stride, const float* res,
+                 const float* bias, int* err) {
+  const int n_pad = frame_pad(frames);
+  ActQuantArgs q;
+  q.x = x;
+  q.x_stride = x_stride;
+  q.frames = frames;
+  q.K = w.cols;
+  q.gamma = gamma;
+  q.eps = eps;
+  q.xq = xq;
+  q.xs = xs;
+  q.n_pad = n_pad;
+  launch_act_quant(q, st);
+  BmmArgs b;
+  b.w = w;
+  b.xq = xq;
+  b.xs = xs;
+  b.frames = frames;
+  b.n_pad = n_pad;
+  b.ns = bmm_frame_tile(n_pad);
+  b.epilogue = epi;
+  b.out = out;
+  b.out_stride = out_stride;
+  b.res = res;
+  b.bias = bias;
+  b.err = err;
+  launch_bmm(b, st);
+}
+
+}  // namespace
+
 static int run_linear(fa_backend* b, const float* input, int frames, const fa_weight* w, const float* bias,
                       float* output, bool want_q8) {
   check_backend(b);
@@ -313,7 +357,25 @@ static int run_linear(fa_backend* b, const float* input, int frames, const fa_we
     FA_CUDA(cudaMemcpyAsync(b->aux.p, bias, (size_t)w->rows * 4, cudaMemcpyHostToDevice, b->stream));
     dbias = b->aux.as<float>();
   }
-  if (want_q8) {
+  const bool tensor_cores = want_q8 && frames >= kBmmMinFrames && bmm_supported(w->view);
+  if (tensor_cores) {
+    const int n_pad = frame_pad(frames);
+    b->bxq.ensure((size_t)n_pad * w->cols);
+    b->bxs.ensure((size_t)n_pad * (w->cols / 32) * 4);
+    if (!b->berr.p) {
+      b->berr.ensure(4);
+      FA_CUDA(cudaMemset(b->berr.p, 0, 4));
+    }
+    enqueue_bmm(b->stream, w->view, b->in.as<float>(), w->cols, frames, nullptr, 1e-6f, b->bxq.as<int8_t>(),
+                b->bxs.as<float>(), kEpiStore, b->out.as<float>(), w->rows, nullptr, dbias, b->berr.as<int>());
+    int err = 0;
+    FA_CUDA(cudaMemcpyAsync(&err, b->berr.p, 4, cudaMemcpyDeviceToHost, b->stream));
+    FA_CUDA(cudaStreamSynchronize(b->stream));
+    if (err != 0) {
+      FA_CUDA(cudaMemset(b->berr.p, 0, 4));
+      throw Error(kErrTimeout, "tensor-core projection: a bounded wait gave up (code " + std::to_string(err) + ")");
+    }
+  } else if (want_q8) {
     GemvArgs a;
     a.x = b->in.as<float>();
     a.frames = frames;
@@ -814,6 +876,12 @@ int fa_model_load_gguf(fa_backend* b, const char* path, int capacity, fa_model**
                  D == kMegaHead && ffn == kMegaFfn && m->vocab % 8 == 0 && m->embed.base != nullptr &&
                  m->embed.rows == m->vocab && m->capacity <= 8192 &&
                  m->lm.base != nullptr && m->embed.scale_f16 && m->lm.scale_f16;
+    if (m->quantized) {
+      bool ok = bmm_supported(m->lm) && D == 128 && m->heads == 2 * m->kv_heads;
+      for (const LayerDev& Ld : m->L)
+        ok = ok && bmm_supported(Ld.qkv) && bmm_supported(Ld.o) && bmm_supported(Ld.gateup) && bmm_supported(Ld.down);
+      m->bmm_ok = ok;
+    }
     if (m->mega_ok) {
       std::vector<MegaLayer> ml(m->layers);
       for (int l = 0; l < m->layers; ++l) {
@@ -924,14 +992,42 @@ AttnArgs attn_args(fa_session* s, int layer, int frames, const int* skip) {
   return a;
 }
 
+// The four projections of one layer for a prefill chunk of >= kBmmMinFrames
+// frames on the tensor cores; attention between them as in enqueue_layers.
+void enqueue_layer_bmm(fa_session* s, int l, int frames) {
+  fa_model* m = s->m;
+  const LayerDev& L = m->L[l];
+  const int W = m->width, qw = m->heads * m->head_size, kvw = m->kv_heads * m->head_size;
+  cudaStream_t st = s->stream;
+  int8_t* xq = s->bxq.as<int8_t>();
+  float* xs = s->bxs.as<float>();
+  int* err = s->d_int(kErrWord);
+  enqueue_bmm(st, L.qkv, s->x.as<float>(), W, frames, L.attn_norm, m->eps, xq, xs, kEpiStore, s->qkv.as<float>(),
+              qw + 2 * kvw, nullptr, nullptr, err);
+  AttnArgs a = attn_args(s, l, frames, nullptr);
+  launch_qk_rope_kv(a, st);
+  launch_attention(a, st);
+  enqueue_bmm(st, L.o, s->attn.as<float>(), qw, frames, nullptr, m->eps, xq, xs, kEpiResidual, s->a.as<float>(), W,
+              s->x.as<float>(), nullptr, err);
+  enqueue_bmm(st, L.gateup, s->a.as<float>(), W, frames, L.ffn_norm, m->eps, xq, xs, kEpiSiluPair,
+              s->act.as<float>(), m->ffn, nullptr, nullptr, err);
+  enqueue_bmm(st, L.down, s->act.as<float>(), m->ffn, frames, nullptr, m->eps, xq, xs, kEpiResidual,
+              s->x.as<float>(), W, s->a.as<float>(), nullptr, err);
+}
+
 // QwenDecoder.Decode's layer loop (QwenDecoder.cs:180-252) for `frames`
 // frames already in s->x; KV positions come from the device word pos.
 void enqueue_layers(fa_session* s, int frames, const int* skip) {
   fa_model* m = s->m;
   const int W = m->width, qw = m->heads * m->head_size, kvw = m->kv_heads * m->head_size;
   cudaStream_t st = s->stream;
+  const bool tensor_cores = m->bmm_ok && frames >= kBmmMinFrames && skip == nullptr && !s->debug;
   for (int l = 0; l < m->layers; ++l) {
     const LayerDev& L = m->L[l];
+    if (tensor_cores) {
+      enqueue_layer_bmm(s, l, frames);
+      continue;
+    }
     if (m->quantized) {
       GemvArgs g;
       g.x = s->x.as<float>();
@@ -1187,13 +1283,21 @@ int fa_session_create(fa_model* m, fa_session** out) {
     const int lm_ctas = (m->vocab + kTileRows - 1) / kTileRows;
     s->am_val.ensure((size_t)lm_ctas * 4);
     s->am_idx.ensure((size_t)lm_ctas * 4);
-    s->ints.ensure(64 * 4);
-    FA_CUDA(cudaMemset(s->ints.p, 0, 64 * 4));
+    s->ints.ensure(kSessionInts * 4);
+    FA_CUDA(cudaMemset(s->ints.p, 0, kSessionInts * 4));
+    if (m->bmm_ok) {
+      const int kmax = std::max(std::max(W, qw), m->ffn);
+      s->bxq.ensure((size_t)frame_pad(F) * kmax);
+      s->bxs.ensure((size_t)frame_pad(F) * (kmax / 32) * 4);
+      FA_CUDA(cudaMemset(s->bxq.p, 0, s->bxq.bytes));
+      FA_CUDA(cudaMemset(s->bxs.p, 0, s->bxs.bytes));
+    }
     s->end_ids.ensure(64 * 4);
     s->log_cap = m->capacity;
     s->log.ensure((size_t)s->log_cap * 4);
     FA_CUDA(cudaStreamCreateWithFlags(&s->stream, cudaStreamNonBlocking));
     prepare_kernels();
+    prepare_batch_kernels();
     FA_CUDA(cudaEventCreate(&s->ev0));
     FA_CUDA(cudaEventCreate(&s->ev1));
     FA_CUDA(cudaMallocHost(&s->pinned, 64 * 4));
@@ -1297,7 +1401,13 @@ static int session_decode_locked(fa_session* s, const float* emb, const int32_t*
     if (logits) FA_CUDA(cudaMemcpyAsync(logits, s->logits.p, (size_t)m->vocab * 4, cudaMemcpyDeviceToHost, s->stream));
     FA_CUDA(cudaMemcpyAsync(s->pinned, s->d_int(1), 4, cudaMemcpyDeviceToHost, s->stream));
   }
+  FA_CUDA(cudaMemcpyAsync(s->pinned + 4, s->d_int(kErrWord), 4, cudaMemcpyDeviceToHost, s->stream));
   FA_CUDA(cudaStreamSynchronize(s->stream));
+  if (s->pinned[4] != 0) {
+    const int code = s->pinned[4];
+    FA_CUDA(cudaMemset(s->d_int(kErrWord), 0, 4));
+    throw Error(kErrTimeout, "tensor-core projection: a bounded wait gave up (code " + std::to_string(code) + ")");
+  }
   s->pos += frames;
   if (output_logits) {
     s->have_token = true;
@@ -1589,6 +1699,316 @@ int fa_session_set_exact_attention(fa_session* s, int on) {
     }
     return (int)kHandled;
   });
+}
+
+}  // extern "C"
+
+// ============================================================== batch ====
+//
+// n sessions of one model decoded together: each step reads every weight once
+// for all sessions (tensor-core projections over the n activation rows) while
+// attention runs per session over its own KV cache and position.  The step is
+// captured once as a CUDA graph; sessions keep their own device position and
+// token words, which the graph gathers before and writes back after each step,
+// so a session can leave the batch and continue on its own.
+
+struct fa_batch {
+  fa_model* m = nullptr;
+  std::vector<fa_session*> sessions;
+  int device = 0, n = 0, n_pad = 0, row_tiles = 0;
+  cudaStream_t stream = nullptr;
+  std::mutex mu;
+  DevBuf x, a, qkv, attn, act, xq, xs, pv, pi, row0, ints, tabs, log, logits;
+  // ints: [0, n) positions, [n, 2n) tokens, 2n step counter, 2n + 1 error word
+  int log_cap = 0;
+  cudaGraphExec_t graph = nullptr;
+  bool graph_logits = false;
+  int* pinned = nullptr;  // [n + 8]
+  cudaEvent_t ev0 = nullptr, ev1 = nullptr;
+  float last_ms = 0.0f;
+  int* d_pos() const { return ints.as<int>(); }
+  int* d_tok() const { return ints.as<int>() + n; }
+  int* d_counter() const { return ints.as<int>() + 2 * n; }
+  int* d_err() const { return ints.as<int>() + 2 * n + 1; }
+};
+
+namespace {
+
+BatchStep batch_state(fa_batch* b) {
+  BatchStep st;
+  void** t = b->tabs.as<void*>();
+  st.spos = reinterpret_cast<int* const*>(t + 2 * b->n);
+  st.stok = reinterpret_cast<int* const*>(t + 3 * b->n);
+  st.pos = b->d_pos();
+  st.tok = b->d_tok();
+  st.counter = b->d_counter();
+  st.log = b->log.as<int>();
+  st.log_cap = b->log_cap;
+  st.part_value = b->pv.as<float>();
+  st.part_index = b->pi.as<int>();
+  st.row0_nan = b->row0.as<int>();
+  st.row_tiles = b->row_tiles;
+  st.n_pad = b->n_pad;
+  st.frames = b->n;
+  return st;
+}
+
+// One decode step of every session: Embed -> 28 layers -> final norm ->
+// lm_head argmax (QwenDecoder.cs:161-268 with Greedy, :278-326).
+void enqueue_batch_step(fa_batch* b, bool want_logits) {
+  fa_model* m = b->m;
+  const int n = b->n, W = m->width, D = m->head_size, qw = m->heads * D, kvw = m->kv_heads * D;
+  cudaStream_t st = b->stream;
+  int8_t* xq = b->xq.as<int8_t>();
+  float* xs = b->xs.as<float>();
+  int* err = b->d_err();
+  const BatchStep bs = batch_state(b);
+  void** t = b->tabs.as<void*>();
+  launch_batch_gather(bs, st);
+  launch_embed(m->embed, b->d_tok(), n, b->x.as<float>(), nullptr, st);
+  for (int l = 0; l < m->layers; ++l) {
+    const LayerDev& L = m->L[l];
+    enqueue_bmm(st, L.qkv, b->x.as<float>(), W, n, L.attn_norm, m->eps, xq, xs, kEpiStore, b->qkv.as<float>(),
+                qw + 2 * kvw, nullptr, nullptr, err);
+    BatchAttnArgs at;
+    at.qkv = b->qkv.as<float>();
+    at.frames = n;
+    at.heads = m->heads;
+    at.kv_heads = m->kv_heads;
+    at.q_norm = L.q_norm;
+    at.k_norm = L.k_norm;
+    at.eps = m->eps;
+    at.rope_cos = m->rope_cos;
+    at.rope_sin = m->rope_sin;
+    at.k_tab = reinterpret_cast<__half* const*>(t);
+    at.v_tab = reinterpret_cast<__half* const*>(t + n);
+    at.layer_off = (size_t)l * m->capacity * kvw;
+    at.pos = b->d_pos();
+    at.capacity = m->capacity;
+    at.attn = b->attn.as<float>();
+    launch_batch_attention(at, st);
+    enqueue_bmm(st, L.o, b->attn.as<float>(), qw, n, nullptr, m->eps, xq, xs, kEpiResidual, b->a.as<float>(), W,
+                b->x.as<float>(), nullptr, err);
+    enqueue_bmm(st, L.gateup, b->a.as<float>(), W, n, L.ffn_norm, m->eps, xq, xs, kEpiSiluPair, b->act.as<float>(),
+                m->ffn, nullptr, nullptr, err);
+    enqueue_bmm(st, L.down, b->act.as<float>(), m->ffn, n, nullptr, m->eps, xq, xs, kEpiResidual, b->x.as<float>(),
+                W, b->a.as<float>(), nullptr, err);
+  }
+  ActQuantArgs q;
+  q.x = b->x.as<float>();
+  q.x_stride = W;
+  q.frames = n;
+  q.K = W;
+  q.gamma = m->out_norm;
+  q.eps = m->eps;
+  q.xq = xq;
+  q.xs = xs;
+  q.n_pad = b->n_pad;
+  launch_act_quant(q, st);
+  BmmArgs h;
+  h.w = m->lm;
+  h.xq = xq;
+  h.xs = xs;
+  h.frames = n;
+  h.n_pad = b->n_pad;
+  h.ns = bmm_frame_tile(b->n_pad);
+  h.epilogue = kEpiArgmax;
+  h.logits = want_logits ? b->logits.as<float>() : nullptr;
+  h.logits_stride = m->vocab;
+  h.part_value = b->pv.as<float>();
+  h.part_index = b->pi.as<int>();
+  h.row0_nan = b->row0.as<int>();
+  h.err = err;
+  launch_bmm(h, st);
+  launch_batch_finish(bs, st);
+}
+
+cudaGraphExec_t capture_batch(fa_batch* b, bool want_logits) {
+  cudaGraph_t graph = nullptr;
+  FA_CUDA(cudaStreamBeginCapture(b->stream, cudaStreamCaptureModeThreadLocal));
+  try {
+    enqueue_batch_step(b, want_logits);
+  } catch (...) {
+    cudaStreamEndCapture(b->stream, &graph);
+    if (graph) cudaGraphDestroy(graph);
+    throw;
+  }
+  FA_CUDA(cudaStreamEndCapture(b->stream, &graph));
+  cudaGraphExec_t exec = nullptr;
+  cudaError_t e = cudaGraphInstantiate(&exec, graph, 0);
+  cudaGraphDestroy(graph);
+  FA_CUDA(e);
+  return exec;
+}
+
+// Runs `body` with the batch and all of its sessions locked (sessions in
+// address order, so two batches sharing sessions cannot deadlock).
+template <typename F>
+int with_batch(fa_batch* b, F&& body) {
+  return guarded([&] {
+    if (!b) throw Error(kErrArgument, "null batch");
+    std::lock_guard<std::mutex> lk(b->mu);
+    std::vector<fa_session*> order(b->sessions);
+    std::sort(order.begin(), order.end());
+    std::vector<std::unique_lock<std::mutex>> locks;
+    locks.reserve(order.size());
+    for (fa_session* s : order) locks.emplace_back(s->mu);
+    DeviceGuard g(b->device);
+    return body();
+  });
+}
+
+// Launches the step graph `steps` times and checks the batched kernels' error word.
+void run_batch(fa_batch* b, int steps, bool want_logits) {
+  if (b->graph && b->graph_logits != want_logits) {
+    cudaGraphExecDestroy(b->graph);
+    b->graph = nullptr;
+  }
+  if (!b->graph) {
+    b->graph = capture_batch(b, want_logits);
+    b->graph_logits = want_logits;
+  }
+  FA_CUDA(cudaMemsetAsync(b->d_counter(), 0, 4, b->stream));
+  FA_CUDA(cudaEventRecord(b->ev0, b->stream));
+  for (int i = 0; i < steps; ++i) FA_CUDA(cudaGraphLaunch(b->graph, b->stream));
+  FA_CUDA(cudaEventRecord(b->ev1, b->stream));
+  FA_CUDA(cudaMemcpyAsync(b->pinned, b->d_err(), 4, cudaMemcpyDeviceToHost, b->stream));
+  FA_CUDA(cudaStreamSynchronize(b->stream));
+  FA_CUDA(cudaEventElapsedTime(&b->last_ms, b->ev0, b->ev1));
+  if (b->pinned[0] != 0) {
+    const int code = b->pinned[0];
+    FA_CUDA(cudaMemset(b->d_err(), 0, 4));
+    throw Error(kErrTimeout, "batched decode: a bounded wait gave up (code " + std::to_string(code) + ")");
+  }
+  for (fa_session* s : b->sessions) {
+    s->pos += steps;
+    s->have_token = true;
+  }
+}
+
+}  // namespace
+
+extern "C" {
+
+int fa_batch_create(fa_session* const* sessions, int n, fa_batch** out) {
+  return guarded([&] {
+    if (!sessions || !out || n < 1 || n > FA_BATCH_MAX_SESSIONS) throw Error(kErrArgument, "invalid arguments");
+    fa_model* m = sessions[0] ? sessions[0]->m : nullptr;
+    if (!m) throw Error(kErrArgument, "null session");
+    std::set<fa_session*> seen;
+    for (int i = 0; i < n; ++i) {
+      if (!sessions[i] || sessions[i]->m != m) throw Error(kErrArgument, "sessions must share one model");
+      if (!seen.insert(sessions[i]).second) throw Error(kErrArgument, "a session appears twice");
+    }
+    if (!m->bmm_ok || (size_t)2 * m->capacity * 4 > 200 * 1024) return (int)kDeclined;
+    auto b = std::make_unique<fa_batch>();
+    b->m = m;
+    b->sessions.assign(sessions, sessions + n);
+    b->device = m->backend->device;
+    b->n = n;
+    b->n_pad = frame_pad(n);
+    b->row_tiles = m->lm.rows / kBmmRows;
+    DeviceGuard g(b->device);
+    const int W = m->width, D = m->head_size, qw = m->heads * D, kvw = m->kv_heads * D;
+    const size_t np = b->n_pad;
+    const int kmax = std::max(std::max(W, qw), m->ffn);
+    b->x.ensure(np * W * 4);
+    b->a.ensure(np * W * 4);
+    b->qkv.ensure(np * (qw + 2 * kvw) * 4);
+    b->attn.ensure(np * qw * 4);
+    b->act.ensure(np * m->ffn * 4);
+    b->xq.ensure(np * kmax);
+    b->xs.ensure(np * (kmax / 32) * 4);
+    FA_CUDA(cudaMemset(b->xq.p, 0, b->xq.bytes));  // padded frames stay zero
+    FA_CUDA(cudaMemset(b->xs.p, 0, b->xs.bytes));
+    b->pv.ensure((size_t)b->row_tiles * np * 4);
+    b->pi.ensure((size_t)b->row_tiles * np * 4);
+    b->row0.ensure(np * 4);
+    b->ints.ensure((2 * np + 8) * 4);
+    FA_CUDA(cudaMemset(b->ints.p, 0, b->ints.bytes));
+    b->log_cap = m->capacity;
+    b->log.ensure((size_t)b->log_cap * n * 4);
+    std::vector<void*> tabs((size_t)4 * n);
+    for (int i = 0; i < n; ++i) {
+      fa_session* s = sessions[i];
+      tabs[i] = s->k_cache.p;
+      tabs[n + i] = s->v_cache.p;
+      tabs[2 * n + i] = s->d_int(0);
+      tabs[3 * n + i] = s->d_int(1);
+    }
+    b->tabs.ensure(tabs.size() * sizeof(void*));
+    FA_CUDA(cudaMemcpy(b->tabs.p, tabs.data(), tabs.size() * sizeof(void*), cudaMemcpyHostToDevice));
+    FA_CUDA(cudaStreamCreateWithFlags(&b->stream, cudaStreamNonBlocking));
+    FA_CUDA(cudaEventCreate(&b->ev0));
+    FA_CUDA(cudaEventCreate(&b->ev1));
+    FA_CUDA(cudaMallocHost(&b->pinned, (size_t)(n + 8) * 4));
+    prepare_kernels();
+    prepare_batch_kernels();
+    *out = b.release();
+    return (int)kHandled;
+  });
+}
+
+int fa_batch_free(fa_batch* b) {
+  return guarded([&] {
+    if (!b) throw Error(kErrArgument, "null batch");
+    {
+      DeviceGuard g(b->device);
+      cudaStreamSynchronize(b->stream);
+      if (b->graph) cudaGraphExecDestroy(b->graph);
+      cudaEventDestroy(b->ev0);
+      cudaEventDestroy(b->ev1);
+      cudaFreeHost(b->pinned);
+      cudaStreamDestroy(b->stream);
+    }
+    delete b;
+    return (int)kHandled;
+  });
+}
+
+int fa_batch_size(const fa_batch* b) { return b ? b->n : -1; }
+
+int fa_batch_step(fa_batch* b, const int32_t* tokens, int32_t* next, float* logits) {
+  return with_batch(b, [&] {
+    fa_model* m = b->m;
+    for (int i = 0; i < b->n; ++i) {
+      fa_session* s = b->sessions[i];
+      if (s->pos + 1 > m->capacity) throw Error(kErrArgument, "Decoder context exhausted or invalid embeddings");
+      if (!tokens && !s->have_token) throw Error(kErrArgument, "a session has no token: Decode with logits first");
+    }
+    if (tokens) {
+      for (int i = 0; i < b->n; ++i) check_tokens(b->sessions[i], tokens + i, 1);
+      std::memcpy(b->pinned, tokens, (size_t)b->n * 4);
+      for (int i = 0; i < b->n; ++i)
+        FA_CUDA(cudaMemcpyAsync(b->sessions[i]->d_int(1), b->pinned + i, 4, cudaMemcpyHostToDevice, b->stream));
+    }
+    if (logits) b->logits.ensure((size_t)b->n * m->vocab * 4);  // before the logits graph is captured
+    run_batch(b, 1, logits != nullptr);
+    if (next) FA_CUDA(cudaMemcpy(next, b->d_tok(), (size_t)b->n * 4, cudaMemcpyDeviceToHost));
+    if (logits) FA_CUDA(cudaMemcpy(logits, b->logits.p, (size_t)b->n * m->vocab * 4, cudaMemcpyDeviceToHost));
+    return (int)kHandled;
+  });
+}
+
+int fa_batch_generate(fa_batch* b, int steps, int32_t* tokens) {
+  return with_batch(b, [&] {
+    fa_model* m = b->m;
+    if (steps < 0 || (steps > 0 && !tokens)) throw Error(kErrArgument, "invalid arguments");
+    for (fa_session* s : b->sessions) {
+      if (!s->have_token) throw Error(kErrArgument, "a session has no token: Decode with logits first");
+      if (s->pos + steps > m->capacity) throw Error(kErrCapacity, "Decoder context exhausted or invalid embeddings");
+    }
+    if (steps == 0) return (int)kHandled;
+    run_batch(b, steps, false);
+    FA_CUDA(cudaMemcpy(tokens, b->log.p, (size_t)steps * b->n * 4, cudaMemcpyDeviceToHost));
+    return (int)kHandled;
+  });
+}
+
+int fa_batch_last_ms(const fa_batch* b, float* ms) {
+  if (!b || !ms) return kErrArgument;
+  *ms = b->last_ms;
+  return kHandled;
 }
 
 }  // extern "C"

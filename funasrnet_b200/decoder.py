@@ -181,6 +181,60 @@ class QwenDecoder:
         self.close()
 
 
+class BatchDecoder:
+    """n QwenDecoder sessions of one model decoded together, one token each per step.
+
+    The reference decodes independent utterances in separate contexts that share
+    read-only weights (src/FunAsrNet/SpeechRuntime.cs:18-22); this group reads every
+    weight once per step for all of them.  Tokens and logits equal those of each
+    session stepping alone.  Close the group before its sessions.
+    """
+
+    def __init__(self, sessions):
+        self.sessions = list(sessions)
+        arr = (C.c_void_p * len(self.sessions))(*[s._h.value for s in self.sessions])
+        h = C.c_void_p()
+        rc = check(lib().fa_batch_create(arr, len(self.sessions), C.byref(h)))
+        if rc != FA_OK:
+            raise NotImplementedError("model shape not supported by the batched decode path")
+        self._h = h
+        self.vocab = self.sessions[0].model.vocab
+
+    def __len__(self) -> int:
+        return len(self.sessions)
+
+    def step(self, tokens=None, want_logits: bool = False):
+        """One greedy step of every session: returns (next tokens [n], logits [n x vocab] or None)."""
+        n = len(self.sessions)
+        t = None if tokens is None else np.ascontiguousarray(tokens, dtype=np.int32).reshape(n)
+        nxt = np.empty(n, np.int32)
+        logits = np.empty((n, self.vocab), np.float32) if want_logits else None
+        check(lib().fa_batch_step(self._h, ptr(t), ptr(nxt), ptr(logits)))
+        return nxt, logits
+
+    def generate(self, steps: int) -> np.ndarray:
+        """`steps` greedy tokens per session from each last argmax: [steps x n]."""
+        out = np.empty((max(1, steps), len(self.sessions)), np.int32)
+        check(lib().fa_batch_generate(self._h, int(steps), ptr(out)))
+        return out[:steps]
+
+    def last_ms(self) -> float:
+        ms = C.c_float()
+        check(lib().fa_batch_last_ms(self._h, C.byref(ms)))
+        return float(ms.value)
+
+    def close(self) -> None:
+        if getattr(self, "_h", None) is not None:
+            check(lib().fa_batch_free(self._h))
+            self._h = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+
 @dataclass
 class DecodeResult:
     tokens: list

@@ -39,6 +39,7 @@ typedef struct fa_backend fa_backend;
 typedef struct fa_weight fa_weight;
 typedef struct fa_model fa_model;
 typedef struct fa_session fa_session;
+typedef struct fa_batch fa_batch;
 
 /* Message of the last failed call on this thread. */
 const char* fa_last_error(void);
@@ -201,6 +202,37 @@ int fa_session_kernels_per_step(const fa_session* session);
  * one decode step's largest launch) `iters` times on the session stream and
  * returns its mean CUDA-event duration in ms. */
 int fa_session_time_lm_head(fa_session* session, int iters, float* ms);
+
+/* ---------------------------------------------------------------------------
+ * Batched multi-session decode.  The reference runs independent utterances as
+ * separate contexts that share read-only weights (src/FunAsrNet/
+ * SpeechRuntime.cs:18-22) and decodes each with its own QwenDecoder; this
+ * group decodes n such sessions per step, reading every weight once for all of
+ * them.  The projections run on the tensor cores (int8 MMA with the
+ * reference's per-block scale arithmetic), attention per session over its own
+ * F16 KV cache and position.  Each session's tokens and logits are
+ * bit-identical to fa_session_step on that session alone.
+ * ------------------------------------------------------------------------ */
+#define FA_BATCH_MAX_SESSIONS 4096
+/* Groups n distinct sessions of one model (the survey's fa_cuda_batch_step
+ * over sessions[]).  FA_DECLINED when the model's shapes do not fit the
+ * tensor-core path (rows % 128, cols % 256, head size 128, paired GQA).  The
+ * group holds the session handles: free it before its sessions. */
+int fa_batch_create(fa_session* const* sessions, int n, fa_batch** out);
+int fa_batch_free(fa_batch* batch);
+int fa_batch_size(const fa_batch* batch);
+/* One FunAsr.Transcribe iteration (FunAsr.cs:167-178) for every session:
+ * Decode(Embed([token]), 1) + Greedy.  tokens [n] feeds each session (NULL:
+ * each session's last argmax); next [n] receives the argmaxes and logits
+ * [n x vocab] the logits (either may be NULL).  Every session's position
+ * advances by one. */
+int fa_batch_step(fa_batch* batch, const int32_t* tokens, int32_t* next, float* logits);
+/* `steps` greedy tokens per session from each session's last argmax, without
+ * an end-token stop (the fixed-length loop of the benchmark configs).
+ * tokens [steps x n]: token of session i at step t is tokens[t * n + i]. */
+int fa_batch_generate(fa_batch* batch, int steps, int32_t* tokens);
+/* CUDA-event time (ms) of the device work of the last step/generate call. */
+int fa_batch_last_ms(const fa_batch* batch, float* ms);
 
 /* ---------------------------------------------------------------------------
  * Allocation-free lm_head step.  It has no counterpart in the reference, whose
