@@ -1,6 +1,7 @@
 """Decode throughput of the Qwen3-0.6B Q8_0 token loop on B200.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl cuda|reference] [--config bs1_400|bs1_100|fp32]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl cuda|reference]
+                    [--config bs1_400|bs1_100|fp32|bs64|bs256]
 
 Workload (the default): seeded synthetic Qwen3-0.6B
 Q8_0 decoder (28 layers, hidden 1024, 16/8 heads of 128, FFN 3072, vocab
@@ -9,7 +10,13 @@ token ids, then fixed-length greedy decode (no end-token stop).  One bench
 step = one decode token; the timed region is K consecutive decode steps
 starting right after the prefill, so positions are the config's 408..408+K.
 
-Multi-GPU (torchrun): one process per GPU, each its own replica and session
+Batched configs (BASELINE configs[3] and, per GPU, configs[4]): bs64 / bs256
+independent sessions with prefixes of U[50, 400] audio vectors + 8 ids,
+prefilled one by one (untimed), then 128 greedy steps of every session at
+once through fa_batch_generate; one bench step = one token of every session.
+The default bs1 line carries both batched measurements under "batched".
+
+Multi-GPU (torchrun): one process per GPU, each its own replica and sessions
 (independent utterances, no collective on the data path): weak scaling.
 """
 from __future__ import annotations
@@ -35,6 +42,13 @@ CONFIGS = {
     "bs1_100": (100, 8, 128, True),   # configs[0]
     "fp32": (100, 8, 128, False),     # configs[2]
 }
+# name: (sessions per GPU, decode tokens per session)
+BATCH_CONFIGS = {
+    "bs64": (64, 128),
+    "bs256": (256, 128),  # configs[4], per GPU
+}
+BATCH_AUDIO = (50, 400)   # prefix audio vectors ~ U[50, 400], plus 8 prompt ids
+BATCH_CAPACITY = 544      # 400 + 8 + 128 decode positions, rounded up
 SEED = 1234
 
 
@@ -159,17 +173,91 @@ def oracle_decode_rate(path: Path, cfg, steps: int, warmup: int, threads: int):
 MEASURED_TRAFFIC_PER_STEP = {"bs1_400": 0.6833e9}
 
 
+def batch_bench(be, path, name, steps, warmup, rank, world, dist, local, barrier):
+    """Config 4/5: `n` ragged sessions decoded together.  Returns the result dict
+    (rank 0's view; device times are max over ranks)."""
+    from funasrnet_b200.decoder import BatchDecoder, CudaModel, QwenDecoder
+    from funasrnet_b200.shard import max_over_ranks
+
+    n, tokens = BATCH_CONFIGS[name]
+    steps = min(steps, tokens)
+    cm = CudaModel(be, path, capacity=BATCH_CAPACITY)
+    rng = np.random.default_rng(SEED + 17 * (rank + 1))
+    audio = rng.integers(BATCH_AUDIO[0], BATCH_AUDIO[1] + 1, n)
+    sessions = [QwenDecoder(cm) for _ in range(n)]
+    prefixes = [prefix(cm.width, int(audio[i]), 8, cm.vocab, sessions[0].embed, seed=SEED + 1000 * rank + i)
+                for i in range(n)]
+
+    def prefill_all():
+        for d, (emb, frames) in zip(sessions, prefixes):
+            d.reset()
+            d.decode(emb, frames, want_logits=False)
+
+    b = BatchDecoder(sessions)
+    try:
+        prefill_all()
+        b.generate(warmup)  # graph capture + warm-up (untimed)
+        prefill_all()
+        pos0 = np.array([d.position for d in sessions], np.float64)
+        barrier()
+        with ClockSampler(local) as clocks:
+            toks = b.generate(steps)
+        dev_ms = max_over_ranks(b.last_ms(), dist, f"cuda:{local}")
+        assert toks.shape == (steps, n)
+        # e2e: the public per-step call with host buffers (n token ids in, n out)
+        prefill_all()
+        nxt, _ = b.step()
+        barrier()
+        t0 = time.perf_counter()
+        for _ in range(steps - 1):
+            nxt, _ = b.step(nxt)
+        e2e_s = max_over_ranks(time.perf_counter() - t0, dist, f"cuda:{local}")
+    finally:
+        b.close()
+        for d in sessions:
+            d.close()
+    # algorithmic bytes per step: every weight once + each session's K/V rows
+    # [0, pos] + its embedding row
+    kv_per_pos = cm.layers * 2 * cm.kv_heads * cm.head_size * 2
+    mean_pos_sum = float(np.sum(pos0 + (steps - 1) / 2.0 + 1.0))
+    step_bytes = cm.weight_bytes + n * 1088 + kv_per_pos * mean_pos_sum
+    ms_per_step = dev_ms / steps
+    peak, peak_kind = measured_peak_hbm()
+    achieved = step_bytes / (ms_per_step * 1e-3) / 1e9
+    cm.close()
+    return {
+        "metric": f"decode tokens/sec (Qwen3-0.6B Q8_0 {name})",
+        "value": world * n * steps / (dev_ms * 1e-3),
+        "unit": "tokens/s",
+        "ms_per_step": ms_per_step,
+        "sessions_per_gpu": n,
+        "steps": steps,
+        "config": {"workload": f"qwen3-0.6b-q8_0 {n} sessions/GPU, prefix U[{BATCH_AUDIO[0]},{BATCH_AUDIO[1]}]+8, "
+                               f"greedy {tokens} each",
+                   "mean_prefix": float(pos0.mean()), "parallelism": f"replicas x{world}",
+                   "l2": "inputs larger than L2: 0.63 GB of weights + per-session KV every step"},
+        "e2e": {"value": world * n * (steps - 1) / e2e_s, "unit": "tokens/s", "h2d_bytes_per_step": 4 * n,
+                "d2h_bytes_per_step": 4 * n},
+        "roofline": {"bound": "hbm", "kernel": "batched decode step (CUDA graph: tcgen05 projections + attention)",
+                     "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                     "bytes_per_step": step_bytes, "peak_source": peak_kind, "traffic": None},
+        "clocks": clocks.summary(),
+    }
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=256)
     ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--impl", choices=["cuda", "reference"], default="cuda")
-    ap.add_argument("--config", choices=sorted(CONFIGS), default="bs1_400")
+    ap.add_argument("--config", choices=sorted(CONFIGS) + sorted(BATCH_CONFIGS), default="bs1_400")
+    ap.add_argument("--no-batched", action="store_true", help="skip the bs64/bs256 lines of the default run")
     ap.add_argument("--cpu-baseline-steps", type=int, default=24)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
-    cfg = CONFIGS[args.config]
+    batched = args.config in BATCH_CONFIGS
+    cfg = CONFIGS["bs1_400" if batched else args.config]
     audio, ids, tokens, quantized = cfg
     steps = min(args.steps, tokens)
     warmup = max(3, args.warmup)
@@ -222,6 +310,19 @@ def main():
 
     path = ensure_model(quantized, rank, barrier)
     be = CudaFloatBackend(local)
+    if batched:
+        r = batch_bench(be, path, args.config, args.steps, warmup, rank, world, dist, local, barrier)
+        line = {"metric": r["metric"], "value": r["value"], "unit": "tokens/s", "n_gpus": world,
+                "steps": r["steps"], "warmup": warmup, "ms_per_step": r["ms_per_step"], "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None, "dtype": "int8 x int8 -> int32 (tcgen05), f32 accumulate",
+                "data": "synthetic (seeded random-init weights and prefixes)", "config": r["config"],
+                "e2e": r["e2e"], "roofline": r["roofline"], "gpu_launches": None, "clocks": r["clocks"]}
+        if rank == 0:
+            print(json.dumps(line), flush=True)
+        be.dispose()
+        if dist is not None:
+            dist.destroy_process_group()
+        return
     cm = CudaModel(be, path, capacity=2048)
     dec = QwenDecoder(cm)
     emb, frames = prefix(cm.width, audio, ids, cm.vocab, dec.embed)
@@ -292,6 +393,15 @@ def main():
     if lm_ms:
         a = lm_bytes / (lm_ms * 1e-3) / 1e9
         line["gemv_lm_head"] = {"ms": lm_ms, "bytes": lm_bytes, "achieved": a, "frac": a / peak}
+    dec.close()
+    cm.close()
+    if args.config == "bs1_400" and not args.no_batched:
+        line["batched"] = {}
+        for name in ("bs64", "bs256"):
+            r = batch_bench(be, path, name, 128, warmup, rank, world, dist, local, barrier)
+            line["batched"][name] = {k: r[k] for k in ("value", "ms_per_step", "sessions_per_gpu", "steps", "e2e",
+                                                       "roofline", "clocks")}
+            line["batched"][name]["workload"] = r["config"]["workload"]
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         threads = os.cpu_count() or 1
         rate, dt = oracle_decode_rate(path, cfg, args.cpu_baseline_steps, 2, threads)
@@ -300,8 +410,6 @@ def main():
                                           f"({dt:.1f} s of CPU decode)"}
     if rank == 0:
         print(json.dumps(line), flush=True)
-    dec.close()
-    cm.close()
     be.dispose()
     if dist is not None:
         dist.destroy_process_group()

@@ -679,17 +679,25 @@ __device__ __forceinline__ int frame_argmax(const float* pv, const int* pi, cons
   return (row0_nan[f] || bi == INT_MAX) ? 0 : bi;
 }
 
+// Host tokens (one copy of n words) into every session's token word.
+__global__ void batch_scatter_kernel(const BatchStep s, const int* src) {
+  const int f = blockIdx.x * blockDim.x + threadIdx.x;
+  if (f < s.frames) *s.stok[f] = src[f];
+}
+
 __global__ void __launch_bounds__(256) batch_finish_kernel(const BatchStep s) {
   const int f = blockIdx.x;
   const int token = frame_argmax(s.part_value, s.part_index, s.row0_nan, s.row_tiles, s.n_pad, f);
   if (threadIdx.x == 0) {
+    // FunAsr.Transcribe (FunAsr.cs:167-178) appends the token it feeds, then
+    // decodes it: the log holds this step's input token.
+    if (s.log != nullptr) {
+      const int step = *s.counter - 1;
+      if (step >= 0 && step < s.log_cap) s.log[(size_t)step * s.frames + f] = s.tok[f];
+    }
     s.tok[f] = token;
     *s.stok[f] = token;
     *s.spos[f] = s.pos[f] + 1;
-    if (s.log != nullptr) {
-      const int step = *s.counter - 1;
-      if (step >= 0 && step < s.log_cap) s.log[(size_t)step * s.frames + f] = token;
-    }
   }
 }
 
@@ -771,6 +779,11 @@ void launch_batch_attention(const BatchAttnArgs& a, cudaStream_t stream) {
 
 void launch_batch_gather(const BatchStep& s, cudaStream_t stream) {
   batch_gather_kernel<<<(s.frames + 255) / 256, 256, 0, stream>>>(s);
+  FA_CUDA(cudaGetLastError());
+}
+
+void launch_batch_scatter(const BatchStep& s, const int* tokens, cudaStream_t stream) {
+  batch_scatter_kernel<<<(s.frames + 255) / 256, 256, 0, stream>>>(s, tokens);
   FA_CUDA(cudaGetLastError());
 }
 

@@ -116,6 +116,8 @@ struct BatchStep {
 };
 void launch_batch_gather(const BatchStep& s, cudaStream_t stream);
 void launch_batch_finish(const BatchStep& s, cudaStream_t stream);
+// tokens [frames] (device) into each session's token word.
+void launch_batch_scatter(const BatchStep& s, const int* tokens, cudaStream_t stream);
 // Standalone per-frame argmax over bmm partials (multi-frame lm_head calls).
 void launch_frame_argmax(const float* part_value, const int* part_index, const int* row0_nan, int row_tiles,
                          int n_pad, int frames, int* token, cudaStream_t stream);

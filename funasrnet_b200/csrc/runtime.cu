@@ -1718,12 +1718,12 @@ struct fa_batch {
   int device = 0, n = 0, n_pad = 0, row_tiles = 0;
   cudaStream_t stream = nullptr;
   std::mutex mu;
-  DevBuf x, a, qkv, attn, act, xq, xs, pv, pi, row0, ints, tabs, log, logits;
+  DevBuf x, a, qkv, attn, act, xq, xs, pv, pi, row0, ints, tabs, log, logits, feed;
   // ints: [0, n) positions, [n, 2n) tokens, 2n step counter, 2n + 1 error word
   int log_cap = 0;
   cudaGraphExec_t graph = nullptr;
   bool graph_logits = false;
-  int* pinned = nullptr;  // [n + 8]
+  int* pinned = nullptr;  // [8 + n]: error word at 0, token staging at 8
   cudaEvent_t ev0 = nullptr, ev1 = nullptr;
   float last_ms = 0.0f;
   int* d_pos() const { return ints.as<int>(); }
@@ -1978,13 +1978,18 @@ int fa_batch_step(fa_batch* b, const int32_t* tokens, int32_t* next, float* logi
     }
     if (tokens) {
       for (int i = 0; i < b->n; ++i) check_tokens(b->sessions[i], tokens + i, 1);
-      std::memcpy(b->pinned, tokens, (size_t)b->n * 4);
-      for (int i = 0; i < b->n; ++i)
-        FA_CUDA(cudaMemcpyAsync(b->sessions[i]->d_int(1), b->pinned + i, 4, cudaMemcpyHostToDevice, b->stream));
+      std::memcpy(b->pinned + 8, tokens, (size_t)b->n * 4);
+      b->feed.ensure((size_t)b->n * 4);
+      FA_CUDA(cudaMemcpyAsync(b->feed.p, b->pinned + 8, (size_t)b->n * 4, cudaMemcpyHostToDevice, b->stream));
+      launch_batch_scatter(batch_state(b), b->feed.as<int>(), b->stream);
     }
     if (logits) b->logits.ensure((size_t)b->n * m->vocab * 4);  // before the logits graph is captured
     run_batch(b, 1, logits != nullptr);
-    if (next) FA_CUDA(cudaMemcpy(next, b->d_tok(), (size_t)b->n * 4, cudaMemcpyDeviceToHost));
+    if (next) {
+      FA_CUDA(cudaMemcpyAsync(b->pinned + 8, b->d_tok(), (size_t)b->n * 4, cudaMemcpyDeviceToHost, b->stream));
+      FA_CUDA(cudaStreamSynchronize(b->stream));
+      std::memcpy(next, b->pinned + 8, (size_t)b->n * 4);
+    }
     if (logits) FA_CUDA(cudaMemcpy(logits, b->logits.p, (size_t)b->n * m->vocab * 4, cudaMemcpyDeviceToHost));
     return (int)kHandled;
   });

@@ -213,7 +213,8 @@ class BatchDecoder:
         return nxt, logits
 
     def generate(self, steps: int) -> np.ndarray:
-        """`steps` greedy tokens per session from each last argmax: [steps x n]."""
+        """`steps` Transcribe-loop iterations per session (no end stop): [steps x n] emitted
+        tokens, the first row being each session's last argmax, as QwenDecoder.generate."""
         out = np.empty((max(1, steps), len(self.sessions)), np.int32)
         check(lib().fa_batch_generate(self._h, int(steps), ptr(out)))
         return out[:steps]

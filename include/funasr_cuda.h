@@ -227,9 +227,11 @@ int fa_batch_size(const fa_batch* batch);
  * [n x vocab] the logits (either may be NULL).  Every session's position
  * advances by one. */
 int fa_batch_step(fa_batch* batch, const int32_t* tokens, int32_t* next, float* logits);
-/* `steps` greedy tokens per session from each session's last argmax, without
- * an end-token stop (the fixed-length loop of the benchmark configs).
- * tokens [steps x n]: token of session i at step t is tokens[t * n + i]. */
+/* `steps` iterations of the FunAsr.Transcribe loop (FunAsr.cs:167-178) per
+ * session, without an end-token stop (the fixed-length loop of the benchmark
+ * configs): each iteration emits the session's current token (first: its last
+ * argmax) and decodes it.  Emits what fa_session_generate with no end ids
+ * emits.  tokens [steps x n]: token of session i at step t is tokens[t * n + i]. */
 int fa_batch_generate(fa_batch* batch, int steps, int32_t* tokens);
 /* CUDA-event time (ms) of the device work of the last step/generate call. */
 int fa_batch_last_ms(const fa_batch* batch, float* ms);
