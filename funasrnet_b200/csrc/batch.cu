@@ -16,12 +16,17 @@
 // and is exact, and the fused multiply-add rounds (M - 1.5 * 2^23) * ws once.
 // That replaces the integer-to-float conversion, a slow-pipe instruction, with
 // one FFMA per element and block.
+#include <cuda.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
+#include <cudaTypedefs.h>
 
+#include <algorithm>
 #include <cfloat>
 #include <climits>
 #include <mutex>
+#include <string>
+#include <utility>
 
 #include "batch.h"
 #include "device_math.cuh"
@@ -59,11 +64,33 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, unsigned by
                "l"(src), "r"(bytes), "r"(saddr(bar))
                : "memory");
 }
+// Tiled tensor loads (no multicast) completing on an mbarrier.
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+          saddr(dst)),
+      "l"(map), "r"(x), "r"(y), "r"(saddr(bar))
+      : "memory");
+}
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, int x, int y, int z, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(
+          saddr(dst)),
+      "l"(map), "r"(x), "r"(y), "r"(z), "r"(saddr(bar))
+      : "memory");
+}
 __device__ __forceinline__ uint64_t globaltimer() {
   uint64_t t;
   asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
   return t;
 }
+
+// Programmatic dependent launch: the next kernel in the stream may start once
+// every CTA of this one has signalled; griddep_wait() returns once the previous
+// kernel has completed and its writes are visible (at once when the launch had
+// no programmatic dependency).
+__device__ __forceinline__ void griddep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
@@ -78,11 +105,11 @@ __device__ __forceinline__ void tc_mma_i8(unsigned d, uint64_t adesc, uint64_t b
       "l"(adesc), "l"(bdesc), "r"(idesc)
       : "memory");
 }
-// Barrier 1 over the four epilogue warps returning the AND of `v`.
+// Barrier 1 over the eight epilogue warps returning the AND of `v`.
 __device__ __forceinline__ bool epilogue_all(bool v) {
   unsigned r;
   asm volatile(
-      "{\n .reg .pred p, q;\n setp.ne.u32 p, %1, 0;\n bar.red.and.pred q, 1, 128, p;\n selp.u32 %0, 1, 0, q;\n}\n"
+      "{\n .reg .pred p, q;\n setp.ne.u32 p, %1, 0;\n bar.red.and.pred q, 1, 256, p;\n selp.u32 %0, 1, 0, q;\n}\n"
       : "=r"(r)
       : "r"((unsigned)v)
       : "memory");
@@ -150,55 +177,130 @@ __device__ __noinline__ bool wait_phase(uint64_t* bar, unsigned parity, volatile
 
 // ------------------------------------------------------ Q8 projection ----
 
-constexpr int kStages = 4;
-constexpr int kBmmThreads = 192;  // warp 0 copies, warp 1 issues MMAs, warps 2-5 run the epilogue
+constexpr int kEpiWarps = 8;                      // two per TMEM lane quarter, one per column half
+constexpr int kBmmThreads = 64 + 32 * kEpiWarps;  // warp 0 copies, warp 1 issues MMAs
+
+// TMEM loads / stores of n = 4, 8, 16 or 32 consecutive columns of this
+// thread's lane.
+template <int N>
+__device__ __forceinline__ void tmem_ld(unsigned addr, unsigned* v) {
+  if constexpr (N == 4) {
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x4.b32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3])
+                 : "r"(addr)
+                 : "memory");
+  } else if constexpr (N == 8) {
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+                 : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7])
+                 : "r"(addr)
+                 : "memory");
+  } else if constexpr (N == 16) {
+    tmem_ld16(addr, v);
+  } else {
+    static_assert(N == 32, "column count");
+    tmem_ld16(addr, v);
+    tmem_ld16(addr + 16, v + 16);
+  }
+}
+template <int N>
+__device__ __forceinline__ void tmem_fill(unsigned addr, unsigned x) {
+  if constexpr (N == 4) {
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x4.b32 [%0], {%1, %1, %1, %1};" ::"r"(addr), "r"(x) : "memory");
+  } else if constexpr (N == 8) {
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1, %1, %1, %1, %1, %1, %1, %1};" ::"r"(addr),
+                 "r"(x)
+                 : "memory");
+  } else if constexpr (N == 16) {
+    tmem_fill16(addr, x);
+  } else {
+    static_assert(N == 32, "column count");
+    tmem_fill16(addr, x);
+    tmem_fill16(addr + 16, x);
+  }
+}
 
 template <int NS, bool F16S>
 struct BmmLayout {
-  static constexpr int S = F16S ? 2 : 4;           // bytes per weight scale
-  static constexpr int kA = 0;                     // 16 tiles x 16 chunks x 128 B
-  static constexpr int kB = 16 * 2048;             // NS/8 frame groups x 16 chunks x 128 B
-  static constexpr int kSA = kB + (NS / 8) * 2048; // 16 tiles x 8 blocks x 8 rows weight scales
-  static constexpr int kSAStride = 64 * S + 16;    // padded: the 4 tiles a warp reads sit in distinct banks
-  static constexpr int kSB = kSA + 16 * kSAStride; // 8 blocks x NS frame scales (f32)
-  static constexpr int kStage = (kSB + 8 * NS * 4 + 1023) & ~1023;
-  static constexpr unsigned kStageTx = 16 * 2048 + (NS / 8) * 2048 + 16 * 64 * S + 8 * NS * 4;
-  static constexpr int kNB = NS <= 32 ? 8 : 4;     // TMEM accumulator buffers
-  static constexpr int kCols = kNB * NS < 32 ? 32 : kNB * NS;  // power of two
-  static constexpr int kBars = kStages * kStage;
-  static constexpr int kMisc = kBars + 8 * (2 * kStages + 2 * kNB + 1);
-  static constexpr int kRed = kMisc + 16;          // argmax: 4 warps x NS x (value, index)
+  static constexpr int S = F16S ? 2 : 4;  // bytes per weight scale
+  // Scale ring, released by the epilogue, so that the MMAs can run ahead of
+  // it: weight scales (16 tiles x 8 blocks x 8 rows), then frame scales
+  // (8 blocks x NS f32).
+  static constexpr int kScs = 8;
+  static constexpr int kSAStride = 64 * S;  // one tile's 8 blocks x 8 rows
+  static constexpr int kSB = 16 * kSAStride;
+  static constexpr int kScStage = (kSB + 8 * NS * 4 + 127) & ~127;
+  static constexpr unsigned kScTx = 16 * 64 * S + 8 * NS * 4;
+  // Operand ring, released by the MMA commit: A = 16 weight tiles x 16 chunks
+  // x 128 B, then B = NS/8 frame groups x 16 chunks x 128 B.  Stage copies
+  // are latency-bound, so the ring takes every stage that fits (at most 6).
+  static constexpr int kB = 16 * 2048;
+  static constexpr int kOpStage = (kB + (NS / 8) * 2048 + 1023) & ~1023;
+  static constexpr unsigned kOpTx = 16 * 2048 + (NS / 8) * 2048;
+  static constexpr int kReserve = 1024 + 4 * NS * 8;  // barriers, misc words, epilogue exchange
+  static constexpr int kFit = (227 * 1024 - kReserve - kScs * kScStage) / kOpStage;
+  static constexpr int kOps = kFit > 6 ? 6 : kFit;
+  static constexpr int kScBase = kOps * kOpStage;
+  // Accumulators: the epilogue drains them G blocks at a time (one TMEM round
+  // trip per group) from kNGB group buffers filling all 512 TMEM columns.
+  static constexpr int G = NS <= 16 ? 8 : 128 / NS;
+  static constexpr int kGroupCols = G * NS;
+  static constexpr int kNGB = 512 / kGroupCols;
+  static constexpr int kCols = 512;
+  static constexpr int HW = NS / 2;  // columns of one block an epilogue warp owns
+  static constexpr int kBars = kScBase + kScs * kScStage;
+  static constexpr int kNumBars = 2 * kOps + 2 * kScs + 2 * kNGB + 1;
+  static constexpr int kMisc = kBars + 8 * kNumBars;
+  static constexpr int kRed = kMisc + 16;  // epilogue exchange: 4 lane quarters x NS x 8 B
   static constexpr int kTotal = kRed + 4 * NS * 8;
-  static_assert((kCols & (kCols - 1)) == 0 && kCols <= 512, "TMEM allocation is a power of two <= 512");
+  static_assert(8 % G == 0, "a stage holds whole groups");
+  static_assert(kOps >= 2, "operand ring");
+  static_assert(kNGB * kGroupCols == kCols, "TMEM groups");
   static_assert(kTotal <= 227 * 1024, "shared memory");
 };
 
-// Grid: (rows/128) * (n_pad/NS) CTAs, frame tiles adjacent so that the CTAs
-// sharing a weight tile run together and read it from L2.
+// Persistent: work item i = (row tile i / ncol, frame tile i % ncol), CTA c
+// takes items c, c + grid, ...; consecutive items share their weight tile, so
+// the CTAs working on them at the same time read it from L2.  Copies, MMAs and
+// the epilogue run one pipeline across items.
+// The four tensor maps of one projection launch (encoded on the host).
+struct BmmMaps {
+  CUtensorMap a;   // weight quants:  (128 B core row, 16-byte chunk, 8-row tile)
+  CUtensorMap sa;  // weight scales:  (scale bytes of a tile, tile)
+  CUtensorMap b;   // frame quants:   (128 B core row, 16-byte chunk, 8-frame group)
+  CUtensorMap sb;  // frame scales:   (frame, block)
+};
+
 template <int NS, bool F16S>
-__global__ void __launch_bounds__(kBmmThreads, 1) bmm_kernel(const BmmArgs a) {
+__global__ void __launch_bounds__(kBmmThreads, 1) bmm_kernel(const BmmArgs a, const __grid_constant__ BmmMaps maps) {
   using L = BmmLayout<NS, F16S>;
+  constexpr int G = L::G, HW = L::HW, OPS = L::kOps, SCS = L::kScs, NGB = L::kNGB;
   extern __shared__ __align__(1024) uint8_t sm[];
-  uint64_t* full = reinterpret_cast<uint64_t*>(sm + L::kBars);
-  uint64_t* empty = full + kStages;
-  uint64_t* afull = empty + kStages;
-  uint64_t* aempty = afull + L::kNB;
-  uint64_t* drained = aempty + L::kNB;
+  uint64_t* op_full = reinterpret_cast<uint64_t*>(sm + L::kBars);
+  uint64_t* op_empty = op_full + OPS;
+  uint64_t* sc_full = op_empty + OPS;
+  uint64_t* sc_empty = sc_full + SCS;
+  uint64_t* afull = sc_empty + SCS;
+  uint64_t* aempty = afull + NGB;
+  uint64_t* drained = aempty + NGB;
   unsigned* tmem_slot = reinterpret_cast<unsigned*>(sm + L::kMisc);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(sm + L::kMisc + 4);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int ncol = a.n_pad / NS;
-  const int rt = blockIdx.x / ncol, ct = blockIdx.x - rt * ncol;
-  const int K = a.w.cols, nblk = K / 32, nstg = K / kBmmKc;
+  const int ncol = a.n_pad / NS, items = (a.w.rows / kBmmRows) * ncol;
+  const int K = a.w.cols, nstg = K / kBmmKc;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kStages; ++s) {
-      mbar_init(&full[s], 1);
-      mbar_init(&empty[s], 5);  // the MMA commit + the 4 epilogue warps (they read the stage's scales)
+    griddep_launch();
+    for (int s = 0; s < OPS; ++s) {
+      mbar_init(&op_full[s], 1);
+      mbar_init(&op_empty[s], 1);
     }
-    for (int b = 0; b < L::kNB; ++b) {
+    for (int s = 0; s < SCS; ++s) {
+      mbar_init(&sc_full[s], 1);
+      mbar_init(&sc_empty[s], kEpiWarps);
+    }
+    for (int b = 0; b < NGB; ++b) {
       mbar_init(&afull[b], 1);
-      mbar_init(&aempty[b], 4);
+      mbar_init(&aempty[b], kEpiWarps);
     }
     mbar_init(drained, 1);
     *abort_flag = 0;
@@ -216,79 +318,91 @@ __global__ void __launch_bounds__(kBmmThreads, 1) bmm_kernel(const BmmArgs a) {
   const unsigned tmem = *tmem_slot;
 
   if (warp == 0) {
-    // ---- producer: one stage = 256 columns of 16 weight tiles + NS frames ----
-    const size_t TB = (size_t)a.w.tile_bytes;
-    const uint8_t* wbase = a.w.base + (size_t)rt * 16 * TB;
-    const int8_t* xbase = a.xq + (size_t)ct * (NS / 8) * 8 * K;
-    const float* sbase = a.xs + (size_t)ct * NS;
-    int issued = 0;
-    for (int s = 0; s < nstg; ++s) {
-      const int slot = s % kStages;
-      if (s >= kStages) {
-        const bool ok = wait_phase(&empty[slot], ((s / kStages) - 1) & 1, abort_flag, a.err, kBatchWaitFree);
-        if (!__all_sync(0xffffffffu, ok)) break;
+    // ---- producer: per stage 256 columns of 16 weight tiles + NS frames,
+    // operands into the operand ring, scales into the scale ring ----
+    // The weights do not depend on the previous kernel: the first item's first
+    // stages of weights and weight scales go out before the dependency wait.
+    const int pre = blockIdx.x < items ? min(nstg, OPS) : 0;
+    if (lane == 0)
+      for (int s = 0; s < pre; ++s) {
+        const int rt = blockIdx.x / ncol;
+        mbar_expect_tx(&op_full[s], L::kOpTx);
+        mbar_expect_tx(&sc_full[s], L::kScTx);
+        tma_load_3d(sm + s * L::kOpStage, &maps.a, 0, s * 16, rt * 16, &op_full[s]);
+        tma_load_2d(sm + L::kScBase + s * L::kScStage, &maps.sa, s * 64 * L::S, rt * 16, &sc_full[s]);
       }
-      uint8_t* st = sm + slot * L::kStage;
-      if (lane == 0) mbar_expect_tx(&full[slot], L::kStageTx);
-      __syncwarp();
-      for (int i = lane; i < 40 + NS / 8; i += 32) {
-        const void* src;
-        void* dst;
-        unsigned bytes;
-        if (i < 16) {
-          src = wbase + i * TB + (size_t)s * 2048;
-          dst = st + L::kA + i * 2048;
-          bytes = 2048;
-        } else if (i < 32) {
-          const int t = i - 16;
-          src = wbase + t * TB + (size_t)8 * K + (size_t)s * 64 * L::S;
-          dst = st + L::kSA + t * L::kSAStride;
-          bytes = 64 * L::S;
-        } else if (i < 32 + NS / 8) {
-          const int g = i - 32;
-          src = xbase + (size_t)g * 8 * K + (size_t)s * 2048;
-          dst = st + L::kB + g * 2048;
-          bytes = 2048;
-        } else {
-          const int kb = i - 32 - NS / 8;
-          src = sbase + (size_t)(s * 8 + kb) * a.n_pad;
-          dst = st + L::kSB + kb * NS * 4;
-          bytes = NS * 4;
+    griddep_wait();
+    int q = 0;  // stages issued
+    bool ok = true;
+    for (int it = blockIdx.x; it < items && ok; it += gridDim.x) {
+      const int rt = it / ncol, ct = it - rt * ncol;
+      for (int s = 0; s < nstg; ++s) {
+        const int os = q % OPS, ss = q % SCS;
+        bool w = true;
+        if (q >= OPS) w = wait_phase(&op_empty[os], ((q / OPS) - 1) & 1, abort_flag, a.err, kBatchWaitFree);
+        if (w && q >= SCS) w = wait_phase(&sc_empty[ss], ((q / SCS) - 1) & 1, abort_flag, a.err, kBatchWaitFree);
+        if (!__all_sync(0xffffffffu, w)) {
+          ok = false;
+          break;
         }
-        bulk_g2s(dst, src, bytes, &full[slot]);
+        uint8_t* ost = sm + os * L::kOpStage;
+        uint8_t* sst = sm + L::kScBase + ss * L::kScStage;
+        if (lane == 0) {
+          if (q >= pre) {
+            mbar_expect_tx(&op_full[os], L::kOpTx);
+            mbar_expect_tx(&sc_full[ss], L::kScTx);
+            tma_load_3d(ost, &maps.a, 0, s * 16, rt * 16, &op_full[os]);
+            tma_load_2d(sst, &maps.sa, s * 64 * L::S, rt * 16, &sc_full[ss]);
+          }
+          tma_load_3d(ost + L::kB, &maps.b, 0, s * 16, ct * (NS / 8), &op_full[os]);
+          tma_load_2d(sst + L::kSB, &maps.sb, ct * NS, s * 8, &sc_full[ss]);
+        }
+        __syncwarp();
+        ++q;
       }
-      issued = s + 1;
     }
     // Copies in flight must land before the CTA exits.
-    if (lane == 0)
-      for (int s = issued > kStages ? issued - kStages : 0; s < issued; ++s)
-        wait_phase(&full[s % kStages], (s / kStages) & 1, abort_flag, a.err, kBatchWaitLoad, false);
+    if (lane == 0) {
+      for (int s = q > OPS ? q - OPS : 0; s < q; ++s)
+        wait_phase(&op_full[s % OPS], (s / OPS) & 1, abort_flag, a.err, kBatchWaitLoad, false);
+      for (int s = q > SCS ? q - SCS : 0; s < q; ++s)
+        wait_phase(&sc_full[s % SCS], (s / SCS) & 1, abort_flag, a.err, kBatchWaitLoad, false);
+    }
     __syncwarp();
   } else if (warp == 1) {
-    // ---- MMA issuer: one K = 32 MMA per Q8 block into a rotating accumulator ----
+    // ---- MMA issuer: one K = 32 MMA per Q8 block, G blocks per accumulator group ----
     if (lane == 0) {
       constexpr unsigned idesc = idesc_i8(kBmmRows, NS);
       bool ok = true;
-      int b = 0;
-      for (; b < nblk; ++b) {
-        const int s = b >> 3, kb = b & 7, slot = s % kStages, buf = b % L::kNB;
-        if (kb == 0 && !wait_phase(&full[slot], (s / kStages) & 1, abort_flag, a.err, kBatchWaitLoad)) {
-          ok = false;
-          break;
+      int q = 0, gq = 0;
+      for (int it = blockIdx.x; it < items && ok; it += gridDim.x) {
+        for (int s = 0; s < nstg && ok; ++s, ++q) {
+          const int os = q % OPS;
+          if (!wait_phase(&op_full[os], (q / OPS) & 1, abort_flag, a.err, kBatchWaitLoad)) {
+            ok = false;
+            break;
+          }
+          const unsigned st = saddr(sm + os * L::kOpStage);
+          for (int g8 = 0; g8 < 8 / G; ++g8, ++gq) {
+            const int gb = gq % NGB;
+            if (!wait_phase(&aempty[gb], (gq / NGB) & 1, abort_flag, a.err, kBatchWaitFree)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+#pragma unroll
+            for (int u = 0; u < G; ++u) {
+              const int kb = g8 * G + u;
+              const uint64_t ad = smem_desc(st + kb * 256, 128, 2048);
+              const uint64_t bd = smem_desc(st + L::kB + kb * 256, 128, 2048);
+              tc_mma_i8(tmem + gb * L::kGroupCols + u * NS, ad, bd, idesc);
+            }
+            tc_commit(&afull[gb]);
+          }
+          if (ok) tc_commit(&op_empty[os]);
         }
-        if (!wait_phase(&aempty[buf], (b / L::kNB) & 1, abort_flag, a.err, kBatchWaitFree)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        const unsigned st = saddr(sm + slot * L::kStage);
-        const uint64_t ad = smem_desc(st + L::kA + kb * 256, 128, 2048);
-        const uint64_t bd = smem_desc(st + L::kB + kb * 256, 128, 2048);
-        tc_mma_i8(tmem + buf * NS, ad, bd, idesc);
-        tc_commit(&afull[buf]);
-        if (kb == 7) tc_commit(&empty[slot]);
       }
-      if (!ok && b > 0) {
+      if (!ok && gq > 0) {
         // MMAs still in flight must finish before the accumulators are freed.
         tc_commit(drained);
         wait_phase(drained, 0, abort_flag, a.err, kBatchWaitMma, false);
@@ -296,96 +410,133 @@ __global__ void __launch_bounds__(kBmmThreads, 1) bmm_kernel(const BmmArgs a) {
     }
     __syncwarp();
   } else {
-    // ---- epilogue: thread = weight row m of the tile (TMEM lane m) ----
-    const int q = warp & 3;  // TMEM lane quarter this warp may access
-    const unsigned lane_addr = tmem + ((unsigned)(32 * q) << 16);
-    const int m = 32 * q + lane, t = m >> 3, r = m & 7;
+    // ---- epilogue: thread = weight row m (TMEM lane m), HW frames of each block ----
+    griddep_wait();                 // residuals and outputs belong to the kernels before
+    const int qd = warp & 3;        // TMEM lane quarter this warp may access
+    const int h = (warp - 2) >> 2;  // column half
+    const unsigned lane_addr = tmem + ((unsigned)(32 * qd) << 16) + h * HW;
+    const int m = 32 * qd + lane, t = m >> 3, r = m & 7;
+#pragma unroll 1
+    for (int gb = 0; gb < NGB; ++gb)
 #pragma unroll
-    for (int buf = 0; buf < L::kNB; ++buf)
-#pragma unroll
-      for (int c = 0; c < NS; c += 16) tmem_fill16(lane_addr + buf * NS + c, kMagicBits);
+      for (int u = 0; u < G; ++u) tmem_fill<HW>(lane_addr + gb * L::kGroupCols + u * NS, kMagicBits);
     tc_wait_st();
     tc_fence_before();
     __syncwarp();
     if (lane == 0)
-      for (int buf = 0; buf < L::kNB; ++buf) mbar_arrive(&aempty[buf]);
-    float acc[NS];
-#pragma unroll
-    for (int j = 0; j < NS; ++j) acc[j] = 0.0f;
+      for (int gb = 0; gb < NGB; ++gb) mbar_arrive(&aempty[gb]);
     bool ok = true;
-    for (int b = 0; b < nblk; ++b) {
-      const int s = b >> 3, kb = b & 7, slot = s % kStages, buf = b % L::kNB;
-      bool w = true;
-      if (kb == 0) w = wait_phase(&full[slot], (s / kStages) & 1, abort_flag, a.err, kBatchWaitLoad);
-      if (w) w = wait_phase(&afull[buf], (b / L::kNB) & 1, abort_flag, a.err, kBatchWaitMma);
-      if (!__all_sync(0xffffffffu, w)) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
-      unsigned v[NS];
+    int q = 0, gq = 0;
+    for (int it = blockIdx.x; it < items; it += gridDim.x) {
+      const int rt = it / ncol, ct = it - rt * ncol;
+      float acc[HW];
 #pragma unroll
-      for (int c = 0; c < NS; c += 16) tmem_ld16(lane_addr + buf * NS + c, v + c);
-      tc_wait_ld();
+      for (int j = 0; j < HW; ++j) acc[j] = 0.0f;
+      for (int s = 0; s < nstg && ok; ++s, ++q) {
+        const int ss = q % SCS;
+        ok = __all_sync(0xffffffffu, wait_phase(&sc_full[ss], (q / SCS) & 1, abort_flag, a.err, kBatchWaitLoad));
+        const uint8_t* st = sm + L::kScBase + ss * L::kScStage;
+        for (int g8 = 0; g8 < 8 / G && ok; ++g8, ++gq) {
+          const int gb = gq % NGB;
+          ok = __all_sync(0xffffffffu, wait_phase(&afull[gb], (gq / NGB) & 1, abort_flag, a.err, kBatchWaitMma));
+          if (!ok) break;
+          tc_fence_after();
+          unsigned v[G * HW];
 #pragma unroll
-      for (int c = 0; c < NS; c += 16) tmem_fill16(lane_addr + buf * NS + c, kMagicBits);
-      tc_wait_st();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&aempty[buf]);
-      const uint8_t* st = sm + slot * L::kStage;
-      const float ws = F16S ? __half2float(reinterpret_cast<const __half*>(st + L::kSA + t * L::kSAStride)[kb * 8 + r])
-                            : reinterpret_cast<const float*>(st + L::kSA + t * L::kSAStride)[kb * 8 + r];
-      const float4* xs4 = reinterpret_cast<const float4*>(st + L::kSB + kb * NS * 4);
-      if (F16S && fabsf(ws) <= 65504.0f) {
-        const float nc = __fmul_rn(ws, -kMagic);  // exact: ws has 11 significant bits
+          for (int u = 0; u < G; ++u) tmem_ld<HW>(lane_addr + gb * L::kGroupCols + u * NS, v + u * HW);
+          tc_wait_ld();
 #pragma unroll
-        for (int j4 = 0; j4 < NS / 4; ++j4) {
-          const float4 x = xs4[j4];
-          const float xv[4] = {x.x, x.y, x.z, x.w};
+          for (int u = 0; u < G; ++u) tmem_fill<HW>(lane_addr + gb * L::kGroupCols + u * NS, kMagicBits);
 #pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            const int j = 4 * j4 + u;
-            acc[j] = __fadd_rn(acc[j], __fmul_rn(__fmaf_rn(__uint_as_float(v[j]), ws, nc), xv[u]));
+          for (int u = 0; u < G; ++u) {
+            const int kb = g8 * G + u;
+            const float ws = F16S ? __half2float(reinterpret_cast<const __half*>(st + t * L::kSAStride)[kb * 8 + r])
+                                  : reinterpret_cast<const float*>(st + t * L::kSAStride)[kb * 8 + r];
+            const float4* xs4 = reinterpret_cast<const float4*>(st + L::kSB + (kb * NS + h * HW) * 4);
+            if (F16S && fabsf(ws) <= 65504.0f) {
+              const float nc = __fmul_rn(ws, -kMagic);  // exact: ws has 11 significant bits
+#pragma unroll
+              for (int j4 = 0; j4 < HW / 4; ++j4) {
+                const float4 x = xs4[j4];
+                const float xv[4] = {x.x, x.y, x.z, x.w};
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                  const int j = 4 * j4 + e;
+                  acc[j] = __fadd_rn(acc[j], __fmul_rn(__fmaf_rn(__uint_as_float(v[u * HW + j]), ws, nc), xv[e]));
+                }
+              }
+            } else {
+#pragma unroll
+              for (int j4 = 0; j4 < HW / 4; ++j4) {
+                const float4 x = xs4[j4];
+                const float xv[4] = {x.x, x.y, x.z, x.w};
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                  const int j = 4 * j4 + e;
+                  const float dot = __fsub_rn(__uint_as_float(v[u * HW + j]), kMagic);  // exact integer
+                  acc[j] = __fadd_rn(acc[j], __fmul_rn(__fmul_rn(dot, ws), xv[e]));
+                }
+              }
+            }
           }
+          tc_wait_st();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&aempty[gb]);
         }
-      } else {
-#pragma unroll
-        for (int j4 = 0; j4 < NS / 4; ++j4) {
-          const float4 x = xs4[j4];
-          const float xv[4] = {x.x, x.y, x.z, x.w};
-#pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            const int j = 4 * j4 + u;
-            const float dot = __fsub_rn(__uint_as_float(v[j]), kMagic);  // exact integer
-            acc[j] = __fadd_rn(acc[j], __fmul_rn(__fmul_rn(dot, ws), xv[u]));
-          }
-        }
-      }
-      if (kb == 7) {
         __syncwarp();
-        if (lane == 0) mbar_arrive(&empty[slot]);
+        if (lane == 0) mbar_arrive(&sc_empty[ss]);
       }
-    }
-    // One decision for the four warps: the argmax epilogue meets at barrier 1.
-    if (epilogue_all(ok)) {
+      // One decision for the eight warps: the exchanging epilogues meet at barrier 1.
+      if (!epilogue_all(ok)) break;
       const int row = rt * kBmmRows + m;
-      const int f0 = ct * NS;
-      if (a.epilogue == kEpiSiluPair) {
+      const int f0 = ct * NS + h * HW;
+      if (a.epilogue == kEpiSiluPair || a.epilogue == kEpiSiluQuant) {
         // tiles (2i, 2i+1) = (gate, up) rows 8i..8i+7: the up row sits 8 lanes on
         const int T = rt * 16 + t;
         const int arow = (T >> 1) * 8 + r;
+        const bool gate = ((lane >> 3) & 1) == 0;
+        float act[HW];
 #pragma unroll
-        for (int j = 0; j < NS; ++j) {
+        for (int j = 0; j < HW; ++j) {
           const float u = __shfl_down_sync(0xffffffffu, acc[j], 8);
-          if (((lane >> 3) & 1) == 0 && f0 + j < a.frames)
-            a.out[(size_t)(f0 + j) * a.out_stride + arow] = silu_mul1(acc[j], u);
+          act[j] = gate ? silu_mul1(acc[j], u) : 0.0f;
+        }
+        if (a.epilogue == kEpiSiluPair) {
+#pragma unroll
+          for (int j = 0; j < HW; ++j)
+            if (gate && f0 + j < a.frames) a.out[(size_t)(f0 + j) * a.out_stride + arow] = act[j];
+        } else {
+          // Quantise the SiLU outputs for the next projection (TensorMath.Quantize
+          // per 32-block): a block of act rows is held by the gate lanes of the
+          // warps of lane quarters 2k and 2k + 1; their |x| bit maxima meet in
+          // shared memory.
+          unsigned* xm = reinterpret_cast<unsigned*>(sm + L::kRed);
+          const int Kq = a.w.rows / 2;
+#pragma unroll
+          for (int j = 0; j < HW; ++j) {
+            const unsigned mb = __reduce_max_sync(0xffffffffu, gate ? (__float_as_uint(act[j]) & 0x7fffffffu) : 0u);
+            if (lane == 0) xm[(h * 4 + qd) * HW + j] = mb;
+          }
+          asm volatile("bar.sync 1, %0;" ::"n"(32 * kEpiWarps) : "memory");
+#pragma unroll
+          for (int j = 0; j < HW; ++j) {
+            const unsigned mb = max(xm[(h * 4 + qd) * HW + j], xm[(h * 4 + (qd ^ 1)) * HW + j]);
+            const float d = __fdiv_rn(__uint_as_float(mb), 127.0f);
+            const float id = d == 0.0f ? 0.0f : __fdiv_rn(1.0f, d);
+            const int f = f0 + j;
+            if (gate && f < a.frames)
+              a.qout[(size_t)(f >> 3) * 8 * Kq + (arow >> 4) * 128 + (f & 7) * 16 + (arow & 15)] =
+                  (int8_t)quant1(act[j], id);
+            if (lane == 0 && (qd & 1) == 0 && f < a.frames) a.qout_s[(size_t)(arow >> 5) * a.qout_npad + f] = d;
+          }
+          asm volatile("bar.sync 1, %0;" ::"n"(32 * kEpiWarps) : "memory");  // xm reused by the next item
         }
       } else if (a.epilogue == kEpiArgmax) {
         float* red_v = reinterpret_cast<float*>(sm + L::kRed);
         int* red_i = reinterpret_cast<int*>(red_v + 4 * NS);
 #pragma unroll
-        for (int j = 0; j < NS; ++j) {
+        for (int j = 0; j < HW; ++j) {
           const int f = f0 + j;
           if (a.logits != nullptr && f < a.frames) a.logits[(size_t)f * a.logits_stride + row] = acc[j];
           if (row == 0 && f < a.frames) a.row0_nan[f] = isnan(acc[j]) ? 1 : 0;
@@ -401,26 +552,27 @@ __global__ void __launch_bounds__(kBmmThreads, 1) bmm_kernel(const BmmArgs a) {
             }
           }
           if (lane == 0) {
-            red_v[q * NS + j] = bv;
-            red_i[q * NS + j] = bi;
+            red_v[qd * NS + h * HW + j] = bv;
+            red_i[qd * NS + h * HW + j] = bi;
           }
         }
-        asm volatile("bar.sync 1, 128;" ::: "memory");
+        asm volatile("bar.sync 1, %0;" ::"n"(32 * kEpiWarps) : "memory");
         const int e = threadIdx.x - 64;
-        for (int j = e; j < NS; j += 128) {
+        if (e < NS) {
           float bv = __int_as_float(0x7fc00000);
           int bi = INT_MAX;
           for (int qq = 0; qq < 4; ++qq)
-            if (better(red_v[qq * NS + j], red_i[qq * NS + j], bv, bi)) {
-              bv = red_v[qq * NS + j];
-              bi = red_i[qq * NS + j];
+            if (better(red_v[qq * NS + e], red_i[qq * NS + e], bv, bi)) {
+              bv = red_v[qq * NS + e];
+              bi = red_i[qq * NS + e];
             }
-          a.part_value[(size_t)rt * a.n_pad + f0 + j] = bv;
-          a.part_index[(size_t)rt * a.n_pad + f0 + j] = bi;
+          a.part_value[(size_t)rt * a.n_pad + ct * NS + e] = bv;
+          a.part_index[(size_t)rt * a.n_pad + ct * NS + e] = bi;
         }
+        asm volatile("bar.sync 1, %0;" ::"n"(32 * kEpiWarps) : "memory");  // red_* reused by the next item
       } else {
 #pragma unroll
-        for (int j = 0; j < NS; ++j) {
+        for (int j = 0; j < HW; ++j) {
           const int f = f0 + j;
           if (f >= a.frames) continue;
           float o = acc[j];
@@ -442,84 +594,162 @@ __global__ void __launch_bounds__(kBmmThreads, 1) bmm_kernel(const BmmArgs a) {
 
 // -------------------------------------------------- activation quant ----
 
-// One CTA per frame, 256 threads.  The RMSNorm sum of squares runs in the
-// single-frame GEMV's association (thread-strided double sums, warp tree, warps
-// in order) so both paths produce the same scale.
+// One CTA per frame, 256 threads; thread t holds elements t + 256 i, which
+// are both its share of the RMSNorm sum of squares (the single-frame GEMV's
+// association: thread-strided double sums, warp tree, warps in order) and its
+// lane of blocks warp + 8 i.  All loads are issued before any arithmetic.
+constexpr int kActMaxCols = 8192;
+template <int NW>  // K / 256 elements per thread; 0: any K up to kActMaxCols
 __global__ void __launch_bounds__(256) act_quant_kernel(const ActQuantArgs a) {
+  constexpr int MAXW = NW > 0 ? NW : kActMaxCols / 256;
   __shared__ double red[8];
-  const int f = blockIdx.x, K = a.K;
+  if (threadIdx.x == 0) griddep_launch();
+  griddep_wait();
+  const int f = blockIdx.x, K = a.K, nw = NW > 0 ? NW : K / 256;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const float* xr = a.x + (size_t)f * a.x_stride;
-  float inv = 1.0f;
+  const float* xr = a.x + (size_t)f * a.x_stride + threadIdx.x;
+  float v[MAXW];
+#pragma unroll
+  for (int i = 0; i < MAXW; ++i) v[i] = i < nw ? xr[256 * i] : 0.0f;
   if (a.gamma != nullptr) {
     double part = 0.0;
-    for (int k = threadIdx.x; k < K; k += 256) {
-      const double z = (double)xr[k];
-      part = __dadd_rn(part, __dmul_rn(z, z));
-    }
+#pragma unroll
+    for (int i = 0; i < MAXW; ++i)
+      if (i < nw) {
+        const double z = (double)v[i];
+        part = __dadd_rn(part, __dmul_rn(z, z));
+      }
     part = warp_sum_d(part);
     if (lane == 0) red[warp] = part;
     __syncthreads();
     double var = 0.0;
 #pragma unroll
     for (int w = 0; w < 8; ++w) var = __dadd_rn(var, red[w]);
-    inv = rms_inverse(var, K, a.eps);
+    const float inv = rms_inverse(var, K, a.eps);
+#pragma unroll
+    for (int i = 0; i < MAXW; ++i)
+      if (i < nw) v[i] = __fmul_rn(__fmul_rn(v[i], inv), a.gamma[threadIdx.x + 256 * i]);
   }
   int8_t* xq = a.xq + (size_t)(f >> 3) * 8 * K + (f & 7) * 16 + (lane & 15);
-  for (int j = warp; j < K / 32; j += 8) {
-    float v = xr[j * 32 + lane];
-    if (a.gamma != nullptr) v = __fmul_rn(__fmul_rn(v, inv), a.gamma[j * 32 + lane]);
-    float d, id;
-    block_scale(v, d, id);
-    xq[(size_t)(2 * j + (lane >> 4)) * 128] = (int8_t)quant1(v, id);
-    if (lane == 0) a.xs[(size_t)j * a.n_pad + f] = d;
-  }
+#pragma unroll
+  for (int i = 0; i < MAXW; ++i)
+    if (i < nw) {
+      const int j = warp + 8 * i;  // block
+      float d, id;
+      block_scale(v[i], d, id);
+      xq[(size_t)(2 * j + (lane >> 4)) * 128] = (int8_t)quant1(v[i], id);
+      if (lane == 0) a.xs[(size_t)j * a.n_pad + f] = d;
+    }
 }
 
 // ------------------------------------------------------ attention ----
 
 __host__ __device__ __forceinline__ int kpos(int c, int D) { return (c & 7) * (D >> 3) + (c >> 3); }
 
-// grid frames * kv_heads, 256 threads; dynamic shared memory 2 * capacity floats.
-// The arithmetic of each part follows the single-session kernels: QK norm and
-// RoPE (QwenDecoder.cs:188-200, TensorMath.Rope.cs:51-53), scores with 8 lane
-// accumulators folded ((l0+l4)+(l1+l5))+((l2+l6)+(l3+l7)) and divided by
-// sqrt(128) (TensorMath.AttentionAvx.cs:87-159), softmax with the double lane
-// sum (TensorMath.SoftmaxAvx.cs:11-58) and the V sum per channel in position
+constexpr int kAttnCh = 32;        // positions per ring chunk (8 KB of K or V rows)
+constexpr int kAttnSlots = 6;      // ring chunks in flight
+constexpr int kAttnThreads = 288;  // 8 compute warps + 1 copy warp
+constexpr int kAttnRing = kAttnSlots * kAttnCh * 256;
+
+__host__ __device__ constexpr size_t attn_smem_bytes(int capacity) {
+  return (size_t)kAttnRing + 16 * kAttnSlots + (size_t)2 * capacity * 4;
+}
+
+__device__ __forceinline__ void csync256() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
+
+// grid frames * kv_heads, 288 threads.  Warp 8 streams the session's K rows
+// [0, len) and then its V rows through a ring of 32-position chunks with bulk
+// async copies; warps 0-7 compute.  The arithmetic of each part follows the
+// single-session kernels: QK norm and RoPE (QwenDecoder.cs:188-200,
+// TensorMath.Rope.cs:51-53), scores with 8 lane accumulators folded
+// ((l0+l4)+(l1+l5))+((l2+l6)+(l3+l7)) and divided by sqrt(128)
+// (TensorMath.AttentionAvx.cs:87-159), softmax with the double lane sum
+// (TensorMath.SoftmaxAvx.cs:11-58) and the V sum per channel in position
 // order (TensorMath.AttentionAvx.cs:173-224).
-__global__ void __launch_bounds__(256) batch_attn_kernel(const BatchAttnArgs a) {
-  constexpr int D = 128, M = D / 8, HALF = D / 2;
-  extern __shared__ __align__(16) float sc[];  // [2][capacity] scores, then probabilities
+__global__ void __launch_bounds__(kAttnThreads) batch_attn_kernel(const BatchAttnArgs a) {
+  constexpr int D = 128, M = D / 8, HALF = D / 2, CH = kAttnCh, RS = kAttnSlots;
+  extern __shared__ __align__(128) uint8_t smraw[];
+  uint8_t* ring = smraw;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smraw + kAttnRing);
+  uint64_t* empty = full + RS;
+  float* sc = reinterpret_cast<float*>(empty + RS);  // [capacity][2]: both heads' scores, then probabilities
   __shared__ float y[2][D];
   __shared__ float qs[2][D];
   __shared__ double red[8];
   __shared__ float red_f[8];
   __shared__ double lanes[2][8];
   __shared__ float s_inv[2];
+  __shared__ int abort_flag;
   const int f = blockIdx.x / a.kv_heads, g = blockIdx.x - f * a.kv_heads;
-  const int tid = threadIdx.x, h = tid >> 7, c = tid & (D - 1), warp = tid >> 5, lane = tid & 31;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int qw = a.heads * D, kvw = a.kv_heads * D;
-  const int p = a.pos[f], len = p + 1;
-  const float* base = a.qkv + (size_t)f * (qw + 2 * kvw);
+  const int p = a.pos[f], len = p + 1, nch = (len + CH - 1) / CH;
   __half* kc = a.k_tab[f] + a.layer_off + (size_t)g * a.capacity * D;
   __half* vc = a.v_tab[f] + a.layer_off + (size_t)g * a.capacity * D;
+  if (tid == 0) {
+    griddep_launch();
+    for (int i = 0; i < RS; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 8);
+    }
+    abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+
+  if (warp == 8) {
+    // ---- copy warp: K chunks 0..nch-1, then V chunks; the chunk holding
+    // position p only after the compute warps wrote row p (barrier 2) ----
+    bool synced = false;
+    int issued = 0;
+    for (int i = 0; i < 2 * nch; ++i) {
+      const int slot = i % RS;
+      if (i >= RS &&
+          !__all_sync(0xffffffffu, wait_phase(&empty[slot], ((i / RS) - 1) & 1, &abort_flag, a.err, kBatchWaitFree)))
+        break;
+      if (!synced && i >= nch - 1) {
+        asm volatile("bar.sync 2, 288;" ::: "memory");
+        synced = true;
+      }
+      const int c = i < nch ? i : i - nch;
+      const __half* src = (i < nch ? kc : vc) + (size_t)c * CH * D;
+      const unsigned bytes = (unsigned)(min(len, (c + 1) * CH) - c * CH) * (D * 2);
+      if (lane == 0) {
+        mbar_expect_tx(&full[slot], bytes);
+        bulk_g2s(ring + slot * (CH * 256), src, bytes, &full[slot]);
+      }
+      issued = i + 1;
+    }
+    if (!synced) asm volatile("bar.sync 2, 288;" ::: "memory");
+    if (lane == 0)
+      for (int i = issued > RS ? issued - RS : 0; i < issued; ++i)
+        wait_phase(&full[i % RS], (i / RS) & 1, &abort_flag, a.err, kBatchWaitLoad, false);
+    __syncwarp();
+    return;
+  }
+
+  // Rows [0, p) of the caches were written by earlier steps, so the copy warp
+  // streams them without waiting; q/k/v and every write wait for the
+  // projection before.
+  griddep_wait();
+  const int h = tid >> 7, c = tid & (D - 1);
+  const float* base = a.qkv + (size_t)f * (qw + 2 * kvw);
   const int i = c < HALF ? c : c - HALF;
   const float co = a.rope_cos[(size_t)p * HALF + i], si = a.rope_sin[(size_t)p * HALF + i];
-
   // query heads 2g (h = 0) and 2g + 1 (h = 1): RMSNorm + RoPE into qs
   {
     const float v = base[(2 * g + h) * D + c];
     const double part = warp_sum_d(__dmul_rn((double)v, (double)v));
     if (lane == 0) red[warp] = part;
-    __syncthreads();
+    csync256();
     double var = 0.0;
     for (int w = 0; w < 4; ++w) var = __dadd_rn(var, red[4 * h + w]);
     y[h][c] = __fmul_rn(__fmul_rn(v, rms_inverse(var, D, a.eps)), a.q_norm[c]);
-    __syncthreads();
+    csync256();
     const float av = y[h][i], bv = y[h][i + HALF];
     qs[h][c] = c < HALF ? __fsub_rn(__fmul_rn(av, co), __fmul_rn(bv, si))
                         : __fadd_rn(__fmul_rn(av, si), __fmul_rn(bv, co));
-    __syncthreads();
+    csync256();
   }
   // key head g (h = 0): RMSNorm + RoPE + binary16 row at p; value head g (h = 1)
   {
@@ -531,24 +761,26 @@ __global__ void __launch_bounds__(256) batch_attn_kernel(const BatchAttnArgs a) 
     } else {
       vc[(size_t)p * D + c] = __float2half_rn(base[qw + kvw + g * D + c]);
     }
-    __syncthreads();
+    csync256();
     if (h == 0) {
       double var = 0.0;
       for (int w = 0; w < 4; ++w) var = __dadd_rn(var, red[w]);
       y[0][c] = __fmul_rn(__fmul_rn(v, rms_inverse(var, D, a.eps)), a.k_norm[c]);
     }
-    __syncthreads();
+    csync256();
     if (h == 0) {
       const float av = y[0][i], bv = y[0][i + HALF];
       const float o = c < HALF ? __fsub_rn(__fmul_rn(av, co), __fmul_rn(bv, si))
                                : __fadd_rn(__fmul_rn(av, si), __fmul_rn(bv, co));
       kc[(size_t)p * D + kpos(c, D)] = __float2half_rn(o);
     }
-    __syncthreads();
+    // row p reaches the copy warp's bulk copies (async proxy) after this fence
+    asm volatile("fence.proxy.async.global;" ::: "memory");
+    asm volatile("bar.arrive 2, 288;" ::: "memory");
   }
-  // scores of both query heads: 8 threads per position, 32 positions per pass
+  // scores of both query heads: 8 threads per position, one chunk per pass
   {
-    const int j = tid & 7, slot = tid >> 3;
+    const int j = tid & 7, slot8 = tid >> 3;
     float q0[M], q1[M];
 #pragma unroll
     for (int k = 0; k < M; ++k) {
@@ -556,11 +788,13 @@ __global__ void __launch_bounds__(256) batch_attn_kernel(const BatchAttnArgs a) 
       q1[k] = qs[1][j + 8 * k];
     }
     const float divisor = __fsqrt_rn((float)D);
-    for (int t0 = 0; t0 < len; t0 += 32) {
-      const int t = t0 + slot;
+    for (int ch = 0; ch < nch; ++ch) {
+      const int slot = ch % RS;
+      wait_phase(&full[slot], (ch / RS) & 1, &abort_flag, a.err, kBatchWaitLoad);
+      const int t = ch * CH + slot8;
       float acc0 = 0.0f, acc1 = 0.0f;
       if (t < len) {
-        const uint4* kr = reinterpret_cast<const uint4*>(kc + (size_t)t * D + j * M);
+        const uint4* kr = reinterpret_cast<const uint4*>(ring + slot * (CH * 256) + slot8 * 256 + j * 32);
         const uint4 ka = kr[0], kb = kr[1];
         const __half* kh0 = reinterpret_cast<const __half*>(&ka);
         const __half* kh1 = reinterpret_cast<const __half*>(&kb);
@@ -571,6 +805,8 @@ __global__ void __launch_bounds__(256) batch_attn_kernel(const BatchAttnArgs a) 
           acc1 = __fadd_rn(acc1, __fmul_rn(q1[k], kv));
         }
       }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[slot]);
       acc0 = __fadd_rn(acc0, __shfl_down_sync(0xffffffffu, acc0, 4));
       acc1 = __fadd_rn(acc1, __shfl_down_sync(0xffffffffu, acc1, 4));
       acc0 = __fadd_rn(acc0, __shfl_down_sync(0xffffffffu, acc0, 1));
@@ -578,54 +814,86 @@ __global__ void __launch_bounds__(256) batch_attn_kernel(const BatchAttnArgs a) 
       acc0 = __fadd_rn(acc0, __shfl_down_sync(0xffffffffu, acc0, 2));
       acc1 = __fadd_rn(acc1, __shfl_down_sync(0xffffffffu, acc1, 2));
       if (j == 0 && t < len) {
-        sc[t] = __fdiv_rn(acc0, divisor);
-        sc[a.capacity + t] = __fdiv_rn(acc1, divisor);
+        sc[2 * t] = __fdiv_rn(acc0, divisor);
+        sc[2 * t + 1] = __fdiv_rn(acc1, divisor);
       }
     }
   }
-  __syncthreads();
-  // softmax of head h over e = sc + h * capacity
-  float* e = sc + (size_t)h * a.capacity;
+  csync256();
+  // softmax of head h over e[2 t + h]
+  float* e = sc + h;
   float mx = -INFINITY;
-  for (int t = c; t < len; t += D) mx = fmaxf(mx, e[t]);
+  for (int t = c; t < len; t += D) mx = fmaxf(mx, e[2 * t]);
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
   if (lane == 0) red_f[warp] = mx;
-  __syncthreads();
+  csync256();
   mx = fmaxf(fmaxf(red_f[4 * h], red_f[4 * h + 1]), fmaxf(red_f[4 * h + 2], red_f[4 * h + 3]));
-  for (int t = c; t < len; t += D) e[t] = exp_ref(__fsub_rn(e[t], mx));
-  __syncthreads();
-  const int full = len & ~7;
+  for (int t = c; t < len; t += D) e[2 * t] = exp_ref(__fsub_rn(e[2 * t], mx));
+  csync256();
+  const int full8 = len & ~7;
   if (c < 8) {
     double acc = 0.0;
-    for (int t = c; t < full; t += 8) acc = __dadd_rn(acc, (double)e[t]);
+    for (int t = c; t < full8; t += 8) acc = __dadd_rn(acc, (double)e[2 * t]);
     lanes[h][c] = acc;
   }
-  __syncthreads();
+  csync256();
   if (c == 0) {
     const double s0 = __dadd_rn(lanes[h][0], lanes[h][4]), s1 = __dadd_rn(lanes[h][1], lanes[h][5]);
     const double s2 = __dadd_rn(lanes[h][2], lanes[h][6]), s3 = __dadd_rn(lanes[h][3], lanes[h][7]);
     double sum = __dadd_rn(__dadd_rn(s0, s2), __dadd_rn(s1, s3));
-    for (int t = full; t < len; ++t) sum = __dadd_rn(sum, (double)e[t]);
+    for (int t = full8; t < len; ++t) sum = __dadd_rn(sum, (double)e[2 * t]);
     s_inv[h] = __double2float_rn(__ddiv_rn(1.0, sum));
   }
-  __syncthreads();
+  csync256();
   const float inv = s_inv[h];
-  for (int t = c; t < len; t += D) e[t] = __fmul_rn(e[t], inv);
-  __syncthreads();
-  // V sum of channel c for head h, in position order, 8 loads ahead
-  const __half* vcol = vc + c;
-  float acc = 0.0f;
-  int t = 0;
-  for (; t + 8 <= len; t += 8) {
-    float v[8];
-#pragma unroll
-    for (int u = 0; u < 8; ++u) v[u] = __half2float(vcol[(size_t)(t + u) * D]);
-#pragma unroll
-    for (int u = 0; u < 8; ++u) acc = __fadd_rn(acc, __fmul_rn(v[u], e[t + u]));
+  for (int t = c; t < len; t += D) e[2 * t] = __fmul_rn(e[2 * t], inv);
+  csync256();
+  // V sums in position order, from the ring: thread c2 < 64 owns channels
+  // 2 c2 and 2 c2 + 1 of both heads (four chains per V load); the other warps
+  // only keep the ring's release count.
+  const int c2 = tid;
+  float s00 = 0.0f, s01 = 0.0f, s10 = 0.0f, s11 = 0.0f;  // s[head][channel parity]
+  const float2* p2 = reinterpret_cast<const float2*>(sc);
+  for (int ch = 0; ch < nch; ++ch) {
+    const int k = nch + ch, slot = k % RS;
+    wait_phase(&full[slot], (k / RS) & 1, &abort_flag, a.err, kBatchWaitLoad);
+    if (warp < 2) {
+      const __half2* vr = reinterpret_cast<const __half2*>(ring + slot * (CH * 256)) + c2;
+      const int t0 = ch * CH, n = min(CH, len - t0);
+#pragma unroll 4
+      for (int u = 0; u < n; ++u) {
+        const float2 v = __half22float2(vr[u * (D / 2)]);
+        const float2 pp = p2[t0 + u];
+        s00 = __fadd_rn(s00, __fmul_rn(v.x, pp.x));
+        s01 = __fadd_rn(s01, __fmul_rn(v.y, pp.x));
+        s10 = __fadd_rn(s10, __fmul_rn(v.x, pp.y));
+        s11 = __fadd_rn(s11, __fmul_rn(v.y, pp.y));
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[slot]);
   }
-  for (; t < len; ++t) acc = __fadd_rn(acc, __fmul_rn(__half2float(vcol[(size_t)t * D]), e[t]));
-  a.attn[(size_t)f * qw + (size_t)(2 * g + h) * D + c] = acc;
+  // back to thread = (head h, channel c) for the output and its quantisation
+  float* ob = &y[0][0];  // y[2][D] is free again
+  if (warp < 2) {
+    ob[2 * c2] = s00;
+    ob[2 * c2 + 1] = s01;
+    ob[D + 2 * c2] = s10;
+    ob[D + 2 * c2 + 1] = s11;
+  }
+  csync256();
+  const float acc = ob[h * D + c];
+  if (a.attn != nullptr) a.attn[(size_t)f * qw + (size_t)(2 * g + h) * D + c] = acc;
+  if (a.xq != nullptr) {
+    // TensorMath.Quantize of the output for the o projection: this warp's 32
+    // channels are one block of the q_width row.
+    const int k = (2 * g + h) * D + c;
+    float d, id;
+    block_scale(acc, d, id);
+    a.xq[(size_t)(f >> 3) * 8 * qw + (k >> 4) * 128 + (f & 7) * 16 + (k & 15)] = (int8_t)quant1(acc, id);
+    if (lane == 0) a.xs[(size_t)(k >> 5) * a.n_pad + f] = d;
+  }
 }
 
 // --------------------------------------------------- step bookkeeping ----
@@ -708,7 +976,7 @@ __global__ void __launch_bounds__(256) frame_argmax_kernel(const float* pv, cons
   if (threadIdx.x == 0) token[f] = t;
 }
 
-constexpr int kAttnMaxSmem = 200 * 1024;  // scores of two heads: capacity <= 25600
+constexpr int kAttnMaxSmem = 200 * 1024;  // ring + scores of two heads: capacity <= 19400
 
 template <int NS, bool F16S>
 void set_bmm_attr() {
@@ -716,10 +984,93 @@ void set_bmm_attr() {
                        BmmLayout<NS, F16S>::kTotal);
 }
 
+// Launch with programmatic stream serialization (overlaps this kernel's
+// launch and prologue with the tail of the previous kernel in the stream).
+template <typename... KArgs, typename... Args>
+void launch_pdl(void (*kernel)(KArgs...), int grid, int block, size_t smem, cudaStream_t stream, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(block);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  FA_CUDA(cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...));
+}
+
+int sm_count() {
+  static int count[64] = {};
+  int dev = 0;
+  FA_CUDA(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64) dev = 0;
+  if (count[dev] == 0) FA_CUDA(cudaDeviceGetAttribute(&count[dev], cudaDevAttrMultiProcessorCount, dev));
+  return count[dev];
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  if (!fn) throw Error(kErrCuda, "cuTensorMapEncodeTiled is unavailable");
+  return fn;
+}
+
+void encode(CUtensorMap* m, CUtensorMapDataType type, int rank, const void* base, const cuuint64_t* dims,
+            const cuuint64_t* strides, const cuuint32_t* box) {
+  const cuuint32_t estr[3] = {1, 1, 1};
+  const CUresult r = encode_fn()(m, type, rank, const_cast<void*>(base), dims, strides, box, estr,
+                                 CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                                 CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) throw Error(kErrCuda, "cuTensorMapEncodeTiled failed: " + std::to_string((int)r));
+}
+
+// Tensor maps over the weights' 8-row tile layout and the frame-tile operand.
+// Every box starts at an x coordinate that is a multiple of 16 bytes.
+BmmMaps make_maps(const BmmArgs& a, int ns) {
+  BmmMaps mp;
+  const int K = a.w.cols, S = a.w.scale_f16 ? 2 : 4;
+  {
+    const cuuint64_t dims[3] = {128, (cuuint64_t)K / 16, (cuuint64_t)a.w.tiles};
+    const cuuint64_t str[2] = {128, (cuuint64_t)a.w.tile_bytes};
+    const cuuint32_t box[3] = {128, 16, 16};
+    encode(&mp.a, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, a.w.base, dims, str, box);
+  }
+  {
+    const cuuint64_t dims[2] = {(cuuint64_t)(K / 32) * 8 * S, (cuuint64_t)a.w.tiles};
+    const cuuint64_t str[1] = {(cuuint64_t)a.w.tile_bytes};
+    const cuuint32_t box[2] = {(cuuint32_t)(64 * S), 16};
+    encode(&mp.sa, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, a.w.base + (size_t)8 * K, dims, str, box);
+  }
+  {
+    const cuuint64_t dims[3] = {128, (cuuint64_t)K / 16, (cuuint64_t)a.n_pad / 8};
+    const cuuint64_t str[2] = {128, (cuuint64_t)8 * K};
+    const cuuint32_t box[3] = {128, 16, (cuuint32_t)(ns / 8)};
+    encode(&mp.b, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, a.xq, dims, str, box);
+  }
+  {
+    const cuuint64_t dims[2] = {(cuuint64_t)a.n_pad, (cuuint64_t)K / 32};
+    const cuuint64_t str[1] = {(cuuint64_t)a.n_pad * 4};
+    const cuuint32_t box[2] = {(cuuint32_t)ns, 8};
+    encode(&mp.sb, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, a.xs, dims, str, box);
+  }
+  return mp;
+}
+
 template <int NS, bool F16S>
 void launch_bmm_t(const BmmArgs& a, cudaStream_t stream) {
-  const int grid = (a.w.rows / kBmmRows) * (a.n_pad / NS);
-  bmm_kernel<NS, F16S><<<grid, kBmmThreads, BmmLayout<NS, F16S>::kTotal, stream>>>(a);
+  const int items = (a.w.rows / kBmmRows) * (a.n_pad / NS);
+  const int grid = std::min(items, sm_count());
+  const BmmMaps maps = make_maps(a, NS);
+  launch_pdl(bmm_kernel<NS, F16S>, grid, kBmmThreads, BmmLayout<NS, F16S>::kTotal, stream, a, maps);
 }
 
 }  // namespace
@@ -727,9 +1078,11 @@ void launch_bmm_t(const BmmArgs& a, cudaStream_t stream) {
 void prepare_batch_kernels() {
   static std::once_flag once;
   std::call_once(once, [] {
+    set_bmm_attr<8, true>();
     set_bmm_attr<16, true>();
     set_bmm_attr<32, true>();
     set_bmm_attr<64, true>();
+    set_bmm_attr<8, false>();
     set_bmm_attr<16, false>();
     set_bmm_attr<32, false>();
     set_bmm_attr<64, false>();
@@ -739,13 +1092,20 @@ void prepare_batch_kernels() {
 
 bool bmm_supported(const Q8View& w) {
   return w.base != nullptr && w.rows > 0 && w.rows % kBmmRows == 0 && w.cols > 0 && w.cols % kBmmKc == 0 &&
+         w.cols <= kActMaxCols &&
          w.tile_bytes % 16 == 0 && (reinterpret_cast<uintptr_t>(w.base) & 15) == 0;
 }
 
-int bmm_frame_tile(int n_pad) {
-  if (n_pad % 64 == 0 && n_pad >= 256) return 64;
-  if (n_pad % 32 == 0 && n_pad >= 128) return 32;
-  return 16;
+// Frames per work item.  A work item's time is set by its chain of stage
+// copies and its epilogue, so the wider tile wins once it still leaves about
+// half the SMs an item (fewer items re-reading each weight tile from L2);
+// narrow tiles spread the 8-row-tile-poor projections (1024 rows) over more
+// SMs.  Measured on B200 with 64 and 256 frames.
+int bmm_frame_tile(int n_pad, int row_tiles) {
+  const int sms = sm_count();
+  for (int ns : {64, 32, 16})
+    if (n_pad % ns == 0 && 2 * row_tiles * (n_pad / ns) >= sms) return ns;
+  return 8;
 }
 
 void launch_bmm(const BmmArgs& a, cudaStream_t stream) {
@@ -755,25 +1115,35 @@ void launch_bmm(const BmmArgs& a, cudaStream_t stream) {
   prepare_batch_kernels();
   const bool f16 = a.w.scale_f16 != 0;
   switch (a.ns) {
+    case 8: f16 ? launch_bmm_t<8, true>(a, stream) : launch_bmm_t<8, false>(a, stream); break;
     case 16: f16 ? launch_bmm_t<16, true>(a, stream) : launch_bmm_t<16, false>(a, stream); break;
     case 32: f16 ? launch_bmm_t<32, true>(a, stream) : launch_bmm_t<32, false>(a, stream); break;
     case 64: f16 ? launch_bmm_t<64, true>(a, stream) : launch_bmm_t<64, false>(a, stream); break;
-    default: throw Error(kErrArgument, "batched projection: frame tile must be 16, 32 or 64");
+    default: throw Error(kErrArgument, "batched projection: frame tile must be 8, 16, 32 or 64");
   }
   FA_CUDA(cudaGetLastError());
 }
 
 void launch_act_quant(const ActQuantArgs& a, cudaStream_t stream) {
-  if (a.K % 32 != 0 || a.frames <= 0) throw Error(kErrArgument, "activation quantiser: bad shape");
-  act_quant_kernel<<<a.frames, 256, 0, stream>>>(a);
+  if (a.K % 256 != 0 || a.K > kActMaxCols || a.frames <= 0)
+    throw Error(kErrArgument, "activation quantiser: bad shape");
+  switch (a.K / 256) {
+    case 4: launch_pdl(act_quant_kernel<4>, a.frames, 256, 0, stream, a); break;
+    case 8: launch_pdl(act_quant_kernel<8>, a.frames, 256, 0, stream, a); break;
+    case 12: launch_pdl(act_quant_kernel<12>, a.frames, 256, 0, stream, a); break;
+    default: launch_pdl(act_quant_kernel<0>, a.frames, 256, 0, stream, a); break;
+  }
   FA_CUDA(cudaGetLastError());
 }
 
+bool batch_attention_fits(int capacity) { return attn_smem_bytes(capacity) <= (size_t)kAttnMaxSmem; }
+
 void launch_batch_attention(const BatchAttnArgs& a, cudaStream_t stream) {
-  const size_t smem = (size_t)2 * a.capacity * sizeof(float);
+  const size_t smem = attn_smem_bytes(a.capacity);
   if (smem > (size_t)kAttnMaxSmem) throw Error(kErrCapacity, "batched attention: capacity too large");
+  if (a.heads != 2 * a.kv_heads) throw Error(kErrArgument, "batched attention: paired GQA only");
   prepare_batch_kernels();
-  batch_attn_kernel<<<a.frames * a.kv_heads, 256, smem, stream>>>(a);
+  launch_pdl(batch_attn_kernel, a.frames * a.kv_heads, kAttnThreads, smem, stream, a);
   FA_CUDA(cudaGetLastError());
 }
 

@@ -21,6 +21,10 @@ namespace fa {
 constexpr int kFramePad = 16;
 constexpr int kBmmRows = 128;  // weight rows per CTA: the MMA's M
 constexpr int kBmmKc = 256;    // columns per pipeline stage (8 Q8 blocks)
+// Batched-projection epilogue beyond kernels.h's GemvEpilogue: the gate/up
+// SiLU product quantised per 32-block straight into the next projection's
+// frame-tile operand (qout / qout_s), never stored as floats.
+constexpr int kEpiSiluQuant = 4;
 
 inline int frame_pad(int n) { return (n + kFramePad - 1) / kFramePad * kFramePad; }
 
@@ -47,7 +51,7 @@ struct BmmArgs {
   const int8_t* xq = nullptr; // frame tiles
   const float* xs = nullptr;  // [cols/32 x n_pad]
   int frames = 0, n_pad = 0;
-  int ns = 16;                // frames per CTA (16, 32 or 64; divides n_pad)
+  int ns = 16;                // frames per work item (8, 16, 32 or 64; divides n_pad)
   int epilogue = kEpiStore;
   float* out = nullptr;       // [frames x out_stride]
   int out_stride = 0;
@@ -60,10 +64,13 @@ struct BmmArgs {
   float* part_value = nullptr;  // [rows/128 x n_pad]
   int* part_index = nullptr;
   int* row0_nan = nullptr;      // [n_pad]
+  int8_t* qout = nullptr;       // kEpiSiluQuant: frame tiles of the [frames x rows/2] result
+  float* qout_s = nullptr;      //   and its block scales [rows/64 x qout_npad]
+  int qout_npad = 0;
   int* err = nullptr;           // device error word (kernel wait that gave up)
 };
 bool bmm_supported(const Q8View& w);
-int bmm_frame_tile(int n_pad);
+int bmm_frame_tile(int n_pad, int row_tiles);
 void launch_bmm(const BmmArgs& a, cudaStream_t stream);
 void prepare_batch_kernels();
 
@@ -94,9 +101,15 @@ struct BatchAttnArgs {
   size_t layer_off = 0;             // elements from a cache base to this layer
   const int* pos = nullptr;         // [frames] KV length before this step
   int capacity = 0;
-  float* attn = nullptr;            // [frames x q_width]
+  float* attn = nullptr;            // [frames x q_width] (optional)
+  int8_t* xq = nullptr;             // optional: the output quantised into frame tiles
+  float* xs = nullptr;              //   and its block scales [q_width/32 x n_pad]
+  int n_pad = 0;
+  int* err = nullptr;               // device error word (a ring wait that gave up)
 };
 void launch_batch_attention(const BatchAttnArgs& a, cudaStream_t stream);
+// Whether the attention kernel's shared memory holds a KV capacity's scores.
+bool batch_attention_fits(int capacity);
 
 // Per-step bookkeeping of a batch: each session's device position and token
 // words, gathered before the step and written back after its argmax.

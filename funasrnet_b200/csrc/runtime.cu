@@ -160,7 +160,7 @@ struct fa_session {
   DevBuf mx, mqkv, mattn, ma, mact, mpv, mpi, mctrl;
   bool trace = false;
   DevBuf trace_buf;                          // [grid x kTraceEvents] phase timestamps
-  DevBuf bxq, bxs;                           // frame-tile operands of tensor-core prefill projections
+  DevBuf bxq, bxs, bxq2, bxs2;               // frame-tile operands of tensor-core prefill projections
   int* d_int(int i) const { return ints.as<int>() + i; }
 };
 
@@ -300,11 +300,37 @@ int fa_weight_release(fa_backend* b, fa_weight* w) {
 
 namespace {
 
+// Tensor-core projection of `frames` activation rows already in frame tiles
+// (xq, xs) with epilogue `epi` (batch.cu); kEpiSiluQuant writes the next
+// operand to (qout, qout_s) instead of floats.
+void launch_proj(cudaStream_t st, const Q8View& w, const int8_t* xq, const float* xs, int frames, int epi, float* out,
+                 int out_stride, const float* res, const float* bias, int* err, int8_t* qout = nullptr,
+                 float* qout_s = nullptr) {
+  const int n_pad = frame_pad(frames);
+  BmmArgs b;
+  b.w = w;
+  b.xq = xq;
+  b.xs = xs;
+  b.frames = frames;
+  b.n_pad = n_pad;
+  b.ns = bmm_frame_tile(n_pad, w.rows / kBmmRows);
+  b.epilogue = epi;
+  b.out = out;
+  b.out_stride = out_stride;
+  b.res = res;
+  b.bias = bias;
+  b.qout = qout;
+  b.qout_s = qout_s;
+  b.qout_npad = n_pad;
+  b.err = err;
+  launch_bmm(b, st);
+}
+
 // [RMSNorm] + quantisation of `frames` activation rows into the frame-tile
 // operand, then the tensor-core projection with epilogue `epi` (batch.cu).
 void enqueue_bmm(cudaStream_t st, const Q8View& w, const float* x, int x_stride, int frames, const float* gamma,
                  float eps, int8_t* xq, float* xs, int epi, float* out, int out_stride, const float* res,
-                 const float* bias, int* err) {
+                 const float* bias, int* err, int8_t* qout = nullptr, float* qout_s = nullptr) {
   const int n_pad = frame_pad(frames);
   ActQuantArgs q;
   q.x = x;
@@ -317,20 +343,7 @@ void enqueue_bmm(cudaStream_t st, const Q8View& w, const float* x, int x_stride,
   q.xs = xs;
   q.n_pad = n_pad;
   launch_act_quant(q, st);
-  BmmArgs b;
-  b.w = w;
-  b.xq = xq;
-  b.xs = xs;
-  b.frames = frames;
-  b.n_pad = n_pad;
-  b.ns = bmm_frame_tile(n_pad);
-  b.epilogue = epi;
-  b.out = out;
-  b.out_stride = out_stride;
-  b.res = res;
-  b.bias = bias;
-  b.err = err;
-  launch_bmm(b, st);
+  launch_proj(st, w, xq, xs, frames, epi, out, out_stride, res, bias, err, qout, qout_s);
 }
 
 }  // namespace
@@ -1009,10 +1022,12 @@ void enqueue_layer_bmm(fa_session* s, int l, int frames) {
   launch_attention(a, st);
   enqueue_bmm(st, L.o, s->attn.as<float>(), qw, frames, nullptr, m->eps, xq, xs, kEpiResidual, s->a.as<float>(), W,
               s->x.as<float>(), nullptr, err);
-  enqueue_bmm(st, L.gateup, s->a.as<float>(), W, frames, L.ffn_norm, m->eps, xq, xs, kEpiSiluPair,
-              s->act.as<float>(), m->ffn, nullptr, nullptr, err);
-  enqueue_bmm(st, L.down, s->act.as<float>(), m->ffn, frames, nullptr, m->eps, xq, xs, kEpiResidual,
-              s->x.as<float>(), W, s->a.as<float>(), nullptr, err);
+  // SiLU(gate) * up quantised in the gate/up epilogue straight into the down
+  // projection's operand (a second buffer: the first is this launch's input)
+  enqueue_bmm(st, L.gateup, s->a.as<float>(), W, frames, L.ffn_norm, m->eps, xq, xs, kEpiSiluQuant, nullptr,
+              m->ffn, nullptr, nullptr, err, s->bxq2.as<int8_t>(), s->bxs2.as<float>());
+  launch_proj(st, L.down, s->bxq2.as<int8_t>(), s->bxs2.as<float>(), frames, kEpiResidual, s->x.as<float>(), W,
+              s->a.as<float>(), nullptr, err);
 }
 
 // QwenDecoder.Decode's layer loop (QwenDecoder.cs:180-252) for `frames`
@@ -1287,10 +1302,14 @@ int fa_session_create(fa_model* m, fa_session** out) {
     FA_CUDA(cudaMemset(s->ints.p, 0, kSessionInts * 4));
     if (m->bmm_ok) {
       const int kmax = std::max(std::max(W, qw), m->ffn);
-      s->bxq.ensure((size_t)frame_pad(F) * kmax);
-      s->bxs.ensure((size_t)frame_pad(F) * (kmax / 32) * 4);
-      FA_CUDA(cudaMemset(s->bxq.p, 0, s->bxq.bytes));
-      FA_CUDA(cudaMemset(s->bxs.p, 0, s->bxs.bytes));
+      for (DevBuf* q : {&s->bxq, &s->bxq2}) {
+        q->ensure((size_t)frame_pad(F) * kmax);
+        FA_CUDA(cudaMemset(q->p, 0, q->bytes));
+      }
+      for (DevBuf* q : {&s->bxs, &s->bxs2}) {
+        q->ensure((size_t)frame_pad(F) * (kmax / 32) * 4);
+        FA_CUDA(cudaMemset(q->p, 0, q->bytes));
+      }
     }
     s->end_ids.ensure(64 * 4);
     s->log_cap = m->capacity;
@@ -1718,7 +1737,7 @@ struct fa_batch {
   int device = 0, n = 0, n_pad = 0, row_tiles = 0;
   cudaStream_t stream = nullptr;
   std::mutex mu;
-  DevBuf x, a, qkv, attn, act, xq, xs, pv, pi, row0, ints, tabs, log, logits, feed;
+  DevBuf x, a, qkv, xq, xs, xq2, xs2, pv, pi, row0, ints, tabs, log, logits, feed;
   // ints: [0, n) positions, [n, 2n) tokens, 2n step counter, 2n + 1 error word
   int log_cap = 0;
   cudaGraphExec_t graph = nullptr;
@@ -1785,14 +1804,17 @@ void enqueue_batch_step(fa_batch* b, bool want_logits) {
     at.layer_off = (size_t)l * m->capacity * kvw;
     at.pos = b->d_pos();
     at.capacity = m->capacity;
-    at.attn = b->attn.as<float>();
+    at.attn = nullptr;  // quantised straight into the o projection's operand
+    at.xq = xq;
+    at.xs = xs;
+    at.n_pad = b->n_pad;
+    at.err = err;
     launch_batch_attention(at, st);
-    enqueue_bmm(st, L.o, b->attn.as<float>(), qw, n, nullptr, m->eps, xq, xs, kEpiResidual, b->a.as<float>(), W,
-                b->x.as<float>(), nullptr, err);
-    enqueue_bmm(st, L.gateup, b->a.as<float>(), W, n, L.ffn_norm, m->eps, xq, xs, kEpiSiluPair, b->act.as<float>(),
-                m->ffn, nullptr, nullptr, err);
-    enqueue_bmm(st, L.down, b->act.as<float>(), m->ffn, n, nullptr, m->eps, xq, xs, kEpiResidual, b->x.as<float>(),
-                W, b->a.as<float>(), nullptr, err);
+    launch_proj(st, L.o, xq, xs, n, kEpiResidual, b->a.as<float>(), W, b->x.as<float>(), nullptr, err);
+    enqueue_bmm(st, L.gateup, b->a.as<float>(), W, n, L.ffn_norm, m->eps, xq, xs, kEpiSiluQuant, nullptr, m->ffn,
+                nullptr, nullptr, err, b->xq2.as<int8_t>(), b->xs2.as<float>());
+    launch_proj(st, L.down, b->xq2.as<int8_t>(), b->xs2.as<float>(), n, kEpiResidual, b->x.as<float>(), W,
+                b->a.as<float>(), nullptr, err);
   }
   ActQuantArgs q;
   q.x = b->x.as<float>();
@@ -1811,7 +1833,7 @@ void enqueue_batch_step(fa_batch* b, bool want_logits) {
   h.xs = xs;
   h.frames = n;
   h.n_pad = b->n_pad;
-  h.ns = bmm_frame_tile(b->n_pad);
+  h.ns = bmm_frame_tile(b->n_pad, m->lm.rows / kBmmRows);
   h.epilogue = kEpiArgmax;
   h.logits = want_logits ? b->logits.as<float>() : nullptr;
   h.logits_stride = m->vocab;
@@ -1900,7 +1922,7 @@ int fa_batch_create(fa_session* const* sessions, int n, fa_batch** out) {
       if (!sessions[i] || sessions[i]->m != m) throw Error(kErrArgument, "sessions must share one model");
       if (!seen.insert(sessions[i]).second) throw Error(kErrArgument, "a session appears twice");
     }
-    if (!m->bmm_ok || (size_t)2 * m->capacity * 4 > 200 * 1024) return (int)kDeclined;
+    if (!m->bmm_ok || !batch_attention_fits(m->capacity)) return (int)kDeclined;
     auto b = std::make_unique<fa_batch>();
     b->m = m;
     b->sessions.assign(sessions, sessions + n);
@@ -1915,12 +1937,14 @@ int fa_batch_create(fa_session* const* sessions, int n, fa_batch** out) {
     b->x.ensure(np * W * 4);
     b->a.ensure(np * W * 4);
     b->qkv.ensure(np * (qw + 2 * kvw) * 4);
-    b->attn.ensure(np * qw * 4);
-    b->act.ensure(np * m->ffn * 4);
-    b->xq.ensure(np * kmax);
-    b->xs.ensure(np * (kmax / 32) * 4);
-    FA_CUDA(cudaMemset(b->xq.p, 0, b->xq.bytes));  // padded frames stay zero
-    FA_CUDA(cudaMemset(b->xs.p, 0, b->xs.bytes));
+    for (DevBuf* q : {&b->xq, &b->xq2}) {
+      q->ensure(np * kmax);
+      FA_CUDA(cudaMemset(q->p, 0, q->bytes));  // padded frames stay zero
+    }
+    for (DevBuf* q : {&b->xs, &b->xs2}) {
+      q->ensure(np * (kmax / 32) * 4);
+      FA_CUDA(cudaMemset(q->p, 0, q->bytes));
+    }
     b->pv.ensure((size_t)b->row_tiles * np * 4);
     b->pi.ensure((size_t)b->row_tiles * np * 4);
     b->row0.ensure(np * 4);
