@@ -647,7 +647,7 @@ __global__ void __launch_bounds__(256) act_quant_kernel(const ActQuantArgs a) {
 __host__ __device__ __forceinline__ int kpos(int c, int D) { return (c & 7) * (D >> 3) + (c >> 3); }
 
 constexpr int kAttnCh = 32;        // positions per ring chunk (8 KB of K or V rows)
-constexpr int kAttnSlots = 6;      // ring chunks in flight
+constexpr int kAttnSlots = 6;      // ring chunks in flight (four CTAs per SM)
 constexpr int kAttnThreads = 288;  // 8 compute warps + 1 copy warp
 constexpr int kAttnRing = kAttnSlots * kAttnCh * 256;
 
@@ -680,7 +680,10 @@ __global__ void __launch_bounds__(kAttnThreads) batch_attn_kernel(const BatchAtt
   __shared__ double lanes[2][8];
   __shared__ float s_inv[2];
   __shared__ int abort_flag;
-  const int f = blockIdx.x / a.kv_heads, g = blockIdx.x - f * a.kv_heads;
+  // CTAs take sessions longest first (a.order): the long ones start in the
+  // first wave and the short ones fill the SMs they leave.
+  const int fi = blockIdx.x / a.kv_heads, g = blockIdx.x - fi * a.kv_heads;
+  const int f = a.order != nullptr ? a.order[fi] : fi;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int qw = a.heads * D, kvw = a.kv_heads * D;
   const int p = a.pos[f], len = p + 1, nch = (len + CH - 1) / CH;
@@ -730,12 +733,13 @@ __global__ void __launch_bounds__(kAttnThreads) batch_attn_kernel(const BatchAtt
 
   // Rows [0, p) of the caches were written by earlier steps, so the copy warp
   // streams them without waiting; q/k/v and every write wait for the
-  // projection before.
-  griddep_wait();
+  // projection before.  The RoPE row and norm weights are constants.
   const int h = tid >> 7, c = tid & (D - 1);
   const float* base = a.qkv + (size_t)f * (qw + 2 * kvw);
   const int i = c < HALF ? c : c - HALF;
   const float co = a.rope_cos[(size_t)p * HALF + i], si = a.rope_sin[(size_t)p * HALF + i];
+  const float gq = a.q_norm[c], gk = a.k_norm[c];
+  griddep_wait();
   // query heads 2g (h = 0) and 2g + 1 (h = 1): RMSNorm + RoPE into qs
   {
     const float v = base[(2 * g + h) * D + c];
@@ -744,7 +748,7 @@ __global__ void __launch_bounds__(kAttnThreads) batch_attn_kernel(const BatchAtt
     csync256();
     double var = 0.0;
     for (int w = 0; w < 4; ++w) var = __dadd_rn(var, red[4 * h + w]);
-    y[h][c] = __fmul_rn(__fmul_rn(v, rms_inverse(var, D, a.eps)), a.q_norm[c]);
+    y[h][c] = __fmul_rn(__fmul_rn(v, rms_inverse(var, D, a.eps)), gq);
     csync256();
     const float av = y[h][i], bv = y[h][i + HALF];
     qs[h][c] = c < HALF ? __fsub_rn(__fmul_rn(av, co), __fmul_rn(bv, si))
@@ -765,7 +769,7 @@ __global__ void __launch_bounds__(kAttnThreads) batch_attn_kernel(const BatchAtt
     if (h == 0) {
       double var = 0.0;
       for (int w = 0; w < 4; ++w) var = __dadd_rn(var, red[w]);
-      y[0][c] = __fmul_rn(__fmul_rn(v, rms_inverse(var, D, a.eps)), a.k_norm[c]);
+      y[0][c] = __fmul_rn(__fmul_rn(v, rms_inverse(var, D, a.eps)), gk);
     }
     csync256();
     if (h == 0) {
@@ -961,7 +965,7 @@ __global__ void __launch_bounds__(256) batch_finish_kernel(const BatchStep s) {
     // decodes it: the log holds this step's input token.
     if (s.log != nullptr) {
       const int step = *s.counter - 1;
-      if (step >= 0 && step < s.log_cap) s.log[(size_t)step * s.frames + f] = s.tok[f];
+      if (step >= 0 && step < s.log_cap) s.log[(size_t)step * s.log_stride + s.frame0 + f] = s.tok[f];
     }
     s.tok[f] = token;
     *s.stok[f] = token;

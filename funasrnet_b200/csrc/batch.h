@@ -100,6 +100,7 @@ struct BatchAttnArgs {
   __half* const* v_tab = nullptr;
   size_t layer_off = 0;             // elements from a cache base to this layer
   const int* pos = nullptr;         // [frames] KV length before this step
+  const int* order = nullptr;       // optional [frames]: sessions by descending length
   int capacity = 0;
   float* attn = nullptr;            // [frames x q_width] (optional)
   int8_t* xq = nullptr;             // optional: the output quantised into frame tiles
@@ -119,8 +120,10 @@ struct BatchStep {
   int* pos = nullptr;          // [frames] batch copy of the positions
   int* tok = nullptr;          // [frames] batch copy of the tokens
   int* counter = nullptr;      // steps taken since the log was reset
-  int* log = nullptr;          // [log_cap x frames] emitted tokens (optional)
+  int* log = nullptr;          // [log_cap x log_stride] emitted tokens (optional)
   int log_cap = 0;
+  int log_stride = 0;          // sessions of the whole batch
+  int frame0 = 0;              // this part's first session in the batch
   const float* part_value = nullptr;
   const int* part_index = nullptr;
   const int* row0_nan = nullptr;
