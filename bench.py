@@ -22,6 +22,7 @@ Multi-GPU (torchrun): one process per GPU, each its own replica and sessions
 from __future__ import annotations
 
 import argparse
+import contextlib
 import json
 import os
 import statistics
@@ -173,13 +174,23 @@ def oracle_decode_rate(path: Path, cfg, steps: int, warmup: int, threads: int):
 MEASURED_TRAFFIC_PER_STEP = {"bs1_400": 0.6833e9}
 
 
-def batch_bench(be, path, name, steps, warmup, rank, world, dist, local, barrier):
+def profile_range(on: bool):
+    """cudaProfilerStart/Stop around the timed region, for `ncu --profile-from-start off`."""
+    if not on:
+        return contextlib.nullcontext()
+    import torch
+
+    return torch.cuda.profiler.profile()
+
+
+def batch_bench(be, path, name, steps, warmup, rank, world, dist, local, barrier, sessions=None, profile=False):
     """Config 4/5: `n` ragged sessions decoded together.  Returns the result dict
     (rank 0's view; device times are max over ranks)."""
     from funasrnet_b200.decoder import BatchDecoder, CudaModel, QwenDecoder
     from funasrnet_b200.shard import max_over_ranks
 
     n, tokens = BATCH_CONFIGS[name]
+    n = sessions or n
     steps = min(steps, tokens)
     cm = CudaModel(be, path, capacity=BATCH_CAPACITY)
     rng = np.random.default_rng(SEED + 17 * (rank + 1))
@@ -200,7 +211,7 @@ def batch_bench(be, path, name, steps, warmup, rank, world, dist, local, barrier
         prefill_all()
         pos0 = np.array([d.position for d in sessions], np.float64)
         barrier()
-        with ClockSampler(local) as clocks:
+        with ClockSampler(local) as clocks, profile_range(profile):
             toks = b.generate(steps)
         dev_ms = max_over_ranks(b.last_ms(), dist, f"cuda:{local}")
         assert toks.shape == (steps, n)
@@ -253,6 +264,9 @@ def main():
     ap.add_argument("--impl", choices=["cuda", "reference"], default="cuda")
     ap.add_argument("--config", choices=sorted(CONFIGS) + sorted(BATCH_CONFIGS), default="bs1_400")
     ap.add_argument("--no-batched", action="store_true", help="skip the bs64/bs256 lines of the default run")
+    ap.add_argument("--sessions", type=int, default=None, help="batched configs: sessions per GPU (profiling runs)")
+    ap.add_argument("--profile-range", action="store_true",
+                    help="bracket the timed region with cudaProfilerStart/Stop (ncu --profile-from-start off)")
     ap.add_argument("--cpu-baseline-steps", type=int, default=24)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
@@ -311,7 +325,8 @@ def main():
     path = ensure_model(quantized, rank, barrier)
     be = CudaFloatBackend(local)
     if batched:
-        r = batch_bench(be, path, args.config, args.steps, warmup, rank, world, dist, local, barrier)
+        r = batch_bench(be, path, args.config, args.steps, warmup, rank, world, dist, local, barrier,
+                        sessions=args.sessions, profile=args.profile_range)
         line = {"metric": r["metric"], "value": r["value"], "unit": "tokens/s", "n_gpus": world,
                 "steps": r["steps"], "warmup": warmup, "ms_per_step": r["ms_per_step"], "higher_is_better": True,
                 "scaling": "weak", "vs_baseline": None, "dtype": "int8 x int8 -> int32 (tcgen05), f32 accumulate",
@@ -335,7 +350,7 @@ def main():
     dec.reset()
     dec.decode(emb, frames, want_logits=False)
     barrier()
-    with ClockSampler(local) as clocks:
+    with ClockSampler(local) as clocks, profile_range(args.profile_range):
         toks = dec.generate(steps, end_ids=())
     dev_ms = dec.last_generate_ms()
     assert len(toks) == steps
