@@ -58,6 +58,18 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, unsigned parity) {
       : "memory");
   return ok != 0;
 }
+// try_wait with a suspend-time hint: a waiting thread sleeps until the phase
+// completes (or ~1 us passes) instead of spinning on issue slots that the
+// working warps of the CTA need.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, unsigned parity) {
+  unsigned ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(saddr(bar)), "r"(parity), "r"(1000u)
+      : "memory");
+  return ok != 0;
+}
 __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, unsigned bytes, uint64_t* bar) {
   asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
                    saddr(dst)),
@@ -163,7 +175,7 @@ __device__ __noinline__ bool wait_phase(uint64_t* bar, unsigned parity, volatile
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer();
   for (unsigned it = 1;; ++it) {
-    if (mbar_try_wait(bar, parity)) return true;
+    if (mbar_try_wait_sleep(bar, parity)) return true;
     if ((it & 15) == 0) {
       if (honour_abort && *abort_flag) return false;
       if (globaltimer() - t0 > kWaitNs) {
@@ -447,14 +459,24 @@ __global__ void __launch_bounds__(kBmmThreads, 1) bmm_kernel(const BmmArgs a, co
           tc_wait_ld();
 #pragma unroll
           for (int u = 0; u < G; ++u) tmem_fill<HW>(lane_addr + gb * L::kGroupCols + u * NS, kMagicBits);
+          // All of the group's scales first, one finiteness test per group, so
+          // the blocks' products overlap and only the sums run in block order.
+          float wsv[G];
 #pragma unroll
           for (int u = 0; u < G; ++u) {
             const int kb = g8 * G + u;
-            const float ws = F16S ? __half2float(reinterpret_cast<const __half*>(st + t * L::kSAStride)[kb * 8 + r])
-                                  : reinterpret_cast<const float*>(st + t * L::kSAStride)[kb * 8 + r];
-            const float4* xs4 = reinterpret_cast<const float4*>(st + L::kSB + (kb * NS + h * HW) * 4);
-            if (F16S && fabsf(ws) <= 65504.0f) {
-              const float nc = __fmul_rn(ws, -kMagic);  // exact: ws has 11 significant bits
+            wsv[u] = F16S ? __half2float(reinterpret_cast<const __half*>(st + t * L::kSAStride)[kb * 8 + r])
+                          : reinterpret_cast<const float*>(st + t * L::kSAStride)[kb * 8 + r];
+          }
+          bool finite = F16S;
+#pragma unroll
+          for (int u = 0; u < G; ++u) finite = finite && fabsf(wsv[u]) <= 65504.0f;
+          if (finite) {
+#pragma unroll
+            for (int u = 0; u < G; ++u) {
+              const int kb = g8 * G + u;
+              const float nc = __fmul_rn(wsv[u], -kMagic);  // exact: ws has 11 significant bits
+              const float4* xs4 = reinterpret_cast<const float4*>(st + L::kSB + (kb * NS + h * HW) * 4);
 #pragma unroll
               for (int j4 = 0; j4 < HW / 4; ++j4) {
                 const float4 x = xs4[j4];
@@ -462,10 +484,15 @@ __global__ void __launch_bounds__(kBmmThreads, 1) bmm_kernel(const BmmArgs a, co
 #pragma unroll
                 for (int e = 0; e < 4; ++e) {
                   const int j = 4 * j4 + e;
-                  acc[j] = __fadd_rn(acc[j], __fmul_rn(__fmaf_rn(__uint_as_float(v[u * HW + j]), ws, nc), xv[e]));
+                  acc[j] = __fadd_rn(acc[j], __fmul_rn(__fmaf_rn(__uint_as_float(v[u * HW + j]), wsv[u], nc), xv[e]));
                 }
               }
-            } else {
+            }
+          } else {
+#pragma unroll
+            for (int u = 0; u < G; ++u) {
+              const int kb = g8 * G + u;
+              const float4* xs4 = reinterpret_cast<const float4*>(st + L::kSB + (kb * NS + h * HW) * 4);
 #pragma unroll
               for (int j4 = 0; j4 < HW / 4; ++j4) {
                 const float4 x = xs4[j4];
@@ -474,7 +501,7 @@ __global__ void __launch_bounds__(kBmmThreads, 1) bmm_kernel(const BmmArgs a, co
                 for (int e = 0; e < 4; ++e) {
                   const int j = 4 * j4 + e;
                   const float dot = __fsub_rn(__uint_as_float(v[u * HW + j]), kMagic);  // exact integer
-                  acc[j] = __fadd_rn(acc[j], __fmul_rn(__fmul_rn(dot, ws), xv[e]));
+                  acc[j] = __fadd_rn(acc[j], __fmul_rn(__fmul_rn(dot, wsv[u]), xv[e]));
                 }
               }
             }
