@@ -83,6 +83,7 @@ SIGNATURES = {
     "fa_batch_size": (i32, [vp]),
     "fa_batch_step": (i32, [vp, vp, vp, vp]),
     "fa_batch_generate": (i32, [vp, i32, vp]),
+    "fa_batch_generate_until": (i32, [vp, i32, vp, i32, vp, vp]),
     "fa_batch_last_ms": (i32, [vp, P(f32)]),
 }
 

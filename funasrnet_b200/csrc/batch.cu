@@ -767,9 +767,12 @@ __global__ void __launch_bounds__(kAttnThreads) batch_attn_kernel(const BatchAtt
   const float co = a.rope_cos[(size_t)p * HALF + i], si = a.rope_sin[(size_t)p * HALF + i];
   const float gq = a.q_norm[c], gk = a.k_norm[c];
   griddep_wait();
+  // all three projections' values at once: one load latency
+  const float qv = base[(2 * g + h) * D + c];
+  const float kv_in = h == 0 ? base[qw + g * D + c] : base[qw + kvw + g * D + c];
   // query heads 2g (h = 0) and 2g + 1 (h = 1): RMSNorm + RoPE into qs
   {
-    const float v = base[(2 * g + h) * D + c];
+    const float v = qv;
     const double part = warp_sum_d(__dmul_rn((double)v, (double)v));
     if (lane == 0) red[warp] = part;
     csync256();
@@ -786,11 +789,11 @@ __global__ void __launch_bounds__(kAttnThreads) batch_attn_kernel(const BatchAtt
   {
     float v = 0.0f;
     if (h == 0) {
-      v = base[qw + g * D + c];
+      v = kv_in;
       const double part = warp_sum_d(__dmul_rn((double)v, (double)v));
       if (lane == 0) red[warp] = part;
     } else {
-      vc[(size_t)p * D + c] = __float2half_rn(base[qw + kvw + g * D + c]);
+      vc[(size_t)p * D + c] = __float2half_rn(kv_in);
     }
     csync256();
     if (h == 0) {
@@ -818,7 +821,6 @@ __global__ void __launch_bounds__(kAttnThreads) batch_attn_kernel(const BatchAtt
       q0[k] = qs[0][j + 8 * k];
       q1[k] = qs[1][j + 8 * k];
     }
-    const float divisor = __fsqrt_rn((float)D);
     for (int ch = 0; ch < nch; ++ch) {
       const int slot = ch % RS;
       wait_phase(&full[slot], (ch / RS) & 1, &abort_flag, a.err, kBatchWaitLoad);
@@ -844,9 +846,9 @@ __global__ void __launch_bounds__(kAttnThreads) batch_attn_kernel(const BatchAtt
       acc1 = __fadd_rn(acc1, __shfl_down_sync(0xffffffffu, acc1, 1));
       acc0 = __fadd_rn(acc0, __shfl_down_sync(0xffffffffu, acc0, 2));
       acc1 = __fadd_rn(acc1, __shfl_down_sync(0xffffffffu, acc1, 2));
-      if (j == 0 && t < len) {
-        sc[2 * t] = __fdiv_rn(acc0, divisor);
-        sc[2 * t + 1] = __fdiv_rn(acc1, divisor);
+      if (j == 0 && t < len) {  // raw dots; the division runs in the max pass, on every lane
+        sc[2 * t] = acc0;
+        sc[2 * t + 1] = acc1;
       }
     }
   }
@@ -854,7 +856,12 @@ __global__ void __launch_bounds__(kAttnThreads) batch_attn_kernel(const BatchAtt
   // softmax of head h over e[2 t + h]
   float* e = sc + h;
   float mx = -INFINITY;
-  for (int t = c; t < len; t += D) mx = fmaxf(mx, e[2 * t]);
+  const float divisor = __fsqrt_rn((float)D);
+  for (int t = c; t < len; t += D) {
+    const float s = __fdiv_rn(e[2 * t], divisor);  // dot / sqrt(128), as the scores pass would
+    e[2 * t] = s;
+    mx = fmaxf(mx, s);
+  }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
   if (lane == 0) red_f[warp] = mx;
@@ -988,24 +995,26 @@ __global__ void __launch_bounds__(256) batch_finish_kernel(const BatchStep s) {
   const int f = blockIdx.x;
   const int token = frame_argmax(s.part_value, s.part_index, s.row0_nan, s.row_tiles, s.n_pad, f);
   if (threadIdx.x == 0) {
-    // FunAsr.Transcribe (FunAsr.cs:167-178) appends the token it feeds, then
-    // decodes it: the log holds this step's input token.
-    if (s.log != nullptr) {
-      const int step = *s.counter - 1;
-      if (step >= 0 && step < s.log_cap) s.log[(size_t)step * s.log_stride + s.frame0 + f] = s.tok[f];
+    // FunAsr.Transcribe (FunAsr.cs:167-178): stop before an end token, else
+    // append the token fed and decode it; the log holds this step's input.
+    const int in = s.tok[f];
+    bool stop = s.stopped != nullptr && s.stopped[f] != 0;
+    if (!stop && s.ends != nullptr)
+      for (int i = 0; i < s.ends[0]; ++i) stop = stop || in == s.ends[1 + i];
+    const int step = *s.counter - 1;
+    if (s.log != nullptr && step >= 0 && step < s.log_cap)
+      s.log[(size_t)step * s.log_stride + s.frame0 + f] = stop ? -1 : in;
+    if (stop) {
+      if (s.stopped != nullptr) s.stopped[f] = 1;
+      return;  // position and token words stay
     }
     s.tok[f] = token;
+    s.pos[f] = s.pos[f] + 1;
     *s.stok[f] = token;
-    *s.spos[f] = s.pos[f] + 1;
+    *s.spos[f] = s.pos[f];
   }
 }
 
-__global__ void __launch_bounds__(256) frame_argmax_kernel(const float* pv, const int* pi, const int* row0_nan,
-                                                           int row_tiles, int n_pad, int* token) {
-  const int f = blockIdx.x;
-  const int t = frame_argmax(pv, pi, row0_nan, row_tiles, n_pad, f);
-  if (threadIdx.x == 0) token[f] = t;
-}
 
 constexpr int kAttnMaxSmem = 200 * 1024;  // ring + scores of two heads: capacity <= 19400
 
@@ -1193,10 +1202,5 @@ void launch_batch_finish(const BatchStep& s, cudaStream_t stream) {
   FA_CUDA(cudaGetLastError());
 }
 
-void launch_frame_argmax(const float* part_value, const int* part_index, const int* row0_nan, int row_tiles,
-                         int n_pad, int frames, int* token, cudaStream_t stream) {
-  frame_argmax_kernel<<<frames, 256, 0, stream>>>(part_value, part_index, row0_nan, row_tiles, n_pad, token);
-  FA_CUDA(cudaGetLastError());
-}
 
 }  // namespace fa

@@ -129,13 +129,14 @@ struct BatchStep {
   const int* row0_nan = nullptr;
   int row_tiles = 0, n_pad = 0;
   int frames = 0;
+  // End-token stop (ByteBpe.IsEnd): ends[0] = count, ends[1..] = ids.  A session
+  // whose input token is an end token stops: position, token and log stay.
+  const int* ends = nullptr;
+  int* stopped = nullptr;      // [frames]
 };
 void launch_batch_gather(const BatchStep& s, cudaStream_t stream);
 void launch_batch_finish(const BatchStep& s, cudaStream_t stream);
 // tokens [frames] (device) into each session's token word.
 void launch_batch_scatter(const BatchStep& s, const int* tokens, cudaStream_t stream);
-// Standalone per-frame argmax over bmm partials (multi-frame lm_head calls).
-void launch_frame_argmax(const float* part_value, const int* part_index, const int* row0_nan, int row_tiles,
-                         int n_pad, int frames, int* token, cudaStream_t stream);
 
 }  // namespace fa

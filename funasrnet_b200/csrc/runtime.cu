@@ -1743,6 +1743,7 @@ struct BatchPart {
   int* d_tok() const { return ints.as<int>() + n; }
   int* d_counter() const { return ints.as<int>() + 2 * n; }
   int* d_err() const { return ints.as<int>() + 2 * n + 1; }
+  int* d_stopped() const { return ints.as<int>() + 2 * n + 2; }  // [n]
 };
 
 struct fa_batch {
@@ -1754,6 +1755,7 @@ struct fa_batch {
   std::mutex mu;
   std::vector<std::unique_ptr<BatchPart>> parts;
   DevBuf log, logits, feed;
+  DevBuf ends;  // [0] = end-token count of the current call, [1..64] = ids
   int log_cap = 0;
   cudaGraphExec_t graph = nullptr;
   bool graph_logits = false;
@@ -1782,6 +1784,8 @@ BatchStep batch_state(fa_batch* b, BatchPart* p) {
   st.row_tiles = b->row_tiles;
   st.n_pad = p->n_pad;
   st.frames = p->n;
+  st.ends = b->ends.as<int>();
+  st.stopped = p->d_stopped();
   return st;
 }
 
@@ -1921,9 +1925,13 @@ void update_order(fa_batch* b) {
   }
 }
 
-// Launches the step graph `steps` times and checks the batched kernels' error words.
-void run_batch(fa_batch* b, int steps, bool want_logits) {
+// Launches the step graph `steps` times and checks the batched kernels' error
+// words; n_end end tokens (ids staged in b->pinned + 8) stop a session.
+void run_batch(fa_batch* b, int steps, bool want_logits, int n_end = 0) {
   update_order(b);
+  b->pinned[7] = n_end;
+  FA_CUDA(cudaMemcpyAsync(b->ends.p, b->pinned + 7, (size_t)(1 + n_end) * 4, cudaMemcpyHostToDevice, b->stream));
+  for (auto& p : b->parts) FA_CUDA(cudaMemsetAsync(p->d_stopped(), 0, (size_t)p->n * 4, b->stream));
   if (b->graph && b->graph_logits != want_logits) {
     cudaGraphExecDestroy(b->graph);
     b->graph = nullptr;
@@ -1946,9 +1954,13 @@ void run_batch(fa_batch* b, int steps, bool want_logits) {
       for (auto& p : b->parts) FA_CUDA(cudaMemset(p->d_err(), 0, 4));
       throw Error(kErrTimeout, "batched decode: a bounded wait gave up (code " + std::to_string(code) + ")");
     }
-  for (fa_session* s : b->sessions) {
-    s->pos += steps;
-    s->have_token = true;
+  // positions after the run (a stopped session stops advancing)
+  std::vector<int> pos(b->n);
+  for (auto& p : b->parts)
+    FA_CUDA(cudaMemcpy(pos.data() + p->f0, p->d_pos(), (size_t)p->n * 4, cudaMemcpyDeviceToHost));
+  for (int i = 0; i < b->n; ++i) {
+    b->sessions[i]->pos = pos[i];
+    b->sessions[i]->have_token = true;
   }
 }
 
@@ -2011,7 +2023,7 @@ int fa_batch_create(fa_session* const* sessions, int n, fa_batch** out) {
       p->pv.ensure((size_t)b->row_tiles * np * 4);
       p->pi.ensure((size_t)b->row_tiles * np * 4);
       p->row0.ensure(np * 4);
-      p->ints.ensure((2 * np + 8) * 4);
+      p->ints.ensure((3 * np + 8) * 4);
       FA_CUDA(cudaMemset(p->ints.p, 0, p->ints.bytes));
       std::vector<void*> tabs((size_t)4 * p->n);
       for (int i = 0; i < p->n; ++i) {
@@ -2028,9 +2040,11 @@ int fa_batch_create(fa_session* const* sessions, int n, fa_batch** out) {
     }
     b->log_cap = m->capacity;
     b->log.ensure((size_t)b->log_cap * n * 4);
+    b->ends.ensure(65 * 4);
+    FA_CUDA(cudaMemset(b->ends.p, 0, b->ends.bytes));
     FA_CUDA(cudaEventCreate(&b->ev0));
     FA_CUDA(cudaEventCreate(&b->ev1));
-    FA_CUDA(cudaMallocHost(&b->pinned, (size_t)(n + 8) * 4));
+    FA_CUDA(cudaMallocHost(&b->pinned, (size_t)(std::max(n, 64) + 8) * 4));
     prepare_kernels();
     prepare_batch_kernels();
     *out = b.release();
@@ -2086,6 +2100,28 @@ int fa_batch_step(fa_batch* b, const int32_t* tokens, int32_t* next, float* logi
       std::memcpy(next, b->pinned + 8, (size_t)b->n * 4);
     }
     if (logits) FA_CUDA(cudaMemcpy(logits, b->logits.p, (size_t)b->n * m->vocab * 4, cudaMemcpyDeviceToHost));
+    return (int)kHandled;
+  });
+}
+
+int fa_batch_generate_until(fa_batch* b, int max_steps, const int32_t* end_ids, int n_end, int32_t* tokens,
+                            int32_t* counts) {
+  return with_batch(b, [&] {
+    fa_model* m = b->m;
+    if (max_steps < 0 || n_end < 0 || n_end > 64 || (n_end > 0 && !end_ids) || (max_steps > 0 && !tokens) || !counts)
+      throw Error(kErrArgument, "invalid arguments");
+    for (fa_session* s : b->sessions) {
+      if (!s->have_token) throw Error(kErrArgument, "a session has no token: Decode with logits first");
+      if (s->pos + max_steps > m->capacity)
+        throw Error(kErrCapacity, "Decoder context exhausted or invalid embeddings");
+    }
+    for (int i = 0; i < b->n; ++i) counts[i] = 0;
+    if (max_steps == 0) return (int)kHandled;
+    if (n_end > 0) std::memcpy(b->pinned + 8, end_ids, (size_t)n_end * 4);
+    run_batch(b, max_steps, false, n_end);
+    FA_CUDA(cudaMemcpy(tokens, b->log.p, (size_t)max_steps * b->n * 4, cudaMemcpyDeviceToHost));
+    for (int i = 0; i < b->n; ++i)
+      while (counts[i] < max_steps && tokens[(size_t)counts[i] * b->n + i] >= 0) ++counts[i];
     return (int)kHandled;
   });
 }

@@ -219,6 +219,16 @@ class BatchDecoder:
         check(lib().fa_batch_generate(self._h, int(steps), ptr(out)))
         return out[:steps]
 
+    def generate_until(self, max_steps: int, end_ids=QWEN_END_TOKENS) -> list[list[int]]:
+        """The Transcribe loop with its end-token stop, per session (as QwenDecoder.generate)."""
+        ends = np.ascontiguousarray(end_ids, dtype=np.int32)
+        n = len(self.sessions)
+        out = np.empty((max(1, max_steps), n), np.int32)
+        counts = np.zeros(n, np.int32)
+        check(lib().fa_batch_generate_until(self._h, int(max_steps), ptr(ends) if ends.size else None, ends.size,
+                                            ptr(out), ptr(counts)))
+        return [out[: counts[i], i].tolist() for i in range(n)]
+
     def last_ms(self) -> float:
         ms = C.c_float()
         check(lib().fa_batch_last_ms(self._h, C.byref(ms)))

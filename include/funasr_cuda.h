@@ -233,6 +233,12 @@ int fa_batch_step(fa_batch* batch, const int32_t* tokens, int32_t* next, float* 
  * argmax) and decodes it.  Emits what fa_session_generate with no end ids
  * emits.  tokens [steps x n]: token of session i at step t is tokens[t * n + i]. */
 int fa_batch_generate(fa_batch* batch, int steps, int32_t* tokens);
+/* The same loop with the end-token stop of fa_session_generate (ByteBpe.IsEnd,
+ * FunAsr.cs:167-178): a session stops before an end token; later entries of its
+ * column in tokens [max_steps x n] are -1 and counts[i] is the number of tokens
+ * session i emitted.  Stopped sessions keep their position and token. */
+int fa_batch_generate_until(fa_batch* batch, int max_steps, const int32_t* end_ids, int n_end, int32_t* tokens,
+                            int32_t* counts);
 /* CUDA-event time (ms) of the device work of the last step/generate call. */
 int fa_batch_last_ms(const fa_batch* batch, float* ms);
 

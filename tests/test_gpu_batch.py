@@ -247,3 +247,26 @@ def test_batch_capacity_and_arguments(small, oracle):
             with pytest.raises(FaError):
                 b.generate(cm.capacity)  # past the KV capacity
             assert [d.position for d in decs] == [10, 11]
+
+
+def test_batch_generate_until_end_tokens(small, oracle):
+    """The end-token stop: each session's tokens equal its own generate(end_ids)
+    and a stopped session keeps its position."""
+    from funasrnet_b200.decoder import BatchDecoder
+
+    cm, om = small
+    lengths = [6, 30, 2, 18]
+    with prefilled(cm, om, oracle, lengths, seed=110, with_oracle=False) as (probe, _, _):
+        with BatchDecoder(probe) as b:
+            seqs = b.generate(20)
+    # an end id that occurs early in session 0's sequence and one that never occurs
+    ends = [int(seqs[5, 0]), 4095 if 4095 not in seqs else 4094]
+    with prefilled(cm, om, oracle, lengths, seed=110, with_oracle=False) as (a, _, _):
+        with BatchDecoder(a) as b:
+            got = b.generate_until(20, ends)
+        with prefilled(cm, om, oracle, lengths, seed=110, with_oracle=False) as (s, _, _):
+            for i, d in enumerate(s):
+                alone = d.generate(20, end_ids=ends)
+                assert got[i] == alone, f"session {i}"
+                assert a[i].position == d.position
+    assert len(got[0]) <= 5
