@@ -170,9 +170,8 @@ constexpr uint64_t kWaitNs = 2000000000ull;   // one wait gives up after 2 s
 // raised (by a wait that timed out elsewhere) or after kWaitNs, raising the
 // flag and recording `code`.  honour_abort = false for the drains, which must
 // outlast the copies and MMAs still in flight.
-__device__ __noinline__ bool wait_phase(uint64_t* bar, unsigned parity, volatile int* abort_flag, int* err, int code,
-                                        bool honour_abort = true) {
-  if (mbar_try_wait(bar, parity)) return true;
+__device__ __noinline__ bool wait_phase_slow(uint64_t* bar, unsigned parity, volatile int* abort_flag, int* err,
+                                             int code, bool honour_abort) {
   const uint64_t t0 = globaltimer();
   for (unsigned it = 1;; ++it) {
     if (mbar_try_wait_sleep(bar, parity)) return true;
@@ -185,6 +184,12 @@ __device__ __noinline__ bool wait_phase(uint64_t* bar, unsigned parity, volatile
       }
     }
   }
+}
+// The completed-phase case inline, the bounded wait out of line.
+__device__ __forceinline__ bool wait_phase(uint64_t* bar, unsigned parity, volatile int* abort_flag, int* err, int code,
+                                           bool honour_abort = true) {
+  if (mbar_try_wait(bar, parity)) return true;
+  return wait_phase_slow(bar, parity, abort_flag, err, code, honour_abort);
 }
 
 // ------------------------------------------------------ Q8 projection ----
