@@ -117,13 +117,14 @@ __device__ __forceinline__ void tc_mma_i8(unsigned d, uint64_t adesc, uint64_t b
       "l"(adesc), "l"(bdesc), "r"(idesc)
       : "memory");
 }
-// Barrier 1 over the eight epilogue warps returning the AND of `v`.
+// Barrier 1 over the N epilogue threads returning the AND of `v`.
+template <int N>
 __device__ __forceinline__ bool epilogue_all(bool v) {
   unsigned r;
   asm volatile(
-      "{\n .reg .pred p, q;\n setp.ne.u32 p, %1, 0;\n bar.red.and.pred q, 1, 256, p;\n selp.u32 %0, 1, 0, q;\n}\n"
+      "{\n .reg .pred p, q;\n setp.ne.u32 p, %1, 0;\n bar.red.and.pred q, 1, %2, p;\n selp.u32 %0, 1, 0, q;\n}\n"
       : "=r"(r)
-      : "r"((unsigned)v)
+      : "r"((unsigned)v), "n"(N)
       : "memory");
   return r != 0;
 }
@@ -194,8 +195,6 @@ __device__ __forceinline__ bool wait_phase(uint64_t* bar, unsigned parity, volat
 
 // ------------------------------------------------------ Q8 projection ----
 
-constexpr int kEpiWarps = 8;                      // two per TMEM lane quarter, one per column half
-constexpr int kBmmThreads = 64 + 32 * kEpiWarps;  // warp 0 copies, warp 1 issues MMAs
 
 // TMEM loads / stores of n = 4, 8, 16 or 32 consecutive columns of this
 // thread's lane.
@@ -263,7 +262,11 @@ struct BmmLayout {
   static constexpr int kGroupCols = G * NS;
   static constexpr int kNGB = 512 / kGroupCols;
   static constexpr int kCols = 512;
-  static constexpr int HW = NS / 2;  // columns of one block an epilogue warp owns
+  // Epilogue warps: EW / 4 per TMEM lane quarter, each owning HW of a block's
+  // NS columns (16 warps once the tile is wide enough, for latency hiding).
+  static constexpr int EW = NS >= 16 ? 16 : 8;
+  static constexpr int kThreads = 64 + 32 * EW;  // warp 0 copies, warp 1 issues MMAs
+  static constexpr int HW = NS / (EW / 4);
   static constexpr int kBars = kScBase + kScs * kScStage;
   static constexpr int kNumBars = 2 * kOps + 2 * kScs + 2 * kNGB + 1;
   static constexpr int kMisc = kBars + 8 * kNumBars;
@@ -288,8 +291,10 @@ struct BmmMaps {
 };
 
 template <int NS, bool F16S>
-__global__ void __launch_bounds__(kBmmThreads, 1) bmm_kernel(const BmmArgs a, const __grid_constant__ BmmMaps maps) {
+__global__ void __launch_bounds__(BmmLayout<NS, F16S>::kThreads, 1)
+    bmm_kernel(const BmmArgs a, const __grid_constant__ BmmMaps maps) {
   using L = BmmLayout<NS, F16S>;
+  constexpr int kEpiWarps = L::EW;
   constexpr int G = L::G, HW = L::HW, OPS = L::kOps, SCS = L::kScs, NGB = L::kNGB;
   extern __shared__ __align__(1024) uint8_t sm[];
   uint64_t* op_full = reinterpret_cast<uint64_t*>(sm + L::kBars);
@@ -430,7 +435,7 @@ __global__ void __launch_bounds__(kBmmThreads, 1) bmm_kernel(const BmmArgs a, co
     // ---- epilogue: thread = weight row m (TMEM lane m), HW frames of each block ----
     griddep_wait();                 // residuals and outputs belong to the kernels before
     const int qd = warp & 3;        // TMEM lane quarter this warp may access
-    const int h = (warp - 2) >> 2;  // column half
+    const int h = (warp - 2) >> 2;  // column part
     const unsigned lane_addr = tmem + ((unsigned)(32 * qd) << 16) + h * HW;
     const int m = 32 * qd + lane, t = m >> 3, r = m & 7;
 #pragma unroll 1
@@ -520,7 +525,7 @@ __global__ void __launch_bounds__(kBmmThreads, 1) bmm_kernel(const BmmArgs a, co
         if (lane == 0) mbar_arrive(&sc_empty[ss]);
       }
       // One decision for the eight warps: the exchanging epilogues meet at barrier 1.
-      if (!epilogue_all(ok)) break;
+      if (!epilogue_all<32 * kEpiWarps>(ok)) break;
       const int row = rt * kBmmRows + m;
       const int f0 = ct * NS + h * HW;
       if (a.epilogue == kEpiSiluPair || a.epilogue == kEpiSiluQuant) {
@@ -1115,7 +1120,8 @@ void launch_bmm_t(const BmmArgs& a, cudaStream_t stream) {
   const int items = (a.w.rows / kBmmRows) * (a.n_pad / NS);
   const int grid = std::min(items, sm_count());
   const BmmMaps maps = make_maps(a, NS);
-  launch_pdl(bmm_kernel<NS, F16S>, grid, kBmmThreads, BmmLayout<NS, F16S>::kTotal, stream, a, maps);
+  launch_pdl(bmm_kernel<NS, F16S>, grid, BmmLayout<NS, F16S>::kThreads, BmmLayout<NS, F16S>::kTotal, stream, a,
+             maps);
 }
 
 }  // namespace
