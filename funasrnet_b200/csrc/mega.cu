@@ -8,10 +8,11 @@
 //   GEMV CTAs stream their static share of every projection: contiguous runs
 //   of 8-row weight tiles, through a 6-slot ring, phase after phase, layer
 //   after layer, then their share of the lm_head.
-//   Attention CTAs stream their KV head's history: K in chunks of 60
-//   positions through a 6-slot ring, V through a 4-slot ring; each ring takes
-//   its next chunk (of this or a later layer) as soon as a slot frees, since
-//   the history does not depend on the current token.
+//   Attention CTAs stream their KV head's history, each layer's K chunks and
+//   then its V chunks (60 positions each), through one 11-slot ring in the
+//   order they are consumed: the V chunks a layer's start cannot hold are
+//   requested while its scores run, the next layer's K while its V sum runs.
+//   The history does not depend on the current token.
 //
 // Phases of one step (QwenDecoder.Decode, QwenDecoder.cs:180-268):
 //   embed (each GEMV CTA computes the token's row itself)
@@ -61,12 +62,12 @@ constexpr int TB_F = 8 * FFN + (FFN / 32) * 16;  // 26112: K = 3072
 constexpr int WSLOTS = 7, WSLOT = TB_F;          // weight ring: 3 K=1024 tiles or 1 K=3072 tile per slot
 constexpr int CHUNK = 60;                        // KV positions per attention chunk (8 threads each)
 constexpr int CSLOT = CHUNK * D * 2;             // 15360 bytes
-constexpr int KSLOTS = 6, VSLOTS = 5;
+constexpr int ASLOTS = 11;                       // attention ring: K then V chunks of each layer
 constexpr int ATT_CTAS = H;
 constexpr unsigned kWaitLimit = 1u << 22;
 
-static_assert(KSLOTS * CSLOT + VSLOTS * CSLOT <= WSLOTS * WSLOT, "KV rings share the weight ring's memory");
-static_assert(2 * WSLOTS <= 16 && 16 + 2 * KSLOTS <= 32 && 32 + 2 * VSLOTS <= 48, "disjoint mbarrier ranges");
+static_assert(ASLOTS * CSLOT <= WSLOTS * WSLOT, "the attention ring shares the weight ring's memory");
+static_assert(2 * WSLOTS <= 16 && 16 + 2 * ASLOTS <= 48, "disjoint mbarrier ranges");
 
 enum { kTagQkv = 1, kTagAttn = 2, kTagA = 3, kTagAct = 4, kTagX = 5, kTagPart = 6 };
 enum { kErrWaitData = 1, kErrWaitFull = 2, kErrWaitEmpty = 3, kErrWaitGo = 4, kErrWaitDrain = 5 };
@@ -81,7 +82,7 @@ struct Shared {
   volatile int quit;        // consumers stop the producer
   volatile int go;          // steps the consumers have committed to
   volatile int window;      // weight-issue windows opened (one per layer, at its attention)
-  volatile int issued[3];   // copies issued per ring (weights / K / V)
+  volatile int issued[2];   // copies issued per ring (weights / attention)
   volatile int prod_exit;   // producer left its loop
   volatile int abort;       // a wait failed somewhere: drain and return
   int token;
@@ -265,18 +266,14 @@ struct Ring {
   int nslot, slot_bytes, id;
 };
 
-// The three rings over the same memory (a CTA uses either the weight ring or
-// the K and V rings).  Barriers: weights 0..13, K 16..27, V 32..41.
+// The two rings over the same memory (a CTA uses either the weight ring or
+// the attention ring).  Barriers: weights 0..13, attention 16..37.
 __device__ __forceinline__ Ring ring_w() {
   return Ring{sm<uint8_t>(kOffRing), sm<uint64_t>(kOffBars), sm<uint64_t>(kOffBars) + WSLOTS, WSLOTS, WSLOT, 0};
 }
-__device__ __forceinline__ Ring ring_k() {
-  return Ring{sm<uint8_t>(kOffRing), sm<uint64_t>(kOffBars) + 16, sm<uint64_t>(kOffBars) + 16 + KSLOTS, KSLOTS, CSLOT,
+__device__ __forceinline__ Ring ring_a() {
+  return Ring{sm<uint8_t>(kOffRing), sm<uint64_t>(kOffBars) + 16, sm<uint64_t>(kOffBars) + 16 + ASLOTS, ASLOTS, CSLOT,
               1};
-}
-__device__ __forceinline__ Ring ring_v() {
-  return Ring{sm<uint8_t>(kOffRing) + KSLOTS * CSLOT, sm<uint64_t>(kOffBars) + 32, sm<uint64_t>(kOffBars) + 32 + VSLOTS,
-              VSLOTS, CSLOT, 2};
 }
 
 // Producer side: copies `bytes` from `src` into the ring's next slot.
@@ -427,27 +424,12 @@ __device__ void producer_gemv(const MegaArgs& A, const Ring& r, Shared* sh) {
   }
 }
 
-// Producer side, non-blocking: true when the ring's next slot is free.
-__device__ __forceinline__ bool ring_free(const Ring& r, int n) {
-  if (n < r.nslot) return true;
-  return mbar_test_wait(&r.empty[n % r.nslot], (unsigned)((n / r.nslot - 1) & 1));
-}
-// Producer side: copies into the ring's next slot, which must be free.
-__device__ __forceinline__ void ring_put(const Ring& r, int& n, const void* src, unsigned bytes, Shared* sh) {
-  const int slot = n % r.nslot;
-  mbar_expect_tx(&r.full[slot], bytes);
-  bulk_load(r.base + (size_t)slot * r.slot_bytes, src, bytes, &r.full[slot]);
-  ++n;
-  sh->issued[r.id] = n;
-}
-
-// K/V history of this CTA's KV head, positions [0, pos), layer after layer,
-// in chunks of CHUNK positions.  The K and V rings advance independently:
-// whichever has a free slot gets its next chunk, so the next layer's K
-// chunks stream in while this layer's V sum still holds the V ring.
-__device__ void producer_attention(const MegaArgs& A, const Ring& kr, const Ring& vr, Shared* sh, int pos0) {
+// K/V history of this CTA's KV head, positions [0, pos), layer after layer:
+// the layer's K chunks, then its V chunks, in the consumers' order, each as
+// soon as a slot frees.
+__device__ void producer_attention(const MegaArgs& A, const Ring& ar, Shared* sh, int pos0) {
   const int g = blockIdx.x >> 1;
-  int nk = 0, nv = 0;
+  int n = 0;
   for (int step = 0; step < A.max_steps; ++step) {
     if (!wait_go(sh, A.ctrl, step)) return;
     // The rows come from generic-proxy stores of earlier steps (ordered by the
@@ -455,36 +437,14 @@ __device__ void producer_attention(const MegaArgs& A, const Ring& kr, const Ring
     __threadfence();
     asm volatile("fence.proxy.async.global;" ::: "memory");
     const int pos = pos0 + step, chunks = (pos + CHUNK - 1) / CHUNK;
-    if (chunks == 0) continue;
-    auto src = [&](const __half* cache, int l, int ch) {
-      return cache + (((size_t)l * KH + g) * A.capacity + (size_t)ch * CHUNK) * D;
-    };
-    auto bytes = [&](int ch) { return (unsigned)(min(CHUNK, pos - ch * CHUNK) * D * 2); };
-    int kl = 0, kc = 0, vl = 0, vc = 0;  // next (layer, chunk) of each ring
-    for (unsigned idle = 0; kl < A.n_layers || vl < A.n_layers;) {
-      bool moved = false;
-      if (kl < A.n_layers && ring_free(kr, nk)) {
-        ring_put(kr, nk, src(A.k_cache, kl, kc), bytes(kc), sh);
-        if (++kc == chunks) kc = 0, ++kl;
-        moved = true;
+    for (int l = 0; l < A.n_layers; ++l)
+      for (int kv = 0; kv < 2; ++kv) {
+        const __half* cache = (kv == 0 ? A.k_cache : A.v_cache) + (((size_t)l * KH + g) * A.capacity) * D;
+        for (int ch = 0; ch < chunks; ++ch)
+          if (!ring_issue(ar, n, cache + (size_t)ch * CHUNK * D, (unsigned)(min(CHUNK, pos - ch * CHUNK) * D * 2), sh,
+                          A.ctrl))
+            return;
       }
-      if (vl < A.n_layers && ring_free(vr, nv)) {
-        ring_put(vr, nv, src(A.v_cache, vl, vc), bytes(vc), sh);
-        if (++vc == chunks) vc = 0, ++vl;
-        moved = true;
-      }
-      if (moved) {
-        idle = 0;
-        continue;
-      }
-      if ((++idle & 63) == 0) {
-        if (sh->abort || sh->quit) return;
-        if (idle > kWaitLimit) {
-          raise_error(sh, A.ctrl, kErrWaitEmpty);
-          return;
-        }
-      }
-    }
   }
 }
 
@@ -493,7 +453,7 @@ __device__ void producer_attention(const MegaArgs& A, const Ring& kr, const Ring
 struct Ctx {
   const MegaArgs* A;
   unsigned long long* trace;  // this CTA's row of phase stamps during a traced step, else nullptr
-  int nw, nk, nv;             // copies consumed per ring
+  int nw, na;                 // copies consumed per ring (weights / attention)
   int tid, warp, lane;
   __device__ Shared* sh() const { return sm<Shared>(kOffShared); }
   __device__ int8_t* xq() const { return sm<int8_t>(kOffXq); }
@@ -838,9 +798,9 @@ __device__ __forceinline__ void add12(float& acc, const float (&x)[12]) {
 // (TensorMath.DecoderAttention.cs:17-52 in the order of TensorMath.AttentionAvx.cs
 // and TensorMath.SoftmaxAvx.cs), K/V history from the chunk rings.
 // co/si: this thread's RoPE entries at pos (threads 0..255).
-// Kept out of line (its registers are its own); returns the updated K and V
-// ring counts.
-__device__ __noinline__ int2 attention(Ctx c, int layer, int pos, unsigned tag_in, unsigned tag_out, float co, float si) {
+// Kept out of line (its registers are its own); returns the updated count of
+// attention-ring copies consumed (the layer's K chunks, then its V chunks).
+__device__ __noinline__ int attention(Ctx c, int layer, int pos, unsigned tag_in, unsigned tag_out, float co, float si) {
   const MegaArgs& A = *c.A;
   const int h = blockIdx.x, g = h >> 1;
   // norm weight of this thread's q (warps 0..3) or k (warps 4..7) channel,
@@ -855,7 +815,7 @@ __device__ __noinline__ int2 attention(Ctx c, int layer, int pos, unsigned tag_i
   }
   csync();
   if (c.trace && c.tid == 0) c.trace[kTraceLayerEvents * layer + 1] = global_ns();
-  if (c.sh()->abort) return make_int2(c.nk, c.nv);
+  if (c.sh()->abort) return c.na;
   if (c.warp < 4) {  // q: RMSNorm + RoPE (QwenDecoder.cs:188,193)
     head_norm(c, c.aq(), gn, A.eps, 0, 2);
     head_rope(c, c.aq(), co, si, 0, 2);
@@ -884,8 +844,8 @@ __device__ __noinline__ int2 attention(Ctx c, int layer, int pos, unsigned tag_i
   for (int i = 0; i < D / 8; ++i) qj[i] = c.aq()[j + 8 * i];
   const int chunks = (pos + CHUNK - 1) / CHUNK;
   for (int ch = 0; ch < chunks; ++ch) {
-    const uint8_t* kb = ring_acquire(ring_k(), c.nk, c.sh(), A.ctrl);
-    if (kb == nullptr) return make_int2(c.nk, c.nv);
+    const uint8_t* kb = ring_acquire(ring_a(), c.na, c.sh(), A.ctrl);
+    if (kb == nullptr) return c.na;
     const int t = ch * CHUNK + slot;
     float acc = 0.0f;
     if (t < pos) {
@@ -905,8 +865,8 @@ __device__ __noinline__ int2 attention(Ctx c, int layer, int pos, unsigned tag_i
     acc = __fadd_rn(acc, __shfl_down_sync(0xffffffffu, acc, 1));
     acc = __fadd_rn(acc, __shfl_down_sync(0xffffffffu, acc, 2));
     if (j == 0 && t < pos) c.sc()[t] = acc;  // raw dot: divided by sqrt(D) in the softmax pass
-    ring_release(ring_k(), c.nk, c.lane);
-    ++c.nk;
+    ring_release(ring_a(), c.na, c.lane);
+    ++c.na;
   }
   if (c.warp == 0) {  // position pos from the fresh k
     float acc = 0.0f;
@@ -962,8 +922,8 @@ __device__ __noinline__ int2 attention(Ctx c, int layer, int pos, unsigned tag_i
   if (c.warp < 4) {
     float acc = 0.0f;
     for (int ch = 0; ch < chunks; ++ch) {
-      const uint8_t* vb = ring_acquire(ring_v(), c.nv, c.sh(), A.ctrl);
-      if (vb == nullptr) return make_int2(c.nk, c.nv);
+      const uint8_t* vb = ring_acquire(ring_a(), c.na + ch, c.sh(), A.ctrl);
+      if (vb == nullptr) return c.na + ch;
       const __half* vv = reinterpret_cast<const __half*>(vb) + c.tid;
       const float* pr = c.sc() + ch * CHUNK;
       const int n = min(CHUNK, pos - ch * CHUNK);
@@ -984,15 +944,16 @@ __device__ __noinline__ int2 attention(Ctx c, int layer, int pos, unsigned tag_i
       } else {
         for (int t = 0; t < n; ++t) acc = __fadd_rn(acc, __fmul_rn(__half2float(vv[t * D]), pr[t]));
       }
-      ring_release(ring_v(), c.nv, c.lane);
-      ++c.nv;
+      // The four V warps' arrivals make up the slot's CWARPS.
+      __syncwarp();
+      if (c.lane == 0) mbar_arrive_count(&ring_a().empty[(c.na + ch) % ASLOTS], c.warp == 0 ? CWARPS - 3 : 1);
     }
     acc = __fadd_rn(acc, __fmul_rn(c.av()[c.tid], c.sc()[pos]));
     // The O projection's input quantisation of this head's four blocks
     // (block 4h + warp), done once here instead of in every GEMV CTA.
     publish_block(A.attn_t, QW, h * 4 + c.warp, acc, tag_out, c.lane);
   }
-  return make_int2(c.nk, c.nv);
+  return c.na + chunks;
 }
 
 // Records a phase timestamp of the first step (thread 0 only; a no-op unless tracing).
@@ -1004,7 +965,7 @@ __device__ __noinline__ int2 attention(Ctx c, int layer, int pos, unsigned tag_i
 
 __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(const MegaArgs A) {
   Shared* sh = sm<Shared>(kOffShared);
-  const Ring wr = ring_w(), kr = ring_k(), vr = ring_v();
+  const Ring wr = ring_w(), ar = ring_a();
   const bool att = blockIdx.x < ATT_CTAS;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   if (tid == 0) {
@@ -1012,17 +973,13 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(const Mega
       mbar_init(&wr.full[i], 1);
       mbar_init(&wr.empty[i], CWARPS);
     }
-    for (int i = 0; i < KSLOTS; ++i) {
-      mbar_init(&kr.full[i], 1);
-      mbar_init(&kr.empty[i], CWARPS);
-    }
-    for (int i = 0; i < VSLOTS; ++i) {
-      mbar_init(&vr.full[i], 1);
-      mbar_init(&vr.empty[i], 4);  // the V sum runs on warps 0..3
+    for (int i = 0; i < ASLOTS; ++i) {
+      mbar_init(&ar.full[i], 1);
+      mbar_init(&ar.empty[i], CWARPS);
     }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     sh->quit = sh->go = sh->window = sh->prod_exit = sh->abort = 0;
-    sh->issued[0] = sh->issued[1] = sh->issued[2] = 0;
+    sh->issued[0] = sh->issued[1] = 0;
   }
   __syncthreads();
   MegaCtrl* ctrl = A.ctrl;
@@ -1031,7 +988,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(const Mega
   const unsigned tps = (unsigned)((A.n_layers + 1) * 8);
   if (warp == CWARPS) {  // producer warp: one elected lane issues every copy
     if (lane == 0) {
-      if (att) producer_attention(A, kr, vr, sh, pos0);
+      if (att) producer_attention(A, ar, sh, pos0);
       else producer_gemv(A, wr, sh);
       sh->prod_exit = 1;
     }
@@ -1042,7 +999,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(const Mega
   csync();
   Ctx c;
   c.A = &sh->args;
-  c.nw = c.nk = c.nv = 0;
+  c.nw = c.na = 0;
   c.trace = nullptr;
   c.tid = tid;
   c.warp = warp;
@@ -1110,9 +1067,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(const Mega
       const int ev = kTraceLayerEvents * layer;
       if (att) {
         MEGA_TRACE(ev + 0);
-        const int2 n = attention(c, layer, pos, tl + kTagQkv, tl + kTagAttn, rope_co, rope_si);
-        c.nk = n.x;
-        c.nv = n.y;
+        c.na = attention(c, layer, pos, tl + kTagQkv, tl + kTagAttn, rope_co, rope_si);
         csync();
         MEGA_TRACE(ev + 5);
         if (sh->abort) goto drain;
@@ -1357,8 +1312,7 @@ drain:
       }
     }
     ring_drain(wr, c.nw, sh->issued[0], sh, ctrl);
-    ring_drain(kr, c.nk, sh->issued[1], sh, ctrl);
-    ring_drain(vr, c.nv, sh->issued[2], sh, ctrl);
+    ring_drain(ar, c.na, sh->issued[1], sh, ctrl);
   }
   csync();
   if (blockIdx.x == 0 && tid == 0) {
