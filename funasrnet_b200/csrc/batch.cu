@@ -684,12 +684,16 @@ __global__ void __launch_bounds__(256) act_quant_kernel(const ActQuantArgs a) {
 __host__ __device__ __forceinline__ int kpos(int c, int D) { return (c & 7) * (D >> 3) + (c >> 3); }
 
 constexpr int kAttnCh = 32;        // positions per ring chunk (8 KB of K or V rows)
-constexpr int kAttnSlots = 6;      // ring chunks in flight (four CTAs per SM)
 constexpr int kAttnThreads = 288;  // 8 compute warps + 1 copy warp
-constexpr int kAttnRing = kAttnSlots * kAttnCh * 256;
+constexpr int kAttnMaxSlots = 8;
 
-__host__ __device__ constexpr size_t attn_smem_bytes(int capacity) {
-  return (size_t)kAttnRing + 16 * kAttnSlots + (size_t)2 * capacity * 4;
+// Ring chunks in flight per CTA.  A CTA's history streams at about one ring
+// per memory latency, so small batches (few CTAs, the longest session's CTA
+// setting the time) take a deeper ring; large ones keep four CTAs per SM.
+inline int attn_slots(int frames) { return frames <= 96 ? 8 : 6; }
+
+__host__ __device__ constexpr size_t attn_smem_bytes(int capacity, int slots) {
+  return (size_t)slots * kAttnCh * 256 + 16 * slots + (size_t)2 * capacity * 4;
 }
 
 __device__ __forceinline__ void csync256() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
@@ -703,11 +707,12 @@ __device__ __forceinline__ void csync256() { asm volatile("bar.sync 1, 256;" :::
 // (TensorMath.AttentionAvx.cs:87-159), softmax with the double lane sum
 // (TensorMath.SoftmaxAvx.cs:11-58) and the V sum per channel in position
 // order (TensorMath.AttentionAvx.cs:173-224).
+template <int RS>
 __global__ void __launch_bounds__(kAttnThreads) batch_attn_kernel(const BatchAttnArgs a) {
-  constexpr int D = 128, M = D / 8, HALF = D / 2, CH = kAttnCh, RS = kAttnSlots;
+  constexpr int D = 128, M = D / 8, HALF = D / 2, CH = kAttnCh;
   extern __shared__ __align__(128) uint8_t smraw[];
   uint8_t* ring = smraw;
-  uint64_t* full = reinterpret_cast<uint64_t*>(smraw + kAttnRing);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smraw + (size_t)RS * CH * 256);
   uint64_t* empty = full + RS;
   float* sc = reinterpret_cast<float*>(empty + RS);  // [capacity][2]: both heads' scores, then probabilities
   __shared__ float y[2][D];
@@ -1026,7 +1031,7 @@ __global__ void __launch_bounds__(256) batch_finish_kernel(const BatchStep s) {
 }
 
 
-constexpr int kAttnMaxSmem = 200 * 1024;  // ring + scores of two heads: capacity <= 19400
+constexpr int kAttnMaxSmem = 200 * 1024;  // deepest ring + scores of two heads: capacity <= 17392
 
 template <int NS, bool F16S>
 void set_bmm_attr() {
@@ -1137,7 +1142,8 @@ void prepare_batch_kernels() {
     set_bmm_attr<16, false>();
     set_bmm_attr<32, false>();
     set_bmm_attr<64, false>();
-    cudaFuncSetAttribute(batch_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kAttnMaxSmem);
+    cudaFuncSetAttribute(batch_attn_kernel<6>, cudaFuncAttributeMaxDynamicSharedMemorySize, kAttnMaxSmem);
+    cudaFuncSetAttribute(batch_attn_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, kAttnMaxSmem);
   });
 }
 
@@ -1187,14 +1193,18 @@ void launch_act_quant(const ActQuantArgs& a, cudaStream_t stream) {
   FA_CUDA(cudaGetLastError());
 }
 
-bool batch_attention_fits(int capacity) { return attn_smem_bytes(capacity) <= (size_t)kAttnMaxSmem; }
+bool batch_attention_fits(int capacity) {
+  return attn_smem_bytes(capacity, kAttnMaxSlots) <= (size_t)kAttnMaxSmem;
+}
 
 void launch_batch_attention(const BatchAttnArgs& a, cudaStream_t stream) {
-  const size_t smem = attn_smem_bytes(a.capacity);
+  const int slots = attn_slots(a.frames);
+  const size_t smem = attn_smem_bytes(a.capacity, slots);
   if (smem > (size_t)kAttnMaxSmem) throw Error(kErrCapacity, "batched attention: capacity too large");
   if (a.heads != 2 * a.kv_heads) throw Error(kErrArgument, "batched attention: paired GQA only");
   prepare_batch_kernels();
-  launch_pdl(batch_attn_kernel, a.frames * a.kv_heads, kAttnThreads, smem, stream, a);
+  if (slots == 8) launch_pdl(batch_attn_kernel<8>, a.frames * a.kv_heads, kAttnThreads, smem, stream, a);
+  else launch_pdl(batch_attn_kernel<6>, a.frames * a.kv_heads, kAttnThreads, smem, stream, a);
   FA_CUDA(cudaGetLastError());
 }
 
