@@ -67,6 +67,7 @@ SIGNATURES = {
     "fa_session_last_generate_ms": (i32, [vp, P(f32)]),
     "fa_session_cache_prefix": (i32, [vp, vp, i32]),
     "fa_session_restore_prefix": (i32, [vp]),
+    "fa_session_share_prefix": (i32, [vp, vp]),
     "fa_session_kv": (i32, [vp, i32, vp, vp]),
     "fa_session_kernels_per_step": (i32, [vp]),
     "fa_session_uses_persistent_kernel": (i32, [vp]),

@@ -138,7 +138,7 @@ struct fa_session {
   int pos = 0;             // host mirror of the device KV length
   int cached_prefix = 0;
   bool have_token = false; // a device argmax exists (a Decode with logits ran)
-  DevBuf k_cache, v_cache;  // [layers][capacity][kv_width] f16
+  DevBuf k_cache, v_cache;  // [layers][kv_heads][capacity][head] f16 (K rows lane-permuted)
   DevBuf x, a, qkv, attn, act, gu, part, logits, am_val, am_idx, ints, end_ids, log;
   // ints: 0 pos, 1 token, 2 step, 3 stopped, 4 row0_nan, 5 counter, 6 scratch token
   int log_cap = 0;
@@ -1602,6 +1602,34 @@ int fa_session_cache_prefix(fa_session* s, const int32_t* tokens, int n) {
     session_decode_locked(s, nullptr, tokens, n, 0, nullptr, nullptr);
     s->cached_prefix = n;
     s->have_token = false;
+    return (int)kHandled;
+  });
+}
+
+int fa_session_share_prefix(fa_session* dst, fa_session* src) {
+  return guarded([&] {
+    if (!dst || !src || dst == src) throw Error(kErrArgument, "share_prefix: two distinct sessions");
+    std::scoped_lock lk(dst->mu, src->mu);
+    if (dst->m != src->m) throw Error(kErrArgument, "share_prefix: sessions of different models");
+    if (src->cached_prefix == 0) throw Error(kErrArgument, "share_prefix: the source has no cached prefix");
+    if (dst->cached_prefix != 0) throw Error(kErrArgument, "Prefix is already cached");
+    DeviceGuard g(dst->device);
+    fa_model* m = dst->m;
+    const int n = src->cached_prefix, kvh = m->kv_heads, D = m->head_size;
+    // rows [0, n) of every (layer, KV head) block: one strided copy per cache
+    FA_CUDA(cudaStreamSynchronize(src->stream));
+    const size_t pitch = (size_t)m->capacity * D * sizeof(__half), width = (size_t)n * D * sizeof(__half);
+    FA_CUDA(cudaMemcpy2DAsync(dst->k_cache.p, pitch, src->k_cache.p, pitch, width, (size_t)m->layers * kvh,
+                              cudaMemcpyDeviceToDevice, dst->stream));
+    FA_CUDA(cudaMemcpy2DAsync(dst->v_cache.p, pitch, src->v_cache.p, pitch, width, (size_t)m->layers * kvh,
+                              cudaMemcpyDeviceToDevice, dst->stream));
+    // the state CachePrefix leaves: position n, no argmax to continue from
+    dst->pinned[0] = n;
+    FA_CUDA(cudaMemcpyAsync(dst->d_int(0), dst->pinned, 4, cudaMemcpyHostToDevice, dst->stream));
+    FA_CUDA(cudaStreamSynchronize(dst->stream));
+    dst->pos = n;
+    dst->cached_prefix = n;
+    dst->have_token = false;
     return (int)kHandled;
   });
 }

@@ -158,6 +158,10 @@ class QwenDecoder:
     def restore_prefix(self) -> None:
         check(lib().fa_session_restore_prefix(self._h))
 
+    def share_prefix(self, source: "QwenDecoder") -> None:
+        """CachePrefix from `source`'s cached prefix without decoding it again (device-to-device KV copy)."""
+        check(lib().fa_session_share_prefix(self._h, source._h))
+
     def kv(self, layer: int):
         n = self.position * self.model.kv_heads * self.model.head_size
         k = np.empty(n, np.float32)

@@ -163,6 +163,15 @@ int fa_session_last_generate_ms(const fa_session* session, float* ms);
 /* CachePrefix / RestorePrefix (QwenDecoder.cs:122-137). */
 int fa_session_cache_prefix(fa_session* session, const int32_t* tokens, int n);
 int fa_session_restore_prefix(fa_session* session);
+/* CachePrefix on `dst` from the prefix `src` cached, without decoding it again:
+ * the prefix's KV rows of every layer are copied device to device and dst is
+ * left as CachePrefix leaves a decoder (position = prefix length, prefix
+ * cached).  Sessions of one model serving the same prompt (the FunAsr
+ * CachePrompt prefix, FunAsr.cs:134-138) prefill it once.  ArgumentException
+ * semantics (FA_ERR_ARGUMENT): dst == src, different models, no prefix cached
+ * in src, or one already cached in dst ("Prefix is already cached",
+ * QwenDecoder.cs:124-127). */
+int fa_session_share_prefix(fa_session* dst, fa_session* src);
 /* Test hook: the F16-valued KV history of one layer as floats, [position x kv_width]. */
 int fa_session_kv(fa_session* session, int layer, float* keys, float* values);
 /* Debug hook (the reference's Trace("qwen_layer0", ...) snapshot, QwenDecoder.cs:35,248-251,

@@ -229,6 +229,51 @@ def test_prefix_cache_restore(small):
     b.close()
 
 
+def test_shared_prefix_across_sessions(small, oracle):
+    """share_prefix: a second session takes the first one's cached prompt (KV rows
+    copied on the device) and decodes exactly as if it had cached it itself; the
+    oracle decoding prompt + audio in one call pins both."""
+    from funasrnet_b200._lib import FaError
+    from funasrnet_b200.decoder import BatchDecoder, QwenDecoder
+
+    cm, om = small
+    prompt = [7, 3001, 42, 4095, 19, 256]
+    a, b, c = QwenDecoder(cm), QwenDecoder(cm), QwenDecoder(cm)
+    with pytest.raises(FaError):
+        b.share_prefix(a)  # nothing cached in the source yet
+    a.cache_prefix(prompt)
+    b.share_prefix(a)
+    assert b.position == len(prompt)
+    with pytest.raises(FaError):
+        b.share_prefix(a)  # "Prefix is already cached"
+    with pytest.raises(FaError):
+        a.share_prefix(a)
+    for layer in range(2):
+        ka, va = a.kv(layer)
+        kb, vb = b.kv(layer)
+        assert_bits_equal(kb, ka, f"layer-{layer} prefix keys")
+        assert_bits_equal(vb, va, f"layer-{layer} prefix values")
+    firsts = []
+    for i, d in enumerate((a, b)):  # two utterances after the shared prompt
+        rest, n = prefix_embeddings(om, 5 + 7 * i, 3, seed=20 + i)
+        d.restore_prefix()
+        lg, arg = d.decode(rest, n)
+        o = oracle.Session(om)
+        exp = o.decode(np.concatenate([om.embed(prompt), rest]), len(prompt) + n)
+        check_logits(lg, exp, f"session {i} after the shared prefix")
+        assert arg == oracle.greedy(exp)
+        firsts.append(arg)
+        o.close()
+    # both continue in one batch
+    with BatchDecoder([a, b]) as bd:
+        got = bd.generate(6)
+    assert got[0].tolist() == firsts
+    c.share_prefix(b)  # a session that received a prefix can pass it on
+    assert c.position == len(prompt)
+    for d in (a, b, c):
+        d.close()
+
+
 def test_fp32_weights_model(backend, oracle, small_gguf_f32):
     from funasrnet_b200.decoder import CudaModel, QwenDecoder
 
