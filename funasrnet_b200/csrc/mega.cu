@@ -6,7 +6,7 @@
 // streams data into shared-memory rings with cp.async.bulk + mbarriers and
 // runs ahead of the compute; warps 0..14 compute.
 //   GEMV CTAs stream their static share of every projection: contiguous runs
-//   of 8-row weight tiles, through a 6-slot ring, phase after phase, layer
+//   of 8-row weight tiles, through a 7-slot ring, phase after phase, layer
 //   after layer, then their share of the lm_head.
 //   Attention CTAs stream their KV head's history, each layer's K chunks and
 //   then its V chunks (60 positions each), through one 11-slot ring in the
