@@ -486,15 +486,23 @@ __global__ void __launch_bounds__(BmmLayout<NS, F16S>::kThreads, 1)
             for (int u = 0; u < G; ++u) {
               const int kb = g8 * G + u;
               const float nc = __fmul_rn(wsv[u], -kMagic);  // exact: ws has 11 significant bits
+              const uint64_t ws2 = pack_f2(wsv[u], wsv[u]), nc2 = pack_f2(nc, nc);
               const float4* xs4 = reinterpret_cast<const float4*>(st + L::kSB + (kb * NS + h * HW) * 4);
 #pragma unroll
               for (int j4 = 0; j4 < HW / 4; ++j4) {
                 const float4 x = xs4[j4];
-                const float xv[4] = {x.x, x.y, x.z, x.w};
 #pragma unroll
-                for (int e = 0; e < 4; ++e) {
+                for (int e = 0; e < 4; e += 2) {
+                  // two columns per instruction: RN(dot ws) by the magic FMA, then RN(. xs);
+                  // the running sums stay scalar adds (block order per column)
                   const int j = 4 * j4 + e;
-                  acc[j] = __fadd_rn(acc[j], __fmul_rn(__fmaf_rn(__uint_as_float(v[u * HW + j]), wsv[u], nc), xv[e]));
+                  const uint64_t t2 = fma_f2(pack_f2(__uint_as_float(v[u * HW + j]), __uint_as_float(v[u * HW + j + 1])),
+                                             ws2, nc2);
+                  const uint64_t p2 = mul_f2(t2, e == 0 ? pack_f2(x.x, x.y) : pack_f2(x.z, x.w));
+                  float p0, p1;
+                  unpack_f2(p2, p0, p1);
+                  acc[j] = __fadd_rn(acc[j], p0);
+                  acc[j + 1] = __fadd_rn(acc[j + 1], p1);
                 }
               }
             }

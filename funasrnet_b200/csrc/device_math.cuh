@@ -111,5 +111,29 @@ __device__ __forceinline__ bool better(float v2, int i2, float v1, int i1) {
   return v2 > v1 || (v2 == v1 && i2 < i1);
 }
 
+// Packed pairs of f32 (fma/mul.rn.f32x2, sm_100): two independent IEEE
+// round-to-nearest operations per instruction.  A packed multiply feeding a
+// packed add was measured to be contracted into a fused multiply-add by the
+// code generator, so packed products feed scalar adds only (the bit-exact
+// projection tests pin this).
+__device__ __forceinline__ uint64_t pack_f2(float a, float b) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+  return r;
+}
+__device__ __forceinline__ void unpack_f2(uint64_t v, float& a, float& b) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(v));
+}
+__device__ __forceinline__ uint64_t fma_f2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+  return r;
+}
+__device__ __forceinline__ uint64_t mul_f2(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+
 }  // namespace dev
 }  // namespace fa
