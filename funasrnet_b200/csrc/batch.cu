@@ -838,12 +838,9 @@ __global__ void __launch_bounds__(kAttnThreads) batch_attn_kernel(const BatchAtt
   // scores of both query heads: 8 threads per position, one chunk per pass
   {
     const int j = tid & 7, slot8 = tid >> 3;
-    float q0[M], q1[M];
+    uint64_t q01[M];  // (head 2g, head 2g + 1) of channel j + 8 k
 #pragma unroll
-    for (int k = 0; k < M; ++k) {
-      q0[k] = qs[0][j + 8 * k];
-      q1[k] = qs[1][j + 8 * k];
-    }
+    for (int k = 0; k < M; ++k) q01[k] = pack_f2(qs[0][j + 8 * k], qs[1][j + 8 * k]);
     for (int ch = 0; ch < nch; ++ch) {
       const int slot = ch % RS;
       wait_phase(&full[slot], (ch / RS) & 1, &abort_flag, a.err, kBatchWaitLoad);
@@ -857,8 +854,10 @@ __global__ void __launch_bounds__(kAttnThreads) batch_attn_kernel(const BatchAtt
 #pragma unroll
         for (int k = 0; k < M; ++k) {
           const float kv = __half2float(k < 8 ? kh0[k] : kh1[k - 8]);
-          acc0 = __fadd_rn(acc0, __fmul_rn(q0[k], kv));
-          acc1 = __fadd_rn(acc1, __fmul_rn(q1[k], kv));
+          float p0, p1;  // both heads' products in one packed multiply, sums scalar
+          unpack_f2(mul_f2(q01[k], pack_f2(kv, kv)), p0, p1);
+          acc0 = __fadd_rn(acc0, p0);
+          acc1 = __fadd_rn(acc1, p1);
         }
       }
       __syncwarp();
@@ -926,10 +925,14 @@ __global__ void __launch_bounds__(kAttnThreads) batch_attn_kernel(const BatchAtt
       for (int u = 0; u < n; ++u) {
         const float2 v = __half22float2(vr[u * (D / 2)]);
         const float2 pp = p2[t0 + u];
-        s00 = __fadd_rn(s00, __fmul_rn(v.x, pp.x));
-        s01 = __fadd_rn(s01, __fmul_rn(v.y, pp.x));
-        s10 = __fadd_rn(s10, __fmul_rn(v.x, pp.y));
-        s11 = __fadd_rn(s11, __fmul_rn(v.y, pp.y));
+        const uint64_t v2 = pack_f2(v.x, v.y);
+        float a, b, c2, d;  // (channel pair) x probability of each head, sums scalar
+        unpack_f2(mul_f2(v2, pack_f2(pp.x, pp.x)), a, b);
+        unpack_f2(mul_f2(v2, pack_f2(pp.y, pp.y)), c2, d);
+        s00 = __fadd_rn(s00, a);
+        s01 = __fadd_rn(s01, b);
+        s10 = __fadd_rn(s10, c2);
+        s11 = __fadd_rn(s11, d);
       }
     }
     __syncwarp();
