@@ -1316,6 +1316,8 @@ drain:
   }
   csync();
   if (blockIdx.x == 0 && tid == 0) {
+    if (A.out_pos) *A.out_pos = pos0 + steps;  // the step-graph path's words, kept in step
+    if (A.out_token) *A.out_token = token;
     ctrl->token = token;
     ctrl->pos = pos0 + steps;
     ctrl->steps = steps;

@@ -55,6 +55,8 @@ struct MegaArgs {
   unsigned long long* part_i = nullptr;  // [grid] argmax partial indices
   float* logits = nullptr;               // optional: written when non-null
   MegaCtrl* ctrl = nullptr;
+  int* out_pos = nullptr;                // optional: the position after the launch, also written here
+  int* out_token = nullptr;              // optional: the last argmax, also written here
   int max_steps = 1;
   int record = 0;                        // 1: the FunAsr.Transcribe loop (end test + log)
   const int* end_ids = nullptr;

@@ -158,6 +158,7 @@ struct fa_session {
   bool use_mega = false;
   int mega_grid = 0;
   DevBuf mx, mqkv, mattn, ma, mact, mpv, mpi, mctrl;
+  unsigned mega_epoch = 1;  // the control block's tag base, as the last launch left it
   bool trace = false;
   DevBuf trace_buf;                          // [grid x kTraceEvents] phase timestamps
   DevBuf bxq, bxs, bxq2, bxs2;               // frame-tile operands of tensor-core prefill projections
@@ -1483,26 +1484,30 @@ static MegaCtrl run_mega(fa_session* s, int steps, int record, int n_end, int ho
     FA_CUDA(cudaMemsetAsync(s->trace_buf.p, 0, bytes, s->stream));
     a.trace = s->trace_buf.as<unsigned long long>();
   }
-  // control block: pos, token (host or last device argmax), counters cleared
-  s->pinned[8] = s->pos;
-  s->pinned[9] = host_token;
-  s->pinned[10] = 0;
-  s->pinned[11] = 0;
+  // the whole control block in one copy: pos, token (host or last device
+  // argmax), counters and error cleared, the tag base the last launch left
+  MegaCtrl in{};
+  in.pos = s->pos;
+  in.token = host_token;
+  in.epoch = s->mega_epoch;
+  static_assert(sizeof(MegaCtrl) <= 32, "control block staging");
+  std::memcpy(s->pinned + 8, &in, sizeof(in));
   char* ctrl = static_cast<char*>(s->mctrl.p);
-  FA_CUDA(cudaMemcpyAsync(ctrl, s->pinned + 8, 16, cudaMemcpyHostToDevice, s->stream));
+  FA_CUDA(cudaMemcpyAsync(ctrl, s->pinned + 8, sizeof(MegaCtrl), cudaMemcpyHostToDevice, s->stream));
   if (host_token < 0) FA_CUDA(cudaMemcpyAsync(ctrl + 4, s->d_int(1), 4, cudaMemcpyDeviceToDevice, s->stream));
-  FA_CUDA(cudaMemsetAsync(ctrl + offsetof(MegaCtrl, error), 0, 8, s->stream));
-  FA_CUDA(cudaEventRecord(s->ev0, s->stream));
+  // the graph path's position and token words follow the launch (written by the kernel)
+  a.out_pos = s->d_int(0);
+  a.out_token = s->d_int(1);
+  const bool timed = record != 0;  // generate reports its device time; a single step does not
+  if (timed) FA_CUDA(cudaEventRecord(s->ev0, s->stream));
   launch_mega(a, s->mega_grid, s->stream);
-  FA_CUDA(cudaEventRecord(s->ev1, s->stream));
-  // keep the graph path's device words in step: pos, token
-  FA_CUDA(cudaMemcpyAsync(s->d_int(0), ctrl + offsetof(MegaCtrl, pos), 4, cudaMemcpyDeviceToDevice, s->stream));
-  FA_CUDA(cudaMemcpyAsync(s->d_int(1), ctrl + offsetof(MegaCtrl, token), 4, cudaMemcpyDeviceToDevice, s->stream));
+  if (timed) FA_CUDA(cudaEventRecord(s->ev1, s->stream));
   FA_CUDA(cudaMemcpyAsync(s->pinned + 16, ctrl, sizeof(MegaCtrl), cudaMemcpyDeviceToHost, s->stream));
   FA_CUDA(cudaStreamSynchronize(s->stream));
-  FA_CUDA(cudaEventElapsedTime(&s->last_ms, s->ev0, s->ev1));
+  if (timed) FA_CUDA(cudaEventElapsedTime(&s->last_ms, s->ev0, s->ev1));
   MegaCtrl c;
   std::memcpy(&c, s->pinned + 16, sizeof(c));
+  s->mega_epoch = c.epoch;
   if (c.error != 0)
     throw Error(kErrTimeout, "persistent decode kernel: a bounded wait gave up (code " + std::to_string(c.error) + ")");
   s->pos = c.pos;
