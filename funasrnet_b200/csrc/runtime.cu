@@ -1792,7 +1792,11 @@ struct fa_batch {
   int log_cap = 0;
   cudaGraphExec_t graph = nullptr;
   bool graph_logits = false;
-  int* pinned = nullptr;  // [8 + n]: error words at 0..3, token staging at 8
+  int* pinned = nullptr;  // [8 + max(n, 64)]: end-token count at 7, token / end-id staging at 8; then words()
+  int dev_n_end = -1;     // end-token count the device holds
+  // Per part k, its words after a run: positions [n_k], tokens [n_k], step
+  // counter, error word (read back in one copy per part).
+  int* words(int k, const BatchPart* p) { return pinned + 8 + std::max(n, 64) + 2 * p->f0 + 2 * k; }
   cudaEvent_t ev0 = nullptr, ev1 = nullptr;
   float last_ms = 0.0f;
 };
@@ -1960,11 +1964,15 @@ void update_order(fa_batch* b) {
 
 // Launches the step graph `steps` times and checks the batched kernels' error
 // words; n_end end tokens (ids staged in b->pinned + 8) stop a session.
-void run_batch(fa_batch* b, int steps, bool want_logits, int n_end = 0) {
+void run_batch(fa_batch* b, int steps, bool want_logits, int n_end = 0, bool timed = true) {
   update_order(b);
-  b->pinned[7] = n_end;
-  FA_CUDA(cudaMemcpyAsync(b->ends.p, b->pinned + 7, (size_t)(1 + n_end) * 4, cudaMemcpyHostToDevice, b->stream));
-  for (auto& p : b->parts) FA_CUDA(cudaMemsetAsync(p->d_stopped(), 0, (size_t)p->n * 4, b->stream));
+  if (n_end > 0 || b->dev_n_end != n_end) {
+    b->pinned[7] = n_end;
+    FA_CUDA(cudaMemcpyAsync(b->ends.p, b->pinned + 7, (size_t)(1 + n_end) * 4, cudaMemcpyHostToDevice, b->stream));
+    b->dev_n_end = n_end;
+  }
+  // step counter, error word and stop flags are contiguous: one clear per part
+  for (auto& p : b->parts) FA_CUDA(cudaMemsetAsync(p->d_counter(), 0, (size_t)(p->n + 2) * 4, b->stream));
   if (b->graph && b->graph_logits != want_logits) {
     cudaGraphExecDestroy(b->graph);
     b->graph = nullptr;
@@ -1973,27 +1981,30 @@ void run_batch(fa_batch* b, int steps, bool want_logits, int n_end = 0) {
     b->graph = capture_batch(b, want_logits);
     b->graph_logits = want_logits;
   }
-  for (auto& p : b->parts) FA_CUDA(cudaMemsetAsync(p->d_counter(), 0, 4, b->stream));
-  FA_CUDA(cudaEventRecord(b->ev0, b->stream));
+  if (timed) FA_CUDA(cudaEventRecord(b->ev0, b->stream));
   for (int i = 0; i < steps; ++i) FA_CUDA(cudaGraphLaunch(b->graph, b->stream));
-  FA_CUDA(cudaEventRecord(b->ev1, b->stream));
-  for (size_t i = 0; i < b->parts.size(); ++i)
-    FA_CUDA(cudaMemcpyAsync(b->pinned + i, b->parts[i]->d_err(), 4, cudaMemcpyDeviceToHost, b->stream));
+  if (timed) FA_CUDA(cudaEventRecord(b->ev1, b->stream));
+  // positions, tokens and the error word of each part in one copy
+  for (size_t k = 0; k < b->parts.size(); ++k) {
+    BatchPart* p = b->parts[k].get();
+    FA_CUDA(cudaMemcpyAsync(b->words((int)k, p), p->d_pos(), (size_t)(2 * p->n + 2) * 4, cudaMemcpyDeviceToHost,
+                            b->stream));
+  }
   FA_CUDA(cudaStreamSynchronize(b->stream));
-  FA_CUDA(cudaEventElapsedTime(&b->last_ms, b->ev0, b->ev1));
-  for (size_t i = 0; i < b->parts.size(); ++i)
-    if (b->pinned[i] != 0) {
-      const int code = b->pinned[i];
-      for (auto& p : b->parts) FA_CUDA(cudaMemset(p->d_err(), 0, 4));
-      throw Error(kErrTimeout, "batched decode: a bounded wait gave up (code " + std::to_string(code) + ")");
-    }
+  if (timed) FA_CUDA(cudaEventElapsedTime(&b->last_ms, b->ev0, b->ev1));
+  for (size_t k = 0; k < b->parts.size(); ++k) {
+    const BatchPart* p = b->parts[k].get();
+    const int code = b->words((int)k, p)[2 * p->n + 1];
+    if (code != 0) throw Error(kErrTimeout, "batched decode: a bounded wait gave up (code " + std::to_string(code) + ")");
+  }
   // positions after the run (a stopped session stops advancing)
-  std::vector<int> pos(b->n);
-  for (auto& p : b->parts)
-    FA_CUDA(cudaMemcpy(pos.data() + p->f0, p->d_pos(), (size_t)p->n * 4, cudaMemcpyDeviceToHost));
-  for (int i = 0; i < b->n; ++i) {
-    b->sessions[i]->pos = pos[i];
-    b->sessions[i]->have_token = true;
+  for (size_t k = 0; k < b->parts.size(); ++k) {
+    const BatchPart* p = b->parts[k].get();
+    const int* w = b->words((int)k, p);
+    for (int i = 0; i < p->n; ++i) {
+      b->sessions[p->f0 + i]->pos = w[i];
+      b->sessions[p->f0 + i]->have_token = true;
+    }
   }
 }
 
@@ -2075,9 +2086,10 @@ int fa_batch_create(fa_session* const* sessions, int n, fa_batch** out) {
     b->log.ensure((size_t)b->log_cap * n * 4);
     b->ends.ensure(65 * 4);
     FA_CUDA(cudaMemset(b->ends.p, 0, b->ends.bytes));
+    b->dev_n_end = 0;
     FA_CUDA(cudaEventCreate(&b->ev0));
     FA_CUDA(cudaEventCreate(&b->ev1));
-    FA_CUDA(cudaMallocHost(&b->pinned, (size_t)(std::max(n, 64) + 8) * 4));
+    FA_CUDA(cudaMallocHost(&b->pinned, (size_t)(std::max(n, 64) + 8 + 2 * n + 2 * (int)b->parts.size()) * 4));
     prepare_kernels();
     prepare_batch_kernels();
     *out = b.release();
@@ -2124,14 +2136,12 @@ int fa_batch_step(fa_batch* b, const int32_t* tokens, int32_t* next, float* logi
       for (auto& p : b->parts) launch_batch_scatter(batch_state(b, p.get()), b->feed.as<int>() + p->f0, b->stream);
     }
     if (logits) b->logits.ensure((size_t)b->n * m->vocab * 4);  // before the logits graph is captured
-    run_batch(b, 1, logits != nullptr);
-    if (next) {
-      for (auto& p : b->parts)
-        FA_CUDA(cudaMemcpyAsync(b->pinned + 8 + p->f0, p->d_tok(), (size_t)p->n * 4, cudaMemcpyDeviceToHost,
-                                b->stream));
-      FA_CUDA(cudaStreamSynchronize(b->stream));
-      std::memcpy(next, b->pinned + 8, (size_t)b->n * 4);
-    }
+    run_batch(b, 1, logits != nullptr, 0, false);
+    if (next)
+      for (size_t k = 0; k < b->parts.size(); ++k) {
+        const BatchPart* p = b->parts[k].get();
+        std::memcpy(next + p->f0, b->words((int)k, p) + p->n, (size_t)p->n * 4);
+      }
     if (logits) FA_CUDA(cudaMemcpy(logits, b->logits.p, (size_t)b->n * m->vocab * 4, cudaMemcpyDeviceToHost));
     return (int)kHandled;
   });

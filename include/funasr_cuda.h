@@ -248,7 +248,8 @@ int fa_batch_generate(fa_batch* batch, int steps, int32_t* tokens);
  * session i emitted.  Stopped sessions keep their position and token. */
 int fa_batch_generate_until(fa_batch* batch, int max_steps, const int32_t* end_ids, int n_end, int32_t* tokens,
                             int32_t* counts);
-/* CUDA-event time (ms) of the device work of the last step/generate call. */
+/* CUDA-event time (ms) of the device work of the last fa_batch_generate /
+ * fa_batch_generate_until call (fa_batch_step is not timed). */
 int fa_batch_last_ms(const fa_batch* batch, float* ms);
 
 /* ---------------------------------------------------------------------------
