@@ -580,33 +580,13 @@ __device__ __forceinline__ void publish_block(unsigned long long* dst, int n, in
 }
 
 // Waits for n quantised values in that format and unpacks them into xq/xs.
-// SENTINEL: warp 0 alone first waits for the n/32 scale words, a light poll
-// while the producers still compute.  That pays where consumers start waiting
-// long before the data (the down projection: CTAs without a gate/up block
-// would otherwise hammer the same lines for the whole gate/up phase) and costs
-// a round trip where they do not.
-template <bool SENTINEL>
+// POLL_NS > 0 paces the polls: the o and down projections' inputs are
+// awaited for microseconds by every GEMV CTA at once (the attention, the
+// gate/up blocks), and unpaced polls of the same few lines slow the stores
+// and copies the other CTAs make meanwhile (400 ns measured best on B200:
+// -7 % per step against the unpaced wait; 100-200 and 800-1600 slower).
+template <int POLL_NS = 0>
 __device__ __forceinline__ void gather_q8(Ctx& c, const unsigned long long* src, int n, unsigned tag) {
-  if (SENTINEL) {
-    if (c.warp == 0) {
-      for (unsigned it = 0;; ++it) {
-        bool all = true;
-        for (int j = c.lane; j < n / 32; j += 32) all &= (unsigned)(ld_word(src + n / 4 + j) >> 32) == tag;
-        if (__all_sync(0xffffffffu, all)) break;
-        if ((it & 1023) == 1023) {
-          if (c.sh()->abort || ld_flag(&c.A->ctrl->error)) {
-            c.sh()->abort = 1;
-            break;
-          }
-          if (it > kWaitLimit) {
-            raise_error(c.sh(), c.A->ctrl, kErrWaitData);
-            break;
-          }
-        }
-      }
-    }
-    csync();
-  }
   const int total = n / 4 + n / 32;  // <= 2 * CTHREADS
   unsigned pending = 0;
 #pragma unroll
@@ -625,7 +605,8 @@ __device__ __forceinline__ void gather_q8(Ctx& c, const unsigned long long* src,
         pending &= ~(1u << k);
       }
     if (pending == 0) break;
-    if (it >= 4096) __nanosleep(128);
+    if (POLL_NS > 0) __nanosleep(POLL_NS);
+    else if (it >= 4096) __nanosleep(128);
     if ((it & 1023) == 1023) {
       if (c.sh()->abort || ld_flag(&c.A->ctrl->error)) {
         c.sh()->abort = 1;
@@ -1105,7 +1086,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(const Mega
       }
       // ---- O: quantised attention output -> o + x ----
       if (sp.on > 0) {
-        gather_q8<false>(c, A.attn_t, QW, tl + kTagAttn);
+        gather_q8<400>(c, A.attn_t, QW, tl + kTagAttn);
         if (sh->abort) goto drain;
         MEGA_TRACE(ev + 4);
         const unsigned tag = tl + kTagA;
@@ -1144,7 +1125,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(const Mega
       MEGA_TRACE(ev + 11);
       // ---- D: quantised act -> down + a ----
       if (sp.dn > 0) {
-        gather_q8<true>(c, A.act_t, FFN, tl + kTagAct);
+        gather_q8<400>(c, A.act_t, FFN, tl + kTagAct);
         if (sh->abort) goto drain;
         MEGA_TRACE(ev + 12);
         const unsigned tag = tl + kTagX;
