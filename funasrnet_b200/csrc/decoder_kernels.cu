@@ -570,7 +570,6 @@ __global__ void __launch_bounds__(128) attn_softmax_v_kernel(const AttnArgs a) {
   __shared__ double lanes[8];
   __shared__ float s_inv;
   const int f = blockIdx.x, h = blockIdx.y, g = h >> 1, c = threadIdx.x;
-  const int kvw = a.kv_heads * D;
   const int len = *a.pos + f + 1;
   const float* sc = a.scores + ((size_t)f * a.heads + h) * a.capacity;
   float mx = -INFINITY;
