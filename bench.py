@@ -58,24 +58,35 @@ def model_path(quantized: bool) -> Path:
     return d / f"funasrnet_b200_synth_{'q8' if quantized else 'f32'}_{SEED}.gguf"
 
 
-def ensure_model(quantized: bool, rank: int, barrier) -> Path:
-    from funasrnet_b200._lib import check, lib
-
+def ensure_model(quantized: bool, rank: int, barrier, writer=None) -> Path:
+    """The seeded synthetic model file.  `writer(path)` makes it; the default is
+    the product library's generator, and the CPU reference arm passes the
+    oracle's (which writes the same bytes), so that arm never loads the product."""
     p = model_path(quantized)
     if rank == 0 and not p.exists():
         tmp = p.with_suffix(f".tmp{os.getpid()}")
-        check(lib().fa_synth_write_gguf(str(tmp).encode(), SEED, 0, 0, 0, 0, 1 if quantized else 0))
+        if writer is None:
+            from funasrnet_b200._lib import check, lib
+
+            check(lib().fa_synth_write_gguf(str(tmp).encode(), SEED, 0, 0, 0, 0, 1 if quantized else 0))
+        else:
+            writer(tmp)
         tmp.replace(p)
     barrier()
     return p
 
 
-def prefix(width: int, audio: int, ids: int, vocab: int, embed, seed: int = SEED):
-    """[audio][prompt] embeddings: N(0,1) audio vectors then Embed(ids)."""
+def product_normals(seed: int, stream: int, n: int):
     from funasrnet_b200._lib import check, lib
 
-    a = np.empty(audio * width, np.float32)
-    check(lib().fa_synth_normals(seed, 9001, 0, a.size, a.ctypes.data))
+    a = np.empty(n, np.float32)
+    check(lib().fa_synth_normals(seed, stream, 0, n, a.ctypes.data))
+    return a
+
+
+def prefix(width: int, audio: int, ids: int, vocab: int, embed, seed: int = SEED, normals=product_normals):
+    """[audio][prompt] embeddings: N(0,1) audio vectors then Embed(ids)."""
+    a = normals(seed, 9001, audio * width)
     rng = np.random.default_rng(seed)
     toks = rng.integers(0, vocab, ids).astype(np.int32)
     return np.concatenate([a, embed(toks)]), audio + ids
@@ -142,9 +153,16 @@ def measured_peak_hbm():
     return 6650.0, "fallback"
 
 
-def oracle_decode_rate(path: Path, cfg, steps: int, warmup: int, threads: int):
+def oracle_normals(seed: int, stream: int, n: int):
+    from oracle import oracle as O
+
+    return O.synth_normals(seed, stream, 0, n)
+
+
+def oracle_decode(path: Path, cfg, steps: int, warmup: int, threads: int):
     """CPU restatement of the reference decoder on this host: prefill (untimed),
-    warm-up steps, then `steps` timed greedy decode steps."""
+    `warmup` greedy steps, then `steps` timed greedy steps.  Returns
+    (tokens/s, seconds, the emitted tokens: the prefill's argmax first)."""
     from oracle import oracle as O
 
     O.build()
@@ -152,26 +170,37 @@ def oracle_decode_rate(path: Path, cfg, steps: int, warmup: int, threads: int):
     audio, ids, _, _ = cfg
     m = O.Model(path, 2048)
     s = O.Session(m)
-    emb, frames = prefix(m.width, audio, ids, m.vocab, m.embed)
+    emb, frames = prefix(m.width, audio, ids, m.vocab, m.embed, normals=oracle_normals)
     lg = s.decode(emb, frames)
     tok = O.greedy(lg)
+    toks = [tok]
     for _ in range(warmup):
         tok = O.greedy(s.decode(m.embed([tok]), 1))
+        toks.append(tok)
     t0 = time.perf_counter()
     for _ in range(steps):
         tok = O.greedy(s.decode(m.embed([tok]), 1))
+        toks.append(tok)
     dt = time.perf_counter() - t0
     s.close()
     m.close()
-    return steps / dt, dt
+    return steps / dt, dt, toks
+
+
+def source_digest() -> str:
+    """sha256 (16 hex digits) of the persistent kernel's source: the build a
+    recorded DRAM traffic figure belongs to."""
+    import hashlib
+
+    return hashlib.sha256((ROOT / "funasrnet_b200" / "csrc" / "mega.cu").read_bytes()).hexdigest()[:16]
 
 
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per decode step of
-# the persistent kernel on the bs1_400 workload: `ncu --set full` of one
-# 3-step launch read 2.043 GB and wrote 7.0 MB (profiles/
-# decode_mega_kernel_bs1_prefix408.md).  Algorithmic bytes at prefix 408:
-# 0.681 GB per step.
-MEASURED_TRAFFIC_PER_STEP = {"bs1_400": 0.6833e9}
+# the persistent kernel on the bs1_400 workload, from one `ncu` capture of a
+# 3-step launch, keyed by the digest of mega.cu it was captured on.  When the
+# source differs the bench reports traffic as null (not measured on this build).
+MEASURED_TRAFFIC = {"bs1_400": {"bytes_per_step": 0.6833e9, "mega_cu_sha256_16": "unrecorded",
+                                "captured": "2026-12-02"}}
 
 
 def profile_range(on: bool):
@@ -256,6 +285,54 @@ def batch_bench(be, path, name, steps, warmup, rank, world, dist, local, barrier
     }
 
 
+def fp32_bench(be, warmup, world, dist, local, barrier, peak, peak_kind):
+    """Config 3 (FP32 weights, prefix 100+8, greedy 128) on one GPU: the CUDA
+    graph step with the FP32 GEMV, timed over all 128 decode steps."""
+    from funasrnet_b200.decoder import CudaModel, QwenDecoder
+    from funasrnet_b200.shard import max_over_ranks
+
+    audio, ids, tokens, _ = CONFIGS["fp32"]
+    path = ensure_model(False, int(os.environ.get("RANK", "0")), barrier)
+    cm = CudaModel(be, path, capacity=2048)
+    dec = QwenDecoder(cm)
+    emb, frames = prefix(cm.width, audio, ids, cm.vocab, dec.embed)
+    try:
+        dec.reset()
+        dec.decode(emb, frames, want_logits=False)
+        dec.generate(warmup, end_ids=())
+        dec.reset()
+        dec.decode(emb, frames, want_logits=False)
+        barrier()
+        with ClockSampler(local) as clocks:
+            toks = dec.generate(tokens, end_ids=())
+        assert len(toks) == tokens
+        dev_ms = max_over_ranks(dec.last_generate_ms(), dist, f"cuda:{local}")
+        dec.reset()
+        _, tok = dec.decode(emb, frames, want_logits=False)
+        barrier()
+        t0 = time.perf_counter()
+        for _ in range(tokens):
+            tok, _ = dec.step(tok)
+        e2e_s = max_over_ranks(time.perf_counter() - t0, dist, f"cuda:{local}")
+        kernels = dec.kernels_per_step()
+    finally:
+        dec.close()
+    kv_per_pos = cm.layers * 2 * cm.kv_heads * cm.head_size * 2
+    step_bytes = cm.weight_bytes + cm.width * 4 + kv_per_pos * (frames + (tokens - 1) / 2.0 + 1)
+    ms = dev_ms / tokens
+    achieved = step_bytes / (ms * 1e-3) / 1e9
+    cm.close()
+    return {"metric": "decode tokens/sec (Qwen3-0.6B FP32 bs1)", "value": world * tokens / (dev_ms * 1e-3),
+            "unit": "tokens/s", "ms_per_step": ms, "steps": tokens, "dtype": "f32",
+            "workload": f"qwen3-0.6b-f32 bs1 prefix {audio}+{ids}, greedy {tokens} (BASELINE configs[2])",
+            "e2e": {"value": world * tokens / e2e_s, "unit": "tokens/s", "h2d_bytes_per_step": 4,
+                    "d2h_bytes_per_step": 4},
+            "roofline": {"bound": "hbm", "kernel": f"decode step (CUDA graph of {kernels} kernels, FP32 GEMV)",
+                         "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                         "bytes_per_step": step_bytes, "peak_source": peak_kind, "traffic": None},
+            "gpu_launches": kernels * tokens, "clocks": clocks.summary()}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -268,6 +345,7 @@ def main():
     ap.add_argument("--profile-range", action="store_true",
                     help="bracket the timed region with cudaProfilerStart/Stop (ncu --profile-from-start off)")
     ap.add_argument("--cpu-baseline-steps", type=int, default=24)
+    ap.add_argument("--no-fp32", action="store_true", help="skip the FP32 (config 3) entry of the default run")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     batched = args.config in BATCH_CONFIGS
@@ -303,9 +381,12 @@ def main():
         # The reference is C# (.NET 10); no dotnet here, so its CPU decoder is
         # timed through the C++ restatement on all host threads (rank 0 only).
         if rank == 0:
-            path = ensure_model(quantized, 0, lambda: None)
+            from oracle import oracle as O
+
+            path = ensure_model(quantized, 0, lambda: None,
+                                writer=lambda p: O.synth_write_gguf(p, SEED, quantized=quantized))
             threads = os.cpu_count() or 1
-            rate, dt = oracle_decode_rate(path, cfg, steps, warmup, threads)
+            rate, dt, _ = oracle_decode(path, cfg, steps, warmup, threads)
             line = {"metric": metric, "value": rate, "unit": "tokens/s", "n_gpus": args.gpus, "steps": steps,
                     "warmup": warmup, "ms_per_step": 1000.0 / rate, "higher_is_better": True, "scaling": "weak",
                     "vs_baseline": None, "dtype": "int8 x int8 -> int32, f32 accumulate", "data": "synthetic",
@@ -348,7 +429,7 @@ def main():
     dec.generate(warmup, end_ids=())
     # timed: fresh prefill (untimed), then K steps through the on-device loop
     dec.reset()
-    dec.decode(emb, frames, want_logits=False)
+    _, first_tok = dec.decode(emb, frames, want_logits=False)
     barrier()
     with ClockSampler(local) as clocks, profile_range(args.profile_range):
         toks = dec.generate(steps, end_ids=())
@@ -380,7 +461,8 @@ def main():
 
     # roofline of the decode step and of its largest single launch (lm_head GEMV)
     peak, peak_kind = measured_peak_hbm()
-    traffic = MEASURED_TRAFFIC_PER_STEP.get(args.config) if dec.persistent_grid() else None
+    rec = MEASURED_TRAFFIC.get(args.config) if dec.persistent_grid() else None
+    traffic = rec["bytes_per_step"] if rec and rec["mega_cu_sha256_16"] == source_digest() else None
     kv_bytes_per_pos = cm.layers * 2 * cm.kv_heads * cm.head_size * 2
     mean_pos = frames + (steps - 1) / 2.0
     step_bytes = cm.weight_bytes + 1088 + kv_bytes_per_pos * (mean_pos + 1)
@@ -411,7 +493,11 @@ def main():
                 "d2h_bytes_per_step": 4},
         "roofline": {"bound": "hbm", "kernel": kernel_name, "achieved": achieved, "peak": peak,
                      "unit": "GB/s", "frac": achieved / peak, "traffic": traffic,
-                     "traffic_unit": "DRAM bytes per decode step (ncu capture of this workload)",
+                     "traffic_unit": "DRAM bytes per decode step (ncu capture of this workload on this source; "
+                                     "null when the kernel source differs from the captured one)",
+                     "traffic_source": {"mega_cu_sha256_16": source_digest(),
+                                        "captured_on": rec["mega_cu_sha256_16"] if rec else None,
+                                        "date": rec["captured"] if rec else None},
                      "bytes_per_step": step_bytes, "peak_source": peak_kind},
         "gpu_launches": launches,
         "clocks": clocks.summary(),
@@ -431,12 +517,23 @@ def main():
             line["batched"][name] = {k: r[k] for k in ("value", "ms_per_step", "sessions_per_gpu", "steps", "e2e",
                                                        "roofline", "clocks")}
             line["batched"][name]["workload"] = r["config"]["workload"]
+    if args.config == "bs1_400" and not args.no_fp32:
+        line["fp32"] = fp32_bench(be, warmup, world, dist, local, barrier, peak, peak_kind)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         threads = os.cpu_count() or 1
-        rate, dt = oracle_decode_rate(path, cfg, args.cpu_baseline_steps, 2, threads)
+        rate, dt, otoks = oracle_decode(path, cfg, args.cpu_baseline_steps, 2, threads)
         line["cpu_baseline"] = {"value": rate, "unit": "tokens/s", "cores": threads, "kind": "port",
                                 "sample": f"{args.cpu_baseline_steps} decode steps after the {frames}-frame prefill "
                                           f"({dt:.1f} s of CPU decode)"}
+        # the reference's published CPU setup runs 4 threads
+        rate4, dt4, _ = oracle_decode(path, cfg, max(4, args.cpu_baseline_steps // 3), 1, 4)
+        line["cpu_baseline_4_threads"] = {"value": rate4, "unit": "tokens/s", "cores": 4, "kind": "port",
+                                          "sample": f"{max(4, args.cpu_baseline_steps // 3)} decode steps after the "
+                                                    f"{frames}-frame prefill ({dt4:.1f} s)"}
+        # the timed GPU tokens against the oracle's greedy tokens from the same prefix
+        gpu = [first_tok] + list(toks)
+        n = min(len(gpu), len(otoks))
+        line["tokens_match_oracle"] = {"compared": n, "equal": gpu[:n] == otoks[:n]}
     if rank == 0:
         print(json.dumps(line), flush=True)
     be.dispose()

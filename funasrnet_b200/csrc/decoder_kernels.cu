@@ -779,21 +779,43 @@ __global__ void step_end_kernel(const StepState s, int frames) {
 }
 
 // Opts every GEMV instantiation into the full 227 KB of dynamic shared memory
-// once per device (the per-launch request still sets the occupancy).
+// once per device context (the per-launch request still sets the occupancy).
+// Function attributes belong to the context, so a device whose context was
+// destroyed and created again (cudaDeviceReset) is set up again.
 void ensure_gemv_attributes() {
   constexpr int kMaxDevices = 64;
-  static std::once_flag flags[kMaxDevices];
+  static std::mutex mu;
+  static void* done[kMaxDevices] = {};
   int dev = 0;
   FA_CUDA(cudaGetDevice(&dev));
   if (dev < 0 || dev >= kMaxDevices) throw Error(kErrCuda, "device index out of range");
-  std::call_once(flags[dev], [] {
-    FA_CUDA(cudaFuncSetAttribute(gemv_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemvMaxSmem));
-    FA_CUDA(cudaFuncSetAttribute(gemv_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemvMaxSmem));
-    FA_CUDA(cudaFuncSetAttribute(gemv_f32_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemvMaxSmem));
-  });
+  void* ctx = current_context();
+  std::lock_guard<std::mutex> lk(mu);
+  if (done[dev] == ctx) return;
+  FA_CUDA(cudaFuncSetAttribute(gemv_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemvMaxSmem));
+  FA_CUDA(cudaFuncSetAttribute(gemv_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemvMaxSmem));
+  FA_CUDA(cudaFuncSetAttribute(gemv_f32_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemvMaxSmem));
+  done[dev] = ctx;
 }
 
 }  // namespace
+
+void* current_context() {
+  // cuCtxGetCurrent through the runtime's driver entry point (no libcuda link).
+  using Fn = int (*)(void**);
+  static Fn fn = [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return (Fn) nullptr;
+    return reinterpret_cast<Fn>(p);
+  }();
+  if (!fn) throw Error(kErrCuda, "cuCtxGetCurrent is unavailable");
+  void* ctx = nullptr;
+  if (fn(&ctx) != 0 || ctx == nullptr) throw Error(kErrCuda, "no current CUDA context");
+  return ctx;
+}
 
 void prepare_kernels() { ensure_gemv_attributes(); }
 

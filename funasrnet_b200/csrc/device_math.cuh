@@ -47,7 +47,7 @@ __device__ __forceinline__ float warp_sum_f(float v) {
   return v;
 }
 
-// exp as the reference's TensorMath.ExpAvx (TensorMath.ExpAvx.cs:83-116)
+// exp as the reference's TensorMath.ExpAvx (TensorMath.ExpAvx.cs:24-57)
 // evaluates it per lane: clamp to [-104, 104] (NaN propagates), x = n*ln2 + r
 // with n = round-half-even(x * log2 e), degree-8 Taylor polynomial of exp(r)
 // in double with FMAs, scaled by 2^n and narrowed to float.  Every operation

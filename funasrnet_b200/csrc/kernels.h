@@ -44,6 +44,9 @@ struct GemvArgs {
 void launch_gemv(const GemvArgs& a, cudaStream_t stream);
 // One-time per-device kernel attributes; call before any stream capture.
 void prepare_kernels();
+// The calling thread's current CUDA context (a CUcontext), which identifies
+// per-context state such as function attributes and module-variable addresses.
+void* current_context();
 // Dynamic shared memory one Q8 GEMV launch needs (<= 227 KB or the launch is refused).
 int gemv_smem_bytes(int K, int epilogue);
 // CTAs of one single-frame Q8 GEMV launch over `tiles` 8-row tiles (the number

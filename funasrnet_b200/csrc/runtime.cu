@@ -609,22 +609,31 @@ namespace {
 
 constexpr int kNoAllocDevices = 64;
 std::mutex g_noalloc_mu;
-unsigned* g_noalloc_addr[kNoAllocDevices] = {};
+struct NoAllocEntry {
+  void* context;   // the context the address belongs to
+  unsigned* addr;
+};
+NoAllocEntry g_noalloc[kNoAllocDevices] = {};
 
 // Device address of the scratch on `device`, which must be current.  The first
-// call per device looks the address up, zeroes the block and sets the GEMV
-// kernels' shared-memory attribute; later calls only read the table.
+// call per device context looks the address up, zeroes the block and sets the
+// GEMV kernels' shared-memory attribute; later calls in the same context only
+// read the table.  Module variables live per context, so a context destroyed
+// and created again (cudaDeviceReset) gets the set-up again.
 unsigned* noalloc_scratch(int device) {
   if (device < 0 || device >= kNoAllocDevices) throw Error(kErrArgument, "device ordinal beyond the scratch table");
+  void* ctx = current_context();
   std::lock_guard<std::mutex> lk(g_noalloc_mu);
-  if (g_noalloc_addr[device] == nullptr) {
+  NoAllocEntry& e = g_noalloc[device];
+  if (e.addr == nullptr || e.context != ctx) {
     void* p = nullptr;
     FA_CUDA(cudaGetSymbolAddress(&p, g_noalloc_scratch));
     FA_CUDA(cudaMemset(p, 0, sizeof(g_noalloc_scratch)));
     prepare_kernels();
-    g_noalloc_addr[device] = static_cast<unsigned*>(p);
+    e.context = ctx;
+    e.addr = static_cast<unsigned*>(p);
   }
-  return g_noalloc_addr[device];
+  return e.addr;
 }
 
 }  // namespace
@@ -1794,6 +1803,7 @@ struct fa_batch {
   bool graph_logits = false;
   int* pinned = nullptr;  // [8 + max(n, 64)]: end-token count at 7, token / end-id staging at 8; then words()
   int dev_n_end = -1;     // end-token count the device holds
+  std::vector<int> dev_ends;  // and its end-token ids (host copy)
   // Per part k, its words after a run: positions [n_k], tokens [n_k], step
   // counter, error word (read back in one copy per part).
   int* words(int k, const BatchPart* p) { return pinned + 8 + std::max(n, 64) + 2 * p->f0 + 2 * k; }
@@ -1963,13 +1973,16 @@ void update_order(fa_batch* b) {
 }
 
 // Launches the step graph `steps` times and checks the batched kernels' error
-// words; n_end end tokens (ids staged in b->pinned + 8) stop a session.
+// words; n_end end tokens (ids staged in b->pinned + 8) stop a session.  The
+// end-token set is uploaded only when it differs from the one the device holds.
 void run_batch(fa_batch* b, int steps, bool want_logits, int n_end = 0, bool timed = true) {
   update_order(b);
-  if (n_end > 0 || b->dev_n_end != n_end) {
+  const int* ends = b->pinned + 8;
+  if (b->dev_n_end != n_end || !std::equal(ends, ends + n_end, b->dev_ends.begin())) {
     b->pinned[7] = n_end;
     FA_CUDA(cudaMemcpyAsync(b->ends.p, b->pinned + 7, (size_t)(1 + n_end) * 4, cudaMemcpyHostToDevice, b->stream));
     b->dev_n_end = n_end;
+    b->dev_ends.assign(ends, ends + n_end);
   }
   // step counter, error word and stop flags are contiguous: one clear per part
   for (auto& p : b->parts) FA_CUDA(cudaMemsetAsync(p->d_counter(), 0, (size_t)(p->n + 2) * 4, b->stream));

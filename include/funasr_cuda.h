@@ -223,8 +223,9 @@ int fa_session_time_lm_head(fa_session* session, int iters, float* ms);
  * bit-identical to fa_session_step on that session alone.
  * ------------------------------------------------------------------------ */
 #define FA_BATCH_MAX_SESSIONS 4096
-/* Groups n distinct sessions of one model (the survey's fa_cuda_batch_step
- * over sessions[]).  FA_DECLINED when the model's shapes do not fit the
+/* Groups n distinct sessions of one model, as SpeechRuntime's independent
+ * contexts (src/FunAsrNet/SpeechRuntime.cs:18-22) decode them, into one
+ * batched step over sessions[].  FA_DECLINED when the model's shapes do not fit the
  * tensor-core path (rows % 128, cols % 256, head size 128, paired GQA).  The
  * group holds the session handles: free it before its sessions. */
 int fa_batch_create(fa_session* const* sessions, int n, fa_batch** out);
@@ -275,7 +276,9 @@ int fa_batch_last_ms(const fa_batch* batch, float* ms);
  *
  * Limit: rows <= FA_NOALLOC_MAX_ROWS, else FA_ERR_CAPACITY.  The argmax
  * partials live in a fixed 64 KB block of module memory, one per device.  The
- * first call on a device sets that block up: make that first call before any
+ * first call on a device sets that block up (and again after the device's
+ * context was destroyed and re-created, e.g. by cudaDeviceReset, which also
+ * invalidates every handle of this library): make that first call before any
  * stream capture.  All calls on one device share the block, so calls that
  * overlap in time on one device race.  Serialise them, on one stream or with
  * events between streams. */

@@ -48,6 +48,8 @@ def lib() -> C.CDLL:
             "or_silu_mul": (None, [vp, vp, i64]),
             "or_greedy": (i64, [vp, i64]),
             "or_exp": (f32, [f32]),
+            "or_set_exp_mode": (i32, [i32]),
+            "or_get_exp_mode": (i32, []),
             "or_half_to_float": (f32, [C.c_uint16]),
             "or_float_to_half": (C.c_uint16, [f32]),
             "or_model_load": (vp, [C.c_char_p, i32]),
@@ -68,6 +70,8 @@ def lib() -> C.CDLL:
             "or_session_kv": (i32, [vp, i32, vp, vp]),
             "or_session_trace_layer0": (i32, [vp, vp]),
             "or_session_debug": (i32, [vp, C.c_char_p, vp]),
+            "or_synth_normals": (i32, [C.c_uint64, C.c_uint64, C.c_uint64, i64, vp]),
+            "or_synth_write_gguf": (i32, [C.c_char_p, C.c_uint64, i32, i32, i32, i32, i32]),
         }
         for name, (res, args) in sigs.items():
             fn = getattr(h, name)
@@ -87,6 +91,20 @@ def f32(a):
 
 def set_threads(n: int) -> None:
     lib().or_set_threads(int(n))
+
+
+EXP_LOCAL, EXP_RUNTIME = 0, 1
+
+
+def set_exp_mode(mode: int) -> None:
+    """0: the reference's ExpAvx everywhere (its .NET 11 selection, the default);
+    1: the correctly rounded exp standing in for the .NET 10 runtime exp."""
+    if lib().or_set_exp_mode(int(mode)) != 0:
+        raise ValueError(f"bad exp mode {mode}")
+
+
+def get_exp_mode() -> int:
+    return int(lib().or_get_exp_mode())
 
 
 def quantize(x):
@@ -170,6 +188,18 @@ def silu_mul(g, u):
 def greedy(logits) -> int:
     x = f32(logits).reshape(-1)
     return int(lib().or_greedy(_p(x), x.size))
+
+
+def synth_normals(seed: int, stream: int, start: int, n: int):
+    out = np.empty(n, np.float32)
+    if lib().or_synth_normals(seed, stream, start, n, _p(out)) != 0:
+        raise ValueError("bad synth_normals arguments")
+    return out
+
+
+def synth_write_gguf(path, seed: int, layers=0, vocab=0, width=0, ffn=0, quantized=True) -> None:
+    if lib().or_synth_write_gguf(str(path).encode(), seed, layers, vocab, width, ffn, 1 if quantized else 0) != 0:
+        raise OSError(f"cannot write {path}")
 
 
 def half_to_float(bits: int) -> float:

@@ -54,13 +54,12 @@ inline int net_float_to_int(float f) {
 // MathF.Round(v, MidpointRounding.AwayFromZero).
 inline float round_away(float v) { return std::round(v); }
 
-// TensorMath.ExpAvx / ExpReduced (TensorMath.ExpAvx.cs:83-116), one lane:
+// TensorMath.ExpAvx / ExpReduced (TensorMath.ExpAvx.cs:24-57), one lane:
 // clamp to [-104, 104] (NaN propagates), x = n*ln2 + r with n = round-to-even
 // of x*log2(e), degree-8 Taylor polynomial of exp(r) in double with FMAs,
 // times 2^n, narrowed to float.  The reference selects this exp on .NET 11
-// (its .NET 10 build calls Vector256.Exp, within an ulp of it); the oracle uses
-// it for every exp of the decoder (softmax lanes and tail, SiLU).
-inline float exp_avx(float v) {
+// (TensorMath.ExpAvx.cs:11,17-18).
+inline float exp_local(float v) {
   if (std::isnan(v)) return v;
   float c = v < -104.0f ? -104.0f : (v > 104.0f ? 104.0f : v);
   double x = (double)c;
@@ -80,6 +79,20 @@ inline float exp_avx(float v) {
   return (float)(e * scale);
 }
 
+// The exp a .NET 10 build of the reference runs instead: Vector256.Exp for the
+// 8-lane loops (TensorMath.ExpAvx.cs:17-18), MathF.Exp for the softmax and SiLU
+// scalar tails (TensorMath.SoftmaxAvx.cs:44, TensorMath.Elementwise.cs:194).
+// Both are the runtime's, not the reference's code; they are stood in for by
+// the correctly rounded binary32 exp, computed as the double exp narrowed to
+// float (the double result is within an ulp of double, so the narrowing is the
+// correctly rounded float except within 2^-29 of a float rounding boundary).
+inline float exp_runtime(float v) { return (float)std::exp((double)v); }
+
+// 0: every exp of the decoder is ExpAvx (the .NET 11 selection, the default);
+// 1: every exp is exp_runtime (the .NET 10 selection).
+int g_exp_mode = 0;
+inline float exp_avx(float v) { return g_exp_mode == 1 ? exp_runtime(v) : exp_local(v); }
+
 // Vector128<float>.Sum as lowered by RyuJIT on x64: (v0 + v1) + (v2 + v3).
 inline float sum4(float v0, float v1, float v2, float v3) { return (v0 + v1) + (v2 + v3); }
 
@@ -93,6 +106,12 @@ inline float fold8(const float* a) {
 extern "C" {
 
 void or_set_threads(int threads) { g_threads = threads < 1 ? 1 : threads; }
+int or_set_exp_mode(int mode) {
+  if (mode != 0 && mode != 1) return -1;
+  g_exp_mode = mode;
+  return 0;
+}
+int or_get_exp_mode(void) { return g_exp_mode; }
 int or_get_threads(void) { return g_threads; }
 const char* or_last_error(void) { return g_error.c_str(); }
 

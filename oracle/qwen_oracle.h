@@ -73,8 +73,13 @@ int or_attention_pair(const float* query, const float* keys, const float* values
 /* TensorMath.SiluMultiply, TensorMath.Elementwise.cs:167-196 (gate overwritten). */
 void or_silu_mul(float* gate, const float* up, int64_t n);
 
-/* TensorMath.ExpAvx (TensorMath.ExpAvx.cs:83-116) for one value: the exp the
- * oracle uses everywhere. */
+/* The exp of the decoder (softmax lanes and tail, SiLU) for one value, in the
+ * selected mode: 0 (default) TensorMath.ExpAvx (TensorMath.ExpAvx.cs:24-57),
+ * which the reference selects on .NET 11 (TensorMath.ExpAvx.cs:11,17-18);
+ * 1 the runtime exp a .NET 10 build calls (Vector256.Exp, MathF.Exp), stood in
+ * for by the correctly rounded binary32 exp.  The mode is process-wide. */
+int or_set_exp_mode(int mode);
+int or_get_exp_mode(void);
 float or_exp(float x);
 
 /* QwenDecoder.Greedy, QwenDecoder.cs:278-326. */
@@ -118,6 +123,14 @@ int or_session_trace_layer0(void* session, float* out);
 /* Layer-0 intermediates of the last Decode: "q" (after RoPE), "attn", "a",
  * "act", "x".  Returns the float count (out may be NULL to query it). */
 int or_session_debug(void* session, const char* name, float* out);
+
+/* ---- seeded synthetic inputs (synth.cpp) ---- */
+
+/* out[i] = N(0,1) sample start+i of stream `stream` under `seed`. */
+int or_synth_normals(uint64_t seed, uint64_t stream, uint64_t start, int64_t n, float* out);
+/* The synthetic Qwen3 GGUF of the benchmark configs (dims <= 0 take the
+ * Qwen3-0.6B defaults); byte-identical to the product's fa_synth_write_gguf. */
+int or_synth_write_gguf(const char* path, uint64_t seed, int layers, int vocab, int width, int ffn, int quantized);
 
 #ifdef __cplusplus
 }

@@ -18,7 +18,7 @@ from the deterministic inputs of the reference's own checks:
   patterns widened to float32 (NaNs: payload kept, quiet bit set).
 * rmsnorm.npz -- TensorMath.Elementwise.cs:59-96 evaluated in float64 / float32.
 * greedy.npz -- QwenDecoder.cs:278-326 edge cases.
-* exp_ref.npz -- TensorMath.ExpAvx.cs:83-116 evaluated with Python floats
+* exp_ref.npz -- TensorMath.ExpAvx.cs:24-57 evaluated with Python floats
   (IEEE double; each FMA rounded once via exact rationals).
 """
 from __future__ import annotations
