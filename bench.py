@@ -531,7 +531,8 @@ def main():
                                           "sample": f"{max(4, args.cpu_baseline_steps // 3)} decode steps after the "
                                                     f"{frames}-frame prefill ({dt4:.1f} s)"}
         # the timed GPU tokens against the oracle's greedy tokens from the same prefix
-        gpu = [first_tok] + list(toks)
+        gpu = list(toks)  # generate emits the prefill's argmax first
+        assert gpu[0] == first_tok
         n = min(len(gpu), len(otoks))
         line["tokens_match_oracle"] = {"compared": n, "equal": gpu[:n] == otoks[:n]}
     if rank == 0:

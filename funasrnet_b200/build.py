@@ -23,7 +23,7 @@ ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 # explicitly, matching the reference's RyuJIT evaluation.
 NVCC_FLAGS = ARCH + ["-O3", "-lineinfo", "-std=c++17", "-fmad=false", "-Xcompiler", "-fPIC,-O3,-ffp-contract=off",
                      "-Xptxas", "-v"]
-SOURCES = ["decoder_kernels.cu", "mega.cu", "batch.cu", "runtime.cu", "host_util.cpp"]
+SOURCES = ["decoder_kernels.cu", "mega.cu", "batch.cu", "f32_stream.cu", "runtime.cu", "host_util.cpp"]
 
 
 def nvcc() -> str:

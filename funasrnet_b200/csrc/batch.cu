@@ -30,6 +30,7 @@
 
 #include "batch.h"
 #include "device_math.cuh"
+#include "tma_host.h"
 
 namespace fa {
 namespace {
@@ -1067,38 +1068,6 @@ void launch_pdl(void (*kernel)(KArgs...), int grid, int block, size_t smem, cuda
   FA_CUDA(cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...));
 }
 
-int sm_count() {
-  static int count[64] = {};
-  int dev = 0;
-  FA_CUDA(cudaGetDevice(&dev));
-  if (dev < 0 || dev >= 64) dev = 0;
-  if (count[dev] == 0) FA_CUDA(cudaDeviceGetAttribute(&count[dev], cudaDevAttrMultiProcessorCount, dev));
-  return count[dev];
-}
-
-PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-  static std::once_flag once;
-  std::call_once(once, [] {
-    void* p = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
-  });
-  if (!fn) throw Error(kErrCuda, "cuTensorMapEncodeTiled is unavailable");
-  return fn;
-}
-
-void encode(CUtensorMap* m, CUtensorMapDataType type, int rank, const void* base, const cuuint64_t* dims,
-            const cuuint64_t* strides, const cuuint32_t* box) {
-  const cuuint32_t estr[3] = {1, 1, 1};
-  const CUresult r = encode_fn()(m, type, rank, const_cast<void*>(base), dims, strides, box, estr,
-                                 CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
-                                 CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS) throw Error(kErrCuda, "cuTensorMapEncodeTiled failed: " + std::to_string((int)r));
-}
-
 // Tensor maps over the weights' 8-row tile layout and the frame-tile operand.
 // Every box starts at an x coordinate that is a multiple of 16 bytes.
 BmmMaps make_maps(const BmmArgs& a, int ns) {
@@ -1108,25 +1077,25 @@ BmmMaps make_maps(const BmmArgs& a, int ns) {
     const cuuint64_t dims[3] = {128, (cuuint64_t)K / 16, (cuuint64_t)a.w.tiles};
     const cuuint64_t str[2] = {128, (cuuint64_t)a.w.tile_bytes};
     const cuuint32_t box[3] = {128, 16, 16};
-    encode(&mp.a, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, a.w.base, dims, str, box);
+    encode_tensor_map(&mp.a, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, a.w.base, dims, str, box);
   }
   {
     const cuuint64_t dims[2] = {(cuuint64_t)(K / 32) * 8 * S, (cuuint64_t)a.w.tiles};
     const cuuint64_t str[1] = {(cuuint64_t)a.w.tile_bytes};
     const cuuint32_t box[2] = {(cuuint32_t)(64 * S), 16};
-    encode(&mp.sa, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, a.w.base + (size_t)8 * K, dims, str, box);
+    encode_tensor_map(&mp.sa, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, a.w.base + (size_t)8 * K, dims, str, box);
   }
   {
     const cuuint64_t dims[3] = {128, (cuuint64_t)K / 16, (cuuint64_t)a.n_pad / 8};
     const cuuint64_t str[2] = {128, (cuuint64_t)8 * K};
     const cuuint32_t box[3] = {128, 16, (cuuint32_t)(ns / 8)};
-    encode(&mp.b, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, a.xq, dims, str, box);
+    encode_tensor_map(&mp.b, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, a.xq, dims, str, box);
   }
   {
     const cuuint64_t dims[2] = {(cuuint64_t)a.n_pad, (cuuint64_t)K / 32};
     const cuuint64_t str[1] = {(cuuint64_t)a.n_pad * 4};
     const cuuint32_t box[2] = {(cuuint32_t)ns, 8};
-    encode(&mp.sb, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, a.xs, dims, str, box);
+    encode_tensor_map(&mp.sb, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, a.xs, dims, str, box);
   }
   return mp;
 }
@@ -1141,6 +1110,38 @@ void launch_bmm_t(const BmmArgs& a, cudaStream_t stream) {
 }
 
 }  // namespace
+
+int sm_count() {
+  static int count[64] = {};
+  int dev = 0;
+  FA_CUDA(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64) dev = 0;
+  if (count[dev] == 0) FA_CUDA(cudaDeviceGetAttribute(&count[dev], cudaDevAttrMultiProcessorCount, dev));
+  return count[dev];
+}
+
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  if (!fn) throw Error(kErrCuda, "cuTensorMapEncodeTiled is unavailable");
+  return fn;
+}
+
+void encode_tensor_map(CUtensorMap* m, CUtensorMapDataType type, int rank, const void* base, const cuuint64_t* dims,
+                       const cuuint64_t* strides, const cuuint32_t* box) {
+  const cuuint32_t estr[3] = {1, 1, 1};
+  const CUresult r = encode_fn()(m, type, rank, const_cast<void*>(base), dims, strides, box, estr,
+                                 CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                                 CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) throw Error(kErrCuda, "cuTensorMapEncodeTiled failed: " + std::to_string((int)r));
+}
 
 void prepare_batch_kernels() {
   static std::once_flag once;

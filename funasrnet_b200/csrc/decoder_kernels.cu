@@ -919,6 +919,7 @@ void pack_f32(const float* w, int rows, int cols, float* out) {
 int gemv_f32_smem_bytes(int K) { return kF32Frames * K * 4; }
 
 void launch_gemv_f32(const F32GemvArgs& a, cudaStream_t stream) {
+  if (launch_gemv_f32_stream(a, stream)) return;
   const int smem = gemv_f32_smem_bytes(a.w.cols);
   if (smem > kGemvMaxSmem) throw Error(kErrCapacity, "GEMV inner dimension too large for shared memory");
   if (a.w.cols % 32 != 0) throw Error(kErrArgument, "FP32 GEMV needs cols % 32 == 0");

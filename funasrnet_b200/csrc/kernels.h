@@ -76,8 +76,14 @@ struct F32GemvArgs {
   const float* res = nullptr;
   const float* bias = nullptr;
   const int* skip = nullptr;
+  int* err = nullptr;         // optional error word (a bounded wait gave up)
 };
 void launch_gemv_f32(const F32GemvArgs& a, cudaStream_t stream);
+// Streaming one-frame FP32 GEMV (f32_stream.cu): TMA-fed persistent CTAs,
+// programmatic dependent launch.  False (nothing launched) when the shape or
+// epilogue is outside it; launch_gemv_f32 then uses the frame-tiled kernel.
+bool launch_gemv_f32_stream(const F32GemvArgs& a, cudaStream_t stream);
+constexpr int kF32StreamWaitError = 21;  // error-word code of a wait that gave up
 int gemv_f32_smem_bytes(int K);
 // act[f][i] = silu(buf[f][i]) * buf[f][ffn + i]  (gate and up rows concatenated)
 void launch_silu_pair(const float* buf, int frames, int ffn, float* act, const int* skip, cudaStream_t stream);

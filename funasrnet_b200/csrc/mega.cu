@@ -454,6 +454,7 @@ struct Ctx {
   const MegaArgs* A;
   unsigned long long* trace;  // this CTA's row of phase stamps during a traced step, else nullptr
   int nw, na;                 // copies consumed per ring (weights / attention)
+  int wait_ev;                // trace event receiving the next phase's weight-wait cycles (-1: none)
   int tid, warp, lane;
   __device__ Shared* sh() const { return sm<Shared>(kOffShared); }
   __device__ int8_t* xq() const { return sm<int8_t>(kOffXq); }
@@ -549,7 +550,9 @@ template <int K, typename Epi>
 __device__ __forceinline__ bool w8a8_phase(Ctx& c, int nt, int per, Epi epi) {
   constexpr int NS = K / 1024, TB = 8 * K + (K / 32) * 16;
   const int np = (nt + per - 1) / per;
+  const long long w0 = c.trace != nullptr ? clock64() : 0;
   const bool failed = !ring_acquire_all(ring_w(), c.nw, np, c.sh(), c.A->ctrl);
+  if (c.trace && c.tid == 0 && c.wait_ev >= 0) c.trace[c.wait_ev] = (unsigned long long)(clock64() - w0);
   // Every warp takes the same branch: the jobs below wait on each other at
   // named barriers, which have no time limit.  (On failure the drain waits
   // for the copies in flight.)
@@ -824,8 +827,13 @@ __device__ __noinline__ int attention(Ctx c, int layer, int pos, unsigned tag_in
 #pragma unroll
   for (int i = 0; i < D / 8; ++i) qj[i] = c.aq()[j + 8 * i];
   const int chunks = (pos + CHUNK - 1) / CHUNK;
+  const bool timed = c.trace != nullptr;  // wait and loop cycles for the trace
+  long long kwait = 0;
+  const long long s0 = timed ? clock64() : 0;
   for (int ch = 0; ch < chunks; ++ch) {
+    const long long k0 = timed ? clock64() : 0;
     const uint8_t* kb = ring_acquire(ring_a(), c.na, c.sh(), A.ctrl);
+    if (timed) kwait += clock64() - k0;
     if (kb == nullptr) return c.na;
     const int t = ch * CHUNK + slot;
     float acc = 0.0f;
@@ -859,6 +867,10 @@ __device__ __noinline__ int attention(Ctx c, int layer, int pos, unsigned tag_in
     acc = __fadd_rn(acc, __shfl_down_sync(0xffffffffu, acc, 1));
     acc = __fadd_rn(acc, __shfl_down_sync(0xffffffffu, acc, 2));
     if (c.lane == 0) c.sc()[pos] = acc;
+  }
+  if (c.trace && c.tid == 0) {
+    c.trace[kTraceLayerEvents * layer + 6] = (unsigned long long)kwait;
+    c.trace[kTraceLayerEvents * layer + 8] = (unsigned long long)(clock64() - s0);
   }
   csync();
   if (c.trace && c.tid == 0) c.trace[kTraceLayerEvents * layer + 3] = global_ns();
@@ -902,8 +914,12 @@ __device__ __noinline__ int attention(Ctx c, int layer, int pos, unsigned tag_in
   // V sum per channel in position order (TensorMath.AttentionAvx.cs:188-213): warps 0..3.
   if (c.warp < 4) {
     float acc = 0.0f;
+    long long vwait = 0;
+    const long long v0 = timed ? clock64() : 0;
     for (int ch = 0; ch < chunks; ++ch) {
+      const long long t0 = timed ? clock64() : 0;
       const uint8_t* vb = ring_acquire(ring_a(), c.na + ch, c.sh(), A.ctrl);
+      if (timed) vwait += clock64() - t0;
       if (vb == nullptr) return c.na + ch;
       const __half* vv = reinterpret_cast<const __half*>(vb) + c.tid;
       const float* pr = c.sc() + ch * CHUNK;
@@ -930,6 +946,10 @@ __device__ __noinline__ int attention(Ctx c, int layer, int pos, unsigned tag_in
       if (c.lane == 0) mbar_arrive_count(&ring_a().empty[(c.na + ch) % ASLOTS], c.warp == 0 ? CWARPS - 3 : 1);
     }
     acc = __fadd_rn(acc, __fmul_rn(c.av()[c.tid], c.sc()[pos]));
+    if (c.trace && c.tid == 0) {
+      c.trace[kTraceLayerEvents * layer + 7] = (unsigned long long)vwait;
+      c.trace[kTraceLayerEvents * layer + 9] = (unsigned long long)(clock64() - v0);
+    }
     // The O projection's input quantisation of this head's four blocks
     // (block 4h + warp), done once here instead of in every GEMV CTA.
     publish_block(A.attn_t, QW, h * 4 + c.warp, acc, tag_out, c.lane);
@@ -981,6 +1001,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(const Mega
   Ctx c;
   c.A = &sh->args;
   c.nw = c.na = 0;
+  c.wait_ev = -1;
   c.trace = nullptr;
   c.tid = tid;
   c.warp = warp;
@@ -1071,6 +1092,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(const Mega
       {
         const unsigned tag = tl + kTagQkv;
         const int q0 = sp.q0;
+        c.wait_ev = ev + 2;
         if (!w8a8_phase<W>(c, sp.qn, 3, [&](int t, int r, float v) { st_word(A.qkv_t + (q0 + t) * 8 + r, pack(v, tag)); }))
           goto drain;
       }
@@ -1091,6 +1113,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(const Mega
         MEGA_TRACE(ev + 4);
         const unsigned tag = tl + kTagA;
         const int o0 = sp.o0;
+        c.wait_ev = ev + 6;
         if (!w8a8_phase<QW>(c, sp.on, 1, [&](int t, int r, float v) {
               const int row = (o0 + t) * 8 + r;
               st_word(A.a_t + row, pack(__fadd_rn(v, c.xres()[row]), tag));
@@ -1115,6 +1138,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(const Mega
       if (sh->abort) goto drain;
       MEGA_TRACE(ev + 9);
       for (int bj = 0; bj < sp.gbn; ++bj) {
+        c.wait_ev = bj == 0 ? ev + 10 : -1;
         if (!w8a8_phase<W>(c, 8, 3, [&](int t, int r, float v) { c.part()[t * 8 + r] = v; })) goto drain;
         if (warp == 0) {  // lane = 8 * pair + row: the block's 32 SiLU(gate) * up values
           const float act = silu_mul1(c.part()[(lane >> 3) * 16 + (lane & 7)], c.part()[(lane >> 3) * 16 + 8 + (lane & 7)]);
@@ -1130,6 +1154,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(const Mega
         MEGA_TRACE(ev + 12);
         const unsigned tag = tl + kTagX;
         const int d0 = sp.d0;
+        c.wait_ev = ev + 14;
         if (!w8a8_phase<FFN>(c, sp.dn, 1, [&](int t, int r, float v) {
               const int row = (d0 + t) * 8 + r;
               st_word(A.x_t + row, pack(__fadd_rn(v, c.ares()[row]), tag));

@@ -66,9 +66,11 @@ struct MegaArgs {
   // Optional phase timestamps of the first step (%globaltimer, ns):
   // trace[cta * kTraceEvents + event].  Events of layer l are 16*l + e.
   // GEMV CTAs: per phase p (0 Q, 1 O, 2 GU, 3 D) e = 4p + {0 inputs ready,
-  // 1 activations quantised, 2 block products done, 3 outputs stored}.
-  // Attention CTAs: e = {0 layer start, 1 q/k/v loaded, 2 norm + RoPE + KV
-  // write, 3 scores, 4 softmax, 5 output stored}.  Then 16*layers + {0 LM
+  // 1 activations quantised, 2 SM cycles spent waiting for the phase's weight
+  // pieces, 3 outputs stored}.  Attention CTAs: e = {0 layer start, 1 q/k/v
+  // loaded, 2 norm + RoPE + KV write, 3 scores, 4 softmax, 5 output stored},
+  // then SM cycles: 6 waiting for K chunks, 7 waiting for V chunks, 8 in the
+  // score loop, 9 in the V loop.  Then 16*layers + {0 LM
   // inputs ready, 1 quantised, 2 lm_head rows done, 3 partials published,
   // 4 token known, 5 all partials read}.
   unsigned long long* trace = nullptr;

@@ -167,6 +167,15 @@ struct fa_session {
 
 // ------------------------------------------------------------ helpers ----
 
+// The session's device error word, read back after a decode call: nonzero
+// when a bounded wait of a kernel gave up.  Cleared, then reported as
+// FA_ERR_TIMEOUT.
+void check_error_word(fa_session* s, int code) {
+  if (code == 0) return;
+  FA_CUDA(cudaMemset(s->d_int(kErrWord), 0, 4));
+  throw Error(kErrTimeout, "a bounded device wait gave up (code " + std::to_string(code) + ")");
+}
+
 static void check_backend(fa_backend* b) {
   if (b == nullptr) throw Error(kErrArgument, "null backend");
   if (b->disposed) throw Error(kErrDisposed, "backend disposed");
@@ -1075,6 +1084,7 @@ void enqueue_layers(fa_session* s, int frames, const int* skip) {
       g.out = s->qkv.as<float>();
       g.out_stride = qw + 2 * kvw;
       g.skip = skip;
+      g.err = s->d_int(kErrWord);
       launch_gemv_f32(g, st);
     }
     AttnArgs a = attn_args(s, l, frames, skip);
@@ -1122,6 +1132,7 @@ void enqueue_layers(fa_session* s, int frames, const int* skip) {
       g.res = s->x.as<float>();
       g.out_stride = W;
       g.skip = skip;
+      g.err = s->d_int(kErrWord);
       launch_gemv_f32(g, st);
       F32GemvArgs u;
       u.x = s->a.as<float>();
@@ -1132,6 +1143,7 @@ void enqueue_layers(fa_session* s, int frames, const int* skip) {
       u.out = s->gu.as<float>();
       u.out_stride = 2 * m->ffn;
       u.skip = skip;
+      u.err = s->d_int(kErrWord);
       launch_gemv_f32(u, st);
       launch_silu_pair(s->gu.as<float>(), frames, m->ffn, s->act.as<float>(), skip, st);
       F32GemvArgs d;
@@ -1143,6 +1155,7 @@ void enqueue_layers(fa_session* s, int frames, const int* skip) {
       d.res = s->a.as<float>();
       d.out_stride = W;
       d.skip = skip;
+      d.err = s->d_int(kErrWord);
       launch_gemv_f32(d, st);
     }
     if (l == 0 && s->debug) {
@@ -1193,6 +1206,7 @@ void enqueue_head(fa_session* s, const float* x_last, const int* skip) {
     g.out = s->logits.as<float>();
     g.out_stride = m->vocab;
     g.skip = skip;
+    g.err = s->d_int(kErrWord);
     launch_gemv_f32(g, s->stream);
     launch_greedy_dev(s->logits.as<float>(), m->vocab, s->d_int(1), skip, s->stream);
   }
@@ -1432,11 +1446,7 @@ static int session_decode_locked(fa_session* s, const float* emb, const int32_t*
   }
   FA_CUDA(cudaMemcpyAsync(s->pinned + 4, s->d_int(kErrWord), 4, cudaMemcpyDeviceToHost, s->stream));
   FA_CUDA(cudaStreamSynchronize(s->stream));
-  if (s->pinned[4] != 0) {
-    const int code = s->pinned[4];
-    FA_CUDA(cudaMemset(s->d_int(kErrWord), 0, 4));
-    throw Error(kErrTimeout, "tensor-core projection: a bounded wait gave up (code " + std::to_string(code) + ")");
-  }
+  check_error_word(s, s->pinned[4]);
   s->pos += frames;
   if (output_logits) {
     s->have_token = true;
@@ -1540,8 +1550,10 @@ int fa_session_step(fa_session* s, int32_t token, float* logits, int32_t* next) 
     FA_CUDA(cudaMemcpyAsync(s->d_int(1), s->pinned, 4, cudaMemcpyHostToDevice, s->stream));
     FA_CUDA(cudaGraphLaunch(s->step_graph, s->stream));
     FA_CUDA(cudaMemcpyAsync(s->pinned + 1, s->d_int(1), 4, cudaMemcpyDeviceToHost, s->stream));
+    FA_CUDA(cudaMemcpyAsync(s->pinned + 32, s->d_int(kErrWord), 4, cudaMemcpyDeviceToHost, s->stream));
     if (logits) FA_CUDA(cudaMemcpyAsync(logits, s->logits.p, (size_t)m->vocab * 4, cudaMemcpyDeviceToHost, s->stream));
     FA_CUDA(cudaStreamSynchronize(s->stream));
+    check_error_word(s, s->pinned[32]);
     s->pos += 1;
     s->have_token = true;
     if (next) *next = s->pinned[1];
@@ -1584,7 +1596,9 @@ int fa_session_generate(fa_session* s, int max_tokens, const int32_t* end_ids, i
     for (int i = 0; i < steps; ++i) FA_CUDA(cudaGraphLaunch(s->gen_graph, s->stream));
     FA_CUDA(cudaEventRecord(s->ev1, s->stream));
     FA_CUDA(cudaMemcpyAsync(s->pinned, s->d_int(0), 16, cudaMemcpyDeviceToHost, s->stream));
+    FA_CUDA(cudaMemcpyAsync(s->pinned + 32, s->d_int(kErrWord), 4, cudaMemcpyDeviceToHost, s->stream));
     FA_CUDA(cudaStreamSynchronize(s->stream));
+    check_error_word(s, s->pinned[32]);
     FA_CUDA(cudaEventElapsedTime(&s->last_ms, s->ev0, s->ev1));
     const int count = s->pinned[2], stopped = s->pinned[3], next = s->pinned[1];
     if (count > 0) FA_CUDA(cudaMemcpy(tokens, s->log.p, (size_t)count * 4, cudaMemcpyDeviceToHost));
