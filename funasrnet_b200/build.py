@@ -21,8 +21,11 @@ LIB = PKG / "libfunasr_cuda.so"
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 # -fmad=false: every a*b+c stays two roundings unless a kernel asks for an FMA
 # explicitly, matching the reference's RyuJIT evaluation.
+# Calls from device code into host-only functions (diagnostics 20011-20015)
+# are errors: nvcc only warns, and the device compiler then treats the calling
+# path as unreachable and drops it.
 NVCC_FLAGS = ARCH + ["-O3", "-lineinfo", "-std=c++17", "-fmad=false", "-Xcompiler", "-fPIC,-O3,-ffp-contract=off",
-                     "-Xptxas", "-v"]
+                     "-Xptxas", "-v", "-diag-error", "20011,20012,20013,20014,20015"]
 SOURCES = ["decoder_kernels.cu", "mega.cu", "batch.cu", "f32_stream.cu", "runtime.cu", "host_util.cpp"]
 
 

@@ -69,8 +69,9 @@ constexpr unsigned kWaitLimit = 1u << 22;
 static_assert(ASLOTS * CSLOT <= WSLOTS * WSLOT, "the attention ring shares the weight ring's memory");
 static_assert(2 * WSLOTS <= 16 && 16 + 2 * ASLOTS <= 48, "disjoint mbarrier ranges");
 
+
 enum { kTagQkv = 1, kTagAttn = 2, kTagA = 3, kTagAct = 4, kTagX = 5, kTagPart = 6 };
-enum { kErrWaitData = 1, kErrWaitFull = 2, kErrWaitEmpty = 3, kErrWaitGo = 4, kErrWaitDrain = 5 };
+enum { kErrWaitData = 1, kErrWaitFull = 2, kErrWaitEmpty = 3, kErrWaitGo = 4, kErrWaitDrain = 5, kErrWaitWindow = 6 };
 
 struct Spans {
   int q0, qn, o0, on, gb0, gbn, d0, dn, lm0, lmn;
@@ -93,7 +94,7 @@ struct Shared {
 // Shared memory: fixed-size regions at compile-time offsets (addresses fold
 // into the instructions instead of occupying registers), then the score row
 // of `capacity` floats.
-constexpr int align_up(int o, int a) { return (o + a - 1) / a * a; }
+__host__ __device__ constexpr int align_up(int o, int a) { return (o + a - 1) / a * a; }
 constexpr int kOffRing = 0;                                        // weight ring / K and V rings
 constexpr int kOffBars = align_up(kOffRing + WSLOTS * WSLOT, 8);   // 48 mbarriers
 constexpr int kOffAttQ = kOffBars + 48 * 8;
@@ -210,8 +211,11 @@ __device__ __forceinline__ unsigned long long global_ns() {
   return t;
 }
 
-__device__ __forceinline__ void raise_error(Shared* sh, MegaCtrl* ctrl, int code) {
-  atomicCAS(&ctrl->error, 0, code);
+// Records the first wait that gave up (its code, and the CTA and warp in
+// `where` as cta * 32 + warp) and makes this CTA abort.  Out of line: the
+// wait loops that call it stay within their registers.
+__device__ __noinline__ void raise_error(Shared* sh, MegaCtrl* ctrl, int code) {
+  if (atomicCAS(&ctrl->error, 0, code) == 0) ctrl->where = (int)blockIdx.x * 32 + (int)(threadIdx.x >> 5);
   sh->abort = 1;
 }
 
@@ -374,7 +378,7 @@ __device__ bool wait_window(Shared* sh, MegaCtrl* ctrl, int w) {
     if (sh->window > w) return true;
     __nanosleep(64);
     if (it > kWaitLimit) {
-      raise_error(sh, ctrl, kErrWaitGo);
+      raise_error(sh, ctrl, kErrWaitWindow);
       return false;
     }
   }
@@ -760,24 +764,6 @@ __device__ __forceinline__ void head_rope(Ctx& c, float* v, float co, float si, 
   v[i] = o;
 }
 
-// Products p_t * v_t of 12 consecutive positions of one channel (weights
-// 16-byte aligned, the channel's column at stride D halves), and their
-// ordered sum into acc.
-__device__ __forceinline__ void vprod12(const __half* vv, const float* pr, int t, float (&x)[12]) {
-#pragma unroll
-  for (int q = 0; q < 3; ++q) {
-    const float4 p = *reinterpret_cast<const float4*>(pr + t + 4 * q);
-    x[4 * q + 0] = __fmul_rn(__half2float(vv[(t + 4 * q + 0) * D]), p.x);
-    x[4 * q + 1] = __fmul_rn(__half2float(vv[(t + 4 * q + 1) * D]), p.y);
-    x[4 * q + 2] = __fmul_rn(__half2float(vv[(t + 4 * q + 2) * D]), p.z);
-    x[4 * q + 3] = __fmul_rn(__half2float(vv[(t + 4 * q + 3) * D]), p.w);
-  }
-}
-__device__ __forceinline__ void add12(float& acc, const float (&x)[12]) {
-#pragma unroll
-  for (int u = 0; u < 12; ++u) acc = __fadd_rn(acc, x[u]);
-}
-
 // Exact paired-GQA attention of query head h = blockIdx.x at position pos
 // (TensorMath.DecoderAttention.cs:17-52 in the order of TensorMath.AttentionAvx.cs
 // and TensorMath.SoftmaxAvx.cs), K/V history from the chunk rings.
@@ -892,26 +878,41 @@ __device__ __noinline__ int attention(Ctx c, int layer, int pos, unsigned tag_in
   for (int w = 1; w < CWARPS; ++w) mx = fmaxf(mx, redf[w]);
   for (int t = c.tid; t < len; t += CTHREADS) c.sc()[t] = exp_ref(__fsub_rn(c.sc()[t], mx));
   csync();
-  const int full = len & ~7;
-  if (c.tid < 8) {
+  if (c.warp == 0) {
+    // Lane j < 8 sums e_j, e_{j+8}, ... in order in double (eight loads ahead
+    // of the dependent adds); the lanes fold as Vector256<double>.Sum(low +
+    // high): s_j = a_j + a_{j+4}, then (s0 + s2) + (s1 + s3); the len % 8 tail
+    // follows in order.
+    const int full = len & ~7;
     double acc = 0.0;
-    for (int t = c.tid; t < full; t += 8) acc = __dadd_rn(acc, (double)c.sc()[t]);
-    c.red()[48 + c.tid] = acc;
-  }
-  csync();
-  if (c.tid == 0) {
-    const double s0 = __dadd_rn(c.red()[48], c.red()[52]), s1 = __dadd_rn(c.red()[49], c.red()[53]);
-    const double s2 = __dadd_rn(c.red()[50], c.red()[54]), s3 = __dadd_rn(c.red()[51], c.red()[55]);
-    double sum = __dadd_rn(__dadd_rn(s0, s2), __dadd_rn(s1, s3));
-    for (int t = full; t < len; ++t) sum = __dadd_rn(sum, (double)c.sc()[t]);
-    redf[31] = __double2float_rn(__ddiv_rn(1.0, sum));
+    if (c.lane < 8) {
+      int t = c.lane;
+      for (; t + 56 < full; t += 64) {
+        float v[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) v[u] = c.sc()[t + 8 * u];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) acc = __dadd_rn(acc, (double)v[u]);
+      }
+      for (; t < full; t += 8) acc = __dadd_rn(acc, (double)c.sc()[t]);
+    }
+    acc = __dadd_rn(acc, __shfl_down_sync(0xffffffffu, acc, 4));
+    acc = __dadd_rn(acc, __shfl_down_sync(0xffffffffu, acc, 2));
+    acc = __dadd_rn(acc, __shfl_down_sync(0xffffffffu, acc, 1));
+    if (c.lane == 0) {
+      for (int t = full; t < len; ++t) acc = __dadd_rn(acc, (double)c.sc()[t]);
+      redf[31] = __double2float_rn(__ddiv_rn(1.0, acc));
+    }
   }
   csync();
   const float inv = redf[31];
   for (int t = c.tid; t < len; t += CTHREADS) c.sc()[t] = __fmul_rn(c.sc()[t], inv);
   csync();
   if (c.trace && c.tid == 0) c.trace[kTraceLayerEvents * layer + 4] = global_ns();
-  // V sum per channel in position order (TensorMath.AttentionAvx.cs:188-213): warps 0..3.
+  // V sum per channel in position order (TensorMath.AttentionAvx.cs:188-213):
+  // warps 0..3, thread = channel.  A full chunk runs as five groups of 12
+  // positions, each group's V values and weights loaded into registers while
+  // the previous group's products and dependent adds run.
   if (c.warp < 4) {
     float acc = 0.0f;
     long long vwait = 0;
@@ -925,19 +926,27 @@ __device__ __noinline__ int attention(Ctx c, int layer, int pos, unsigned tag_in
       const float* pr = c.sc() + ch * CHUNK;
       const int n = min(CHUNK, pos - ch * CHUNK);
       if (n == CHUNK) {
-        // Five groups of 12: a group's products form while the previous
-        // group's dependent adds run.
-        float x[12], y[12];
-        vprod12(vv, pr, 0, x);
-        vprod12(vv, pr, 12, y);
-        add12(acc, x);
-        vprod12(vv, pr, 24, x);
-        add12(acc, y);
-        vprod12(vv, pr, 36, y);
-        add12(acc, x);
-        vprod12(vv, pr, 48, x);
-        add12(acc, y);
-        add12(acc, x);
+        __half hv[2][12];
+        float4 pv[2][3];
+        auto load = [&](int grp, int k) {
+#pragma unroll
+          for (int u = 0; u < 12; ++u) hv[k][u] = vv[(grp * 12 + u) * D];
+#pragma unroll
+          for (int q = 0; q < 3; ++q) pv[k][q] = *reinterpret_cast<const float4*>(pr + grp * 12 + 4 * q);
+        };
+        load(0, 0);
+#pragma unroll
+        for (int grp = 0; grp < CHUNK / 12; ++grp) {
+          const int k = grp & 1;
+          if (grp + 1 < CHUNK / 12) load(grp + 1, k ^ 1);
+#pragma unroll
+          for (int q = 0; q < 3; ++q) {
+            acc = __fadd_rn(acc, __fmul_rn(__half2float(hv[k][4 * q + 0]), pv[k][q].x));
+            acc = __fadd_rn(acc, __fmul_rn(__half2float(hv[k][4 * q + 1]), pv[k][q].y));
+            acc = __fadd_rn(acc, __fmul_rn(__half2float(hv[k][4 * q + 2]), pv[k][q].z));
+            acc = __fadd_rn(acc, __fmul_rn(__half2float(hv[k][4 * q + 3]), pv[k][q].w));
+          }
+        }
       } else {
         for (int t = 0; t < n; ++t) acc = __fadd_rn(acc, __fmul_rn(__half2float(vv[t * D]), pr[t]));
       }
@@ -978,6 +987,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(const Mega
       mbar_init(&ar.full[i], 1);
       mbar_init(&ar.empty[i], CWARPS);
     }
+
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     sh->quit = sh->go = sh->window = sh->prod_exit = sh->abort = 0;
     sh->issued[0] = sh->issued[1] = 0;

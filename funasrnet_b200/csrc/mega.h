@@ -28,7 +28,7 @@ struct MegaCtrl {
   unsigned epoch;   // tag base: advances by tags_per_step * steps (never 0)
   int error;        // nonzero: a bounded wait gave up (code names the wait)
   int log_count;    // tokens appended to the log by the last launch
-  int pad;
+  int where;        // with error: cta * 32 + warp of the wait that gave up first
 };
 
 struct MegaArgs {

@@ -1528,7 +1528,9 @@ static MegaCtrl run_mega(fa_session* s, int steps, int record, int n_end, int ho
   std::memcpy(&c, s->pinned + 16, sizeof(c));
   s->mega_epoch = c.epoch;
   if (c.error != 0)
-    throw Error(kErrTimeout, "persistent decode kernel: a bounded wait gave up (code " + std::to_string(c.error) + ")");
+    throw Error(kErrTimeout, "persistent decode kernel: a bounded wait gave up (code " + std::to_string(c.error) +
+                                 ", CTA " + std::to_string(c.where / 32) + " warp " + std::to_string(c.where % 32) +
+                                 ")");
   s->pos = c.pos;
   return c;
 }
