@@ -86,6 +86,7 @@ struct Shared {
   volatile int issued[2];   // copies issued per ring (weights / attention)
   volatile int prod_exit;   // producer left its loop
   volatile int abort;       // a wait failed somewhere: drain and return
+  unsigned wait_limit;      // polls before a wait gives up (the launch's, else kWaitLimit)
   int token;
   float best_v[32];
   int best_i[32];
@@ -235,7 +236,7 @@ __device__ bool wait_word(const unsigned long long* p, unsigned tag, float& out,
         sh->abort = 1;
         return false;
       }
-      if (it > kWaitLimit) {
+      if (it > sh->wait_limit) {
         raise_error(sh, ctrl, kErrWaitData);
         return false;
       }
@@ -289,7 +290,7 @@ __device__ bool ring_issue(const Ring& r, int& n, const void* src, unsigned byte
       if (mbar_try_wait(&r.empty[slot], parity)) break;
       if ((it & 63) == 63) {
         if (sh->abort || sh->quit) return false;
-        if (it > kWaitLimit) {
+        if (it > sh->wait_limit) {
           raise_error(sh, ctrl, kErrWaitEmpty);
           return false;
         }
@@ -318,7 +319,7 @@ __device__ const uint8_t* ring_acquire(const Ring& r, int n, Shared* sh, MegaCtr
     }
     if ((it & 63) == 63) {
       if (sh->abort) break;
-      if (it > kWaitLimit) {
+      if (it > sh->wait_limit) {
         raise_error(sh, ctrl, kErrWaitFull);
         break;
       }
@@ -350,7 +351,7 @@ __device__ void ring_drain(const Ring& r, int consumed, int issued, Shared* sh, 
     const int slot = n % r.nslot;
     const unsigned parity = (unsigned)((n / r.nslot) & 1);
     for (unsigned it = 0; !mbar_try_wait(&r.full[slot], parity); ++it)
-      if (it > kWaitLimit) {
+      if (it > sh->wait_limit) {
         raise_error(sh, ctrl, kErrWaitDrain);
         return;
       }
@@ -364,7 +365,7 @@ __device__ bool wait_go(Shared* sh, MegaCtrl* ctrl, int step) {
     if (sh->quit || sh->abort) return false;
     if (sh->go > step) return true;
     __nanosleep(64);
-    if (it > kWaitLimit) {
+    if (it > sh->wait_limit) {
       raise_error(sh, ctrl, kErrWaitGo);
       return false;
     }
@@ -377,7 +378,7 @@ __device__ bool wait_window(Shared* sh, MegaCtrl* ctrl, int w) {
     if (sh->quit || sh->abort) return false;
     if (sh->window > w) return true;
     __nanosleep(64);
-    if (it > kWaitLimit) {
+    if (it > sh->wait_limit) {
       raise_error(sh, ctrl, kErrWaitWindow);
       return false;
     }
@@ -560,7 +561,7 @@ __device__ __forceinline__ bool w8a8_phase(Ctx& c, int nt, int per, Epi epi) {
   // Every warp takes the same branch: the jobs below wait on each other at
   // named barriers, which have no time limit.  (On failure the drain waits
   // for the copies in flight.)
-  if (csync_or(failed)) return false;
+  if (csync_or(failed || c.sh()->abort)) return false;
   for (int j = c.warp; j < nt * NS; j += CWARPS) {  // warp-uniform
     const int t = j / NS, s = j - t * NS, piece = t / per;
     const uint8_t* tile = ring_w().base + (size_t)((c.nw + piece) % WSLOTS) * WSLOT + (size_t)(t - piece * per) * TB;
@@ -619,7 +620,7 @@ __device__ __forceinline__ void gather_q8(Ctx& c, const unsigned long long* src,
         c.sh()->abort = 1;
         break;
       }
-      if (it > kWaitLimit) {
+      if (it > c.sh()->wait_limit) {
         raise_error(c.sh(), c.A->ctrl, kErrWaitData);
         break;
       }
@@ -674,7 +675,7 @@ __device__ __forceinline__ void gather(Ctx& c, const unsigned long long* src, in
         c.sh()->abort = 1;
         break;
       }
-      if (it > kWaitLimit) {
+      if (it > c.sh()->wait_limit) {
         raise_error(c.sh(), c.A->ctrl, kErrWaitData);
         break;
       }
@@ -783,9 +784,11 @@ __device__ __noinline__ int attention(Ctx c, int layer, int pos, unsigned tag_in
     if (!wait_word(A.qkv_t + src, tag_in, v, c.sh(), A.ctrl)) break;
     (i < D ? c.aq() : (i < 2 * D ? c.ak() : c.av()))[i % D] = v;
   }
+  // No early return after an abort: every later wait gives up at once and the
+  // work runs on with discarded data, so that all compute warps keep meeting
+  // the same barriers; the caller decides, on a barrier reduction.
   csync();
   if (c.trace && c.tid == 0) c.trace[kTraceLayerEvents * layer + 1] = global_ns();
-  if (c.sh()->abort) return c.na;
   if (c.warp < 4) {  // q: RMSNorm + RoPE (QwenDecoder.cs:188,193)
     head_norm(c, c.aq(), gn, A.eps, 0, 2);
     head_rope(c, c.aq(), co, si, 0, 2);
@@ -814,13 +817,17 @@ __device__ __noinline__ int attention(Ctx c, int layer, int pos, unsigned tag_in
   for (int i = 0; i < D / 8; ++i) qj[i] = c.aq()[j + 8 * i];
   const int chunks = (pos + CHUNK - 1) / CHUNK;
   const bool timed = c.trace != nullptr;  // wait and loop cycles for the trace
+  bool failed = false;
   long long kwait = 0;
   const long long s0 = timed ? clock64() : 0;
   for (int ch = 0; ch < chunks; ++ch) {
     const long long k0 = timed ? clock64() : 0;
-    const uint8_t* kb = ring_acquire(ring_a(), c.na, c.sh(), A.ctrl);
+    const uint8_t* kb = failed ? nullptr : ring_acquire(ring_a(), c.na, c.sh(), A.ctrl);
     if (timed) kwait += clock64() - k0;
-    if (kb == nullptr) return c.na;
+    if (kb == nullptr) {  // abort: stop consuming; all warps leave together below
+      failed = true;
+      continue;
+    }
     const int t = ch * CHUNK + slot;
     float acc = 0.0f;
     if (t < pos) {
@@ -990,6 +997,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(const Mega
 
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     sh->quit = sh->go = sh->window = sh->prod_exit = sh->abort = 0;
+    sh->wait_limit = A.wait_limit != 0 ? A.wait_limit : kWaitLimit;
     sh->issued[0] = sh->issued[1] = 0;
   }
   __syncthreads();
@@ -1080,9 +1088,9 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(const Mega
       if (att) {
         MEGA_TRACE(ev + 0);
         c.na = attention(c, layer, pos, tl + kTagQkv, tl + kTagAttn, rope_co, rope_si);
-        csync();
+        const bool ab = csync_or(sh->abort);
         MEGA_TRACE(ev + 5);
-        if (sh->abort) goto drain;
+        if (ab) goto drain;
         continue;
       }
       // ---- Q: x -> RMSNorm -> quantise -> q/k/v rows ----
@@ -1097,13 +1105,16 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(const Mega
         MEGA_TRACE(ev + 0);
         norm_quant(c, v, load_gamma(c, s_attn), A.eps, layer > 0 ? c.xres() : nullptr);
       }
-      if (sh->abort) goto drain;
       MEGA_TRACE(ev + 1);
       {
         const unsigned tag = tl + kTagQkv;
         const int q0 = sp.q0;
         c.wait_ev = ev + 2;
-        if (!w8a8_phase<W>(c, sp.qn, 3, [&](int t, int r, float v) { st_word(A.qkv_t + (q0 + t) * 8 + r, pack(v, tag)); }))
+        // Failure-path test hook: the named CTA leaves its first q/k/v rows unpublished.
+        const bool hold = A.withhold == (int)blockIdx.x && step == 0 && layer == 0;
+        if (!w8a8_phase<W>(c, sp.qn, 3, [&](int t, int r, float v) {
+              if (!hold) st_word(A.qkv_t + (q0 + t) * 8 + r, pack(v, tag));
+            }))
           goto drain;
       }
       MEGA_TRACE(ev + 3);
@@ -1119,7 +1130,6 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(const Mega
       // ---- O: quantised attention output -> o + x ----
       if (sp.on > 0) {
         gather_q8<400>(c, A.attn_t, QW, tl + kTagAttn);
-        if (sh->abort) goto drain;
         MEGA_TRACE(ev + 4);
         const unsigned tag = tl + kTagA;
         const int o0 = sp.o0;
@@ -1145,7 +1155,6 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(const Mega
           csync();
         }
       }
-      if (sh->abort) goto drain;
       MEGA_TRACE(ev + 9);
       for (int bj = 0; bj < sp.gbn; ++bj) {
         c.wait_ev = bj == 0 ? ev + 10 : -1;
@@ -1160,7 +1169,6 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(const Mega
       // ---- D: quantised act -> down + a ----
       if (sp.dn > 0) {
         gather_q8<400>(c, A.act_t, FFN, tl + kTagAct);
-        if (sh->abort) goto drain;
         MEGA_TRACE(ev + 12);
         const unsigned tag = tl + kTagX;
         const int d0 = sp.d0;
@@ -1187,7 +1195,6 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(const Mega
           MEGA_TRACE(ev + 0);
           norm_quant(c, v, load_gamma(c, s_out), A.eps, nullptr);
         }
-        if (sh->abort) goto drain;
         MEGA_TRACE(ev + 1);
         // Rounds of 15 tiles (5 ring pieces of 3 tiles), one tile per warp,
         // closed by a barrier: the pieces in use at any time are those of one
@@ -1220,7 +1227,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(const Mega
               }
             }
           }
-          if (csync_or(failed)) goto drain;
+          if (csync_or(failed || sh->abort)) goto drain;
         }
         c.nw += (sp.lmn + 2) / 3;
         MEGA_TRACE(ev + 2);
@@ -1293,8 +1300,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(const Mega
         sh->best_v[warp] = pv;
         sh->best_i[warp] = force0 ? -2 : pi;
       }
-      csync();
-      if (sh->abort) goto drain;
+      if (csync_or(sh->abort)) goto drain;
       if (tid == 0) {
         float bv = sh->best_v[0];
         int bi = sh->best_i[0];
@@ -1322,7 +1328,7 @@ drain:
   if (tid == 0) {
     for (unsigned it = 0; !sh->prod_exit; ++it) {
       __nanosleep(64);
-      if (it > kWaitLimit) {
+      if (it > sh->wait_limit) {
         raise_error(sh, ctrl, kErrWaitDrain);
         break;
       }

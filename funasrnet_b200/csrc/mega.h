@@ -74,6 +74,11 @@ struct MegaArgs {
   // inputs ready, 1 quantised, 2 lm_head rows done, 3 partials published,
   // 4 token known, 5 all partials read}.
   unsigned long long* trace = nullptr;
+  // Failure-path test hooks (fa_session_set_fault_test): polls before any
+  // bounded wait gives up (0: the default), and a GEMV CTA that leaves its
+  // first step's layer-0 q/k/v rows unpublished (-1: none).
+  unsigned wait_limit = 0;
+  int withhold = -1;
 };
 constexpr int kTraceLayerEvents = 16;
 constexpr int kTraceEvents = kTraceLayerEvents * 28 + 8;

@@ -159,6 +159,8 @@ struct fa_session {
   int mega_grid = 0;
   DevBuf mx, mqkv, mattn, ma, mact, mpv, mpi, mctrl;
   unsigned mega_epoch = 1;  // the control block's tag base, as the last launch left it
+  unsigned test_wait_limit = 0;  // failure-path test hooks for the next persistent launch
+  int test_withhold = -1;
   bool trace = false;
   DevBuf trace_buf;                          // [grid x kTraceEvents] phase timestamps
   DevBuf bxq, bxs, bxq2, bxs2;               // frame-tile operands of tensor-core prefill projections
@@ -1497,6 +1499,10 @@ static MegaCtrl run_mega(fa_session* s, int steps, int record, int n_end, int ho
   a.n_end = n_end;
   a.log = s->log.as<int>();
   a.log_cap = s->log_cap;
+  a.wait_limit = s->test_wait_limit;
+  a.withhold = s->test_withhold;
+  s->test_wait_limit = 0;  // the hooks hold for one launch
+  s->test_withhold = -1;
   if (s->trace) {
     const size_t bytes = (size_t)s->mega_grid * kTraceEvents * 8;
     s->trace_buf.ensure(bytes);
@@ -1526,7 +1532,9 @@ static MegaCtrl run_mega(fa_session* s, int steps, int record, int n_end, int ho
   if (timed) FA_CUDA(cudaEventElapsedTime(&s->last_ms, s->ev0, s->ev1));
   MegaCtrl c;
   std::memcpy(&c, s->pinned + 16, sizeof(c));
-  s->mega_epoch = c.epoch;
+  // After a failed launch its exchange words may carry any tag of its steps:
+  // the next launch starts past all of them.
+  s->mega_epoch = c.error != 0 ? in.epoch + (unsigned)steps * (unsigned)((m->layers + 1) * 8) : c.epoch;
   if (c.error != 0)
     throw Error(kErrTimeout, "persistent decode kernel: a bounded wait gave up (code " + std::to_string(c.error) +
                                  ", CTA " + std::to_string(c.where / 32) + " warp " + std::to_string(c.where % 32) +
@@ -1682,6 +1690,16 @@ int fa_session_kernels_per_step(const fa_session* s) {
 
 int fa_session_uses_persistent_kernel(const fa_session* s) {
   return s ? ((s->use_mega && s->exact_attention) ? s->mega_grid : 0) : -1;
+}
+
+int fa_session_set_fault_test(fa_session* s, uint32_t wait_limit, int withhold_cta) {
+  return with_session(s, [&] {
+    if (withhold_cta >= 0 && (s->mega_grid <= 0 || withhold_cta < 16 || withhold_cta >= s->mega_grid))
+      throw Error(kErrArgument, "withhold_cta must name a GEMV CTA of the persistent kernel");
+    s->test_wait_limit = wait_limit;
+    s->test_withhold = withhold_cta;
+    return (int)kHandled;
+  });
 }
 
 int fa_session_set_trace(fa_session* s, int on) {

@@ -133,6 +133,12 @@ class QwenDecoder:
     def set_persistent(self, on: bool = True) -> bool:
         return check(lib().fa_session_set_persistent_kernel(self._h, 1 if on else 0)) == FA_OK
 
+    def set_fault_test(self, wait_limit: int = 0, withhold_cta: int = -1) -> None:
+        """Failure-path test hook for the next persistent-kernel launch only: a
+        shorter bounded-wait limit (polls) and a GEMV CTA whose first q/k/v rows
+        stay unpublished, so that the waits give up (FA_ERR_TIMEOUT)."""
+        check(lib().fa_session_set_fault_test(self._h, int(wait_limit), int(withhold_cta)))
+
     def trace_phases(self, on: bool = True) -> None:
         check(lib().fa_session_set_trace(self._h, 1 if on else 0))
 

@@ -205,6 +205,15 @@ int fa_session_set_persistent_kernel(fa_session* session, int on);
  * layers: {0 lm_head inputs ready, 1 quantised, 2 rows done, 3 partials
  * published, 4 token known, 5 all partials read}. */
 int fa_session_set_trace(fa_session* session, int on);
+/* Test hook of the failure path (the reference's worker-team recovery checks,
+ * tests/FunAsrNet.Checks/Program.cs:625-645, are its analogue): for the next
+ * persistent-kernel launch only, wait_limit > 0 replaces the number of polls
+ * after which a bounded device wait gives up, and withhold_cta >= 0 (a GEMV
+ * CTA, 16 <= cta < grid) leaves that CTA's layer-0 q/k/v rows of the first
+ * step unpublished, so that the waits on them run out.  The launch then ends
+ * with FA_ERR_TIMEOUT; nothing faults, and the session stays usable (its
+ * position is unchanged; reset or decode again). */
+int fa_session_set_fault_test(fa_session* session, uint32_t wait_limit, int withhold_cta);
 int fa_session_get_trace(fa_session* session, uint64_t* out, int capacity);
 /* Number of kernel launches one generate iteration replays (kernel nodes of
  * its CUDA graph); 0 before the first fa_session_generate. */

@@ -113,3 +113,52 @@ def test_reset_and_reuse(small):
             d.decode(emb, frames, want_logits=False)
             runs.append(d.generate(12, end_ids=()))
         assert runs[0] == runs[1] == runs[2]
+
+
+def test_bounded_wait_gives_up_and_session_recovers(small):
+    """The failure path of the persistent kernel's bounded waits, without a GPU
+    fault: one GEMV CTA leaves its first q/k/v rows unpublished and the wait
+    limit is short, so the attention CTAs' waits run out.  The call returns
+    FA_ERR_TIMEOUT naming the wait, the kernel has returned (the context stays
+    usable), the session keeps its position, and the next calls on it give the
+    same tokens and bit-identical logits as a session that never failed."""
+    from funasrnet_b200._lib import FaError
+    from funasrnet_b200.decoder import QwenDecoder
+
+    cm, om = small
+    emb, frames = prefix_embeddings(om, 30, 8, seed=61)
+    with QwenDecoder(cm) as d, QwenDecoder(cm) as ref:
+        grid = d.persistent_grid()
+        d.decode(emb, frames, want_logits=False)
+        ref.decode(emb, frames, want_logits=False)
+        d.set_fault_test(wait_limit=100000, withhold_cta=grid - 1)
+        with pytest.raises(FaError) as err:
+            d.generate(3, end_ids=())
+        assert err.value.code == -6  # FA_ERR_TIMEOUT
+        assert "bounded wait gave up" in str(err.value)
+        assert d.position == frames
+        # the hooks held for one launch: the same session decodes normally again
+        assert d.generate(6, end_ids=()) == ref.generate(6, end_ids=())
+        assert d.position == ref.position
+        nxt, lg = d.step(7, want_logits=True)
+        nref, lref = ref.step(7, want_logits=True)
+        assert nxt == nref
+        assert_bits_equal(lg, lref, "after recovery")
+        # and after a reset it matches a fresh decode bit for bit
+        d.reset()
+        ref.reset()
+        la, _ = d.decode(emb, frames)
+        lb, _ = ref.decode(emb, frames)
+        assert_bits_equal(la, lb, "fresh decode after the failure")
+
+
+def test_fault_test_hook_rejects_attention_ctas(small):
+    from funasrnet_b200._lib import FaError
+    from funasrnet_b200.decoder import QwenDecoder
+
+    cm, _ = small
+    with QwenDecoder(cm) as d:
+        with pytest.raises(FaError):
+            d.set_fault_test(withhold_cta=3)
+        with pytest.raises(FaError):
+            d.set_fault_test(withhold_cta=d.persistent_grid())
