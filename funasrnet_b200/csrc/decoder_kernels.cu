@@ -356,7 +356,7 @@ __global__ void qk_rope_kv_kernel(const AttnArgs a) {
   const int f = blockIdx.x, h = blockIdx.y;
   const int qw = a.heads * D, kvw = a.kv_heads * D;
   const int stride = a.qkv_stride ? a.qkv_stride : qw + 2 * kvw;
-  const int p = *a.pos + f;
+  const int p = *a.pos + a.pos_offset + f;
   float* base = a.qkv + (size_t)f * stride;
   if (h < a.heads + a.kv_heads) {
     const bool isq = h < a.heads;
@@ -396,7 +396,7 @@ __global__ void __launch_bounds__(128) attn_partial_kernel(const AttnArgs a) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int qw = a.heads * D, kvw = a.kv_heads * D;
   const int stride = a.qkv_stride ? a.qkv_stride : qw + 2 * kvw;
-  const int len = *a.pos + f + 1;  // causal: frame f sees [0, pos + f]
+  const int len = *a.pos + a.pos_offset + f + 1;  // causal: frame f sees [0, pos + f]
   const int chunk = (len + a.splits - 1) / a.splits;
   const int t0 = s * chunk, t1 = min(len, t0 + chunk);
   const float* q = a.qkv + (size_t)f * stride + (size_t)(2 * g) * D;
@@ -519,7 +519,7 @@ __global__ void __launch_bounds__(256) attn_scores_kernel(const AttnArgs a) {
     q0[i] = qs[0][j + 8 * i];
     q1[i] = qs[1][j + 8 * i];
   }
-  const int len = *a.pos + f + 1;
+  const int len = *a.pos + a.pos_offset + f + 1;
   const int chunk = (len + a.splits - 1) / a.splits;
   const int t0 = s * chunk, t1 = min(len, t0 + chunk);
   const float divisor = __fsqrt_rn((float)D);
@@ -570,7 +570,7 @@ __global__ void __launch_bounds__(128) attn_softmax_v_kernel(const AttnArgs a) {
   __shared__ double lanes[8];
   __shared__ float s_inv;
   const int f = blockIdx.x, h = blockIdx.y, g = h >> 1, c = threadIdx.x;
-  const int len = *a.pos + f + 1;
+  const int len = *a.pos + a.pos_offset + f + 1;
   const float* sc = a.scores + ((size_t)f * a.heads + h) * a.capacity;
   float mx = -INFINITY;
   for (int t = c; t < len; t += D) {

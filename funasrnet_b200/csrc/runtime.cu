@@ -26,10 +26,11 @@ using namespace fa;
 
 namespace {
 
-constexpr int kMaxChunkFrames = 64;   // prefill frames per kernel sequence
+constexpr int kMaxChunkFrames = 256;  // prefill frames per layer sequence (one weight pass each)
+constexpr int kAttnChunkFrames = 64;  // frames per attention launch (its scores / partials buffers)
 constexpr int kAttnSplits = 16;       // split-K CTAs per (frame, KV head)
 constexpr int kBmmMinFrames = 16;     // frames from which projections run on the tensor cores
-constexpr int kSessionInts = 128;     // device words of a session (tokens staged at 16..79)
+constexpr int kSessionInts = 128;     // device words of a session
 constexpr int kErrWord = 100;         // session int word: error code of the batched kernels
 
 struct DevBuf {
@@ -140,6 +141,7 @@ struct fa_session {
   bool have_token = false; // a device argmax exists (a Decode with logits ran)
   DevBuf k_cache, v_cache;  // [layers][kv_heads][capacity][head] f16 (K rows lane-permuted)
   DevBuf x, a, qkv, attn, act, gu, part, logits, am_val, am_idx, ints, end_ids, log;
+  DevBuf tokens;  // prefix token ids of one prefill chunk [kMaxChunkFrames]
   // ints: 0 pos, 1 token, 2 step, 3 stopped, 4 row0_nan, 5 counter, 6 scratch token
   int log_cap = 0;
   int n_end_graph = -1;
@@ -1026,6 +1028,23 @@ AttnArgs attn_args(fa_session* s, int layer, int frames, const int* skip) {
   return a;
 }
 
+// QK-norm + RoPE + KV write and attention of `frames` frames of layer l, in
+// launches of at most kAttnChunkFrames frames (the scores and partials buffers
+// hold that many); each launch's frames follow the previous launch's in the
+// KV cache, so the causal order is kept.
+void enqueue_attention(fa_session* s, int l, int frames, const int* skip) {
+  fa_model* m = s->m;
+  const int qw = m->heads * m->head_size, kvw = m->kv_heads * m->head_size;
+  for (int f0 = 0; f0 < frames; f0 += kAttnChunkFrames) {
+    AttnArgs a = attn_args(s, l, std::min(kAttnChunkFrames, frames - f0), skip);
+    a.qkv += (size_t)f0 * (qw + 2 * kvw);
+    a.attn += (size_t)f0 * qw;
+    a.pos_offset = f0;
+    launch_qk_rope_kv(a, s->stream);
+    launch_attention(a, s->stream);
+  }
+}
+
 // The four projections of one layer for a prefill chunk of >= kBmmMinFrames
 // frames on the tensor cores; attention between them as in enqueue_layers.
 void enqueue_layer_bmm(fa_session* s, int l, int frames) {
@@ -1038,9 +1057,7 @@ void enqueue_layer_bmm(fa_session* s, int l, int frames) {
   int* err = s->d_int(kErrWord);
   enqueue_bmm(st, L.qkv, s->x.as<float>(), W, frames, L.attn_norm, m->eps, xq, xs, kEpiStore, s->qkv.as<float>(),
               qw + 2 * kvw, nullptr, nullptr, err);
-  AttnArgs a = attn_args(s, l, frames, nullptr);
-  launch_qk_rope_kv(a, st);
-  launch_attention(a, st);
+  enqueue_attention(s, l, frames, nullptr);
   enqueue_bmm(st, L.o, s->attn.as<float>(), qw, frames, nullptr, m->eps, xq, xs, kEpiResidual, s->a.as<float>(), W,
               s->x.as<float>(), nullptr, err);
   // SiLU(gate) * up quantised in the gate/up epilogue straight into the down
@@ -1089,9 +1106,7 @@ void enqueue_layers(fa_session* s, int frames, const int* skip) {
       g.err = s->d_int(kErrWord);
       launch_gemv_f32(g, st);
     }
-    AttnArgs a = attn_args(s, l, frames, skip);
-    launch_qk_rope_kv(a, st);
-    launch_attention(a, st);
+    enqueue_attention(s, l, frames, skip);
     if (m->quantized) {
       GemvArgs g;
       g.x = s->attn.as<float>();
@@ -1318,12 +1333,13 @@ int fa_session_create(fa_model* m, fa_session** out) {
     s->attn.ensure((size_t)F * qw * 4);
     s->act.ensure((size_t)F * m->ffn * 4);
     if (!m->quantized) s->gu.ensure((size_t)F * 2 * m->ffn * 4);
-    s->part.ensure((size_t)F * m->kv_heads * kAttnSplits * (4 + 2 * D) * 4);
-    s->scores.ensure((size_t)F * m->heads * m->capacity * 4);
+    s->part.ensure((size_t)kAttnChunkFrames * m->kv_heads * kAttnSplits * (4 + 2 * D) * 4);
+    s->scores.ensure((size_t)kAttnChunkFrames * m->heads * m->capacity * 4);
     s->logits.ensure((size_t)m->vocab * 4);
     const int lm_ctas = (m->vocab + kTileRows - 1) / kTileRows;
     s->am_val.ensure((size_t)lm_ctas * 4);
     s->am_idx.ensure((size_t)lm_ctas * 4);
+    s->tokens.ensure((size_t)F * 4);
     s->ints.ensure(kSessionInts * 4);
     FA_CUDA(cudaMemset(s->ints.p, 0, kSessionInts * 4));
     if (m->bmm_ok) {
@@ -1411,8 +1427,8 @@ int fa_session_embed(fa_session* s, const int32_t* tokens, int n, float* out) {
     const int W = s->m->width;
     for (int done = 0; done < n;) {
       const int c = std::min(kMaxChunkFrames, n - done);
-      FA_CUDA(cudaMemcpyAsync(s->d_int(16), tokens + done, (size_t)c * 4, cudaMemcpyHostToDevice, s->stream));
-      enqueue_embed(s, s->d_int(16), c, nullptr);
+      FA_CUDA(cudaMemcpyAsync(s->tokens.as<int>(), tokens + done, (size_t)c * 4, cudaMemcpyHostToDevice, s->stream));
+      enqueue_embed(s, s->tokens.as<int>(), c, nullptr);
       FA_CUDA(cudaMemcpyAsync(out + (size_t)done * W, s->x.p, (size_t)c * W * 4, cudaMemcpyDeviceToHost, s->stream));
       FA_CUDA(cudaStreamSynchronize(s->stream));
       done += c;
@@ -1432,8 +1448,8 @@ static int session_decode_locked(fa_session* s, const float* emb, const int32_t*
     if (emb) {
       FA_CUDA(cudaMemcpyAsync(s->x.p, emb + (size_t)done * W, (size_t)c * W * 4, cudaMemcpyHostToDevice, s->stream));
     } else {
-      FA_CUDA(cudaMemcpyAsync(s->d_int(16), tokens + done, (size_t)c * 4, cudaMemcpyHostToDevice, s->stream));
-      enqueue_embed(s, s->d_int(16), c, nullptr);
+      FA_CUDA(cudaMemcpyAsync(s->tokens.as<int>(), tokens + done, (size_t)c * 4, cudaMemcpyHostToDevice, s->stream));
+      enqueue_embed(s, s->tokens.as<int>(), c, nullptr);
     }
     enqueue_layers(s, c, nullptr);
     done += c;
