@@ -554,6 +554,52 @@ __global__ void __launch_bounds__(256) attn_scores_kernel(const AttnArgs a) {
   }
 }
 
+// The same scores for a prefill launch whose length bound the host knows:
+// grid (kv_heads, position blocks of 32, frame groups of 8), 256 threads
+// (8 per position).  A thread loads its lane's 16 K values of one position
+// once and forms the dots of all 8 frames x 2 query heads of its group with
+// them; each dot keeps the 8-lane order and fold of attn_scores_kernel.
+__global__ void __launch_bounds__(256) attn_scores_block_kernel(const AttnArgs a) {
+  constexpr int D = 128, M = D / 8, FG = 8;
+  __shared__ float qs[2 * FG][D];
+  const int g = blockIdx.x, t = blockIdx.y * 32 + (threadIdx.x >> 3), f0 = blockIdx.z * FG;
+  const int j = threadIdx.x & 7;
+  const int qw = a.heads * D, kvw = a.kv_heads * D;
+  const int stride = a.qkv_stride ? a.qkv_stride : qw + 2 * kvw;
+  const int nf = min(FG, a.frames - f0);
+  for (int i = threadIdx.x; i < 2 * FG * D; i += 256) {
+    const int p = i / D, c = i - p * D;
+    qs[p][c] = p < 2 * nf ? a.qkv[(size_t)(f0 + (p >> 1)) * stride + (size_t)(2 * g + (p & 1)) * D + c] : 0.0f;
+  }
+  __syncthreads();
+  const int base = *a.pos + a.pos_offset;  // frame f sees positions [0, base + f]
+  float k[M];
+  if (t < base + f0 + nf) {
+    const uint4* kr = reinterpret_cast<const uint4*>(a.k_cache + ((size_t)g * a.capacity + t) * D + j * M);
+    const uint4 ka = kr[0], kb = kr[1];
+    const __half* kh0 = reinterpret_cast<const __half*>(&ka);
+    const __half* kh1 = reinterpret_cast<const __half*>(&kb);
+#pragma unroll
+    for (int i = 0; i < M; ++i) k[i] = __half2float(i < 8 ? kh0[i] : kh1[i - 8]);
+  } else {
+#pragma unroll
+    for (int i = 0; i < M; ++i) k[i] = 0.0f;
+  }
+  const float divisor = __fsqrt_rn((float)D);
+  for (int p = 0; p < 2 * nf; ++p) {  // block-uniform: every lane takes part in the folds
+    const float* q = qs[p];
+    float acc = 0.0f;
+#pragma unroll
+    for (int i = 0; i < M; ++i) acc = __fadd_rn(acc, __fmul_rn(q[j + 8 * i], k[i]));
+    acc = __fadd_rn(acc, __shfl_down_sync(0xffffffffu, acc, 4));
+    acc = __fadd_rn(acc, __shfl_down_sync(0xffffffffu, acc, 1));
+    acc = __fadd_rn(acc, __shfl_down_sync(0xffffffffu, acc, 2));
+    const int f = f0 + (p >> 1);
+    if (j == 0 && t <= base + f)
+      a.scores[((size_t)f * a.heads + 2 * g + (p & 1)) * a.capacity + t] = __fdiv_rn(acc, divisor);
+  }
+}
+
 // Softmax + weighted V sum of one query head, in the reference's order
 // (TensorMath.SoftmaxAvx.cs:11-58, TensorMath.AttentionAvx.cs:173-224):
 // max; e_t = exp(s_t - max); sum in double over 8 lane accumulators
@@ -603,10 +649,17 @@ __global__ void __launch_bounds__(128) attn_softmax_v_kernel(const AttnArgs a) {
   const float inv = s_inv;
   for (int t = c; t < len; t += D) e[t] = __fmul_rn(e[t], inv);
   __syncthreads();
-  // Sequential V sum per channel: 8 loads in flight ahead of the adds.
+  // Sequential V sum per channel: 32 loads (from L2) in flight ahead of the adds.
   const __half* vc = a.v_cache + (size_t)g * a.capacity * D + c;
   float acc = 0.0f;
   int t = 0;
+  for (; t + 32 <= len; t += 32) {
+    float v[32];
+#pragma unroll
+    for (int u = 0; u < 32; ++u) v[u] = __half2float(vc[(size_t)(t + u) * D]);
+#pragma unroll
+    for (int u = 0; u < 32; ++u) acc = __fadd_rn(acc, __fmul_rn(v[u], e[t + u]));
+  }
   for (; t + 8 <= len; t += 8) {
     float v[8];
 #pragma unroll
@@ -892,8 +945,13 @@ void launch_attention(const AttnArgs& a, cudaStream_t stream) {
   if (a.exact) {
     if (a.scores == nullptr || a.capacity <= 0 || a.capacity * 4 > kGemvMaxSmem)
       throw Error(kErrArgument, "exact attention needs a scores buffer and capacity <= 57856");
-    dim3 g1(a.frames, a.kv_heads, a.splits);
-    attn_scores_kernel<<<g1, 256, 0, stream>>>(a);
+    if (a.max_len > 0 && a.skip == nullptr) {
+      dim3 g1(a.kv_heads, (a.max_len + 31) / 32, (a.frames + 7) / 8);
+      attn_scores_block_kernel<<<g1, 256, 0, stream>>>(a);
+    } else {
+      dim3 g1(a.frames, a.kv_heads, a.splits);
+      attn_scores_kernel<<<g1, 256, 0, stream>>>(a);
+    }
     FA_CUDA(cudaGetLastError());
     dim3 g2(a.frames, a.heads);
     attn_softmax_v_kernel<<<g2, 128, (size_t)a.capacity * 4, stream>>>(a);

@@ -123,6 +123,7 @@ struct AttnArgs {
   __half* v_cache = nullptr;        // [kv_heads x capacity x head]
   const int* pos = nullptr;         // device: KV length before this call
   int pos_offset = 0;               // frame 0 of this launch sits at position *pos + pos_offset
+  int max_len = 0;                  // > 0: host-known bound of *pos + pos_offset + frames (prefill)
   int splits = 16;                  // partial CTAs per (frame, kv head)
   float* part = nullptr;            // [F x kv_heads x splits x (4 + 2*head)] (split-K mode)
   float* attn = nullptr;            // [F x q_width]

@@ -161,6 +161,7 @@ struct fa_session {
   int mega_grid = 0;
   DevBuf mx, mqkv, mattn, ma, mact, mpv, mpi, mctrl;
   unsigned mega_epoch = 1;  // the control block's tag base, as the last launch left it
+  int host_pos = -1;        // position of the prefill chunk being enqueued (-1: unknown, e.g. in a graph)
   unsigned test_wait_limit = 0;  // failure-path test hooks for the next persistent launch
   int test_withhold = -1;
   bool trace = false;
@@ -1036,10 +1037,12 @@ void enqueue_attention(fa_session* s, int l, int frames, const int* skip) {
   fa_model* m = s->m;
   const int qw = m->heads * m->head_size, kvw = m->kv_heads * m->head_size;
   for (int f0 = 0; f0 < frames; f0 += kAttnChunkFrames) {
-    AttnArgs a = attn_args(s, l, std::min(kAttnChunkFrames, frames - f0), skip);
+    const int n = std::min(kAttnChunkFrames, frames - f0);
+    AttnArgs a = attn_args(s, l, n, skip);
     a.qkv += (size_t)f0 * (qw + 2 * kvw);
     a.attn += (size_t)f0 * qw;
     a.pos_offset = f0;
+    if (s->host_pos >= 0) a.max_len = s->host_pos + f0 + n;
     launch_qk_rope_kv(a, s->stream);
     launch_attention(a, s->stream);
   }
@@ -1451,7 +1454,9 @@ static int session_decode_locked(fa_session* s, const float* emb, const int32_t*
       FA_CUDA(cudaMemcpyAsync(s->tokens.as<int>(), tokens + done, (size_t)c * 4, cudaMemcpyHostToDevice, s->stream));
       enqueue_embed(s, s->tokens.as<int>(), c, nullptr);
     }
+    s->host_pos = s->pos + done;
     enqueue_layers(s, c, nullptr);
+    s->host_pos = -1;
     done += c;
     if (done == frames && output_logits) enqueue_head(s, s->x.as<float>() + (size_t)(c - 1) * W, nullptr);
     StepState st = step_state(s);
