@@ -266,14 +266,19 @@ struct BmmLayout {
   // Epilogue warps: EW / 4 per TMEM lane quarter, each owning HW of a block's
   // NS columns (16 warps once the tile is wide enough, for latency hiding).
   static constexpr int EW = NS >= 16 ? 16 : 8;
-  static constexpr int kThreads = 64 + 32 * EW;  // warp 0 copies, warp 1 issues MMAs
+  // Warp 0 copies; warps 1 and 2 + EW issue the MMAs, each half of every
+  // accumulator group: one issuing thread reaches one K = 32 MMA per ~70
+  // cycles, two reach the tensor pipe's ~40 (measured on B200).
+  static constexpr int kIssuer2 = 2 + EW;
+  static constexpr int kThreads = 64 + 32 * EW + 32;
   static constexpr int HW = NS / (EW / 4);
   static constexpr int kBars = kScBase + kScs * kScStage;
-  static constexpr int kNumBars = 2 * kOps + 2 * kScs + 2 * kNGB + 1;
+  static constexpr int kNumBars = 2 * kOps + 2 * kScs + 2 * kNGB + 2;
   static constexpr int kMisc = kBars + 8 * kNumBars;
   static constexpr int kRed = kMisc + 16;  // epilogue exchange: 4 lane quarters x NS x 8 B
   static constexpr int kTotal = kRed + 4 * NS * 8;
   static_assert(8 % G == 0, "a stage holds whole groups");
+  static_assert(G % 2 == 0, "each issuer takes half of a group");
   static_assert(kOps >= 2, "operand ring");
   static_assert(kNGB * kGroupCols == kCols, "TMEM groups");
   static_assert(kTotal <= 227 * 1024, "shared memory");
@@ -304,7 +309,7 @@ __global__ void __launch_bounds__(BmmLayout<NS, F16S>::kThreads, 1)
   uint64_t* sc_empty = sc_full + SCS;
   uint64_t* afull = sc_empty + SCS;
   uint64_t* aempty = afull + NGB;
-  uint64_t* drained = aempty + NGB;
+  uint64_t* drained = aempty + NGB;  // one per MMA issuer
   unsigned* tmem_slot = reinterpret_cast<unsigned*>(sm + L::kMisc);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(sm + L::kMisc + 4);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -315,17 +320,18 @@ __global__ void __launch_bounds__(BmmLayout<NS, F16S>::kThreads, 1)
     griddep_launch();
     for (int s = 0; s < OPS; ++s) {
       mbar_init(&op_full[s], 1);
-      mbar_init(&op_empty[s], 1);
+      mbar_init(&op_empty[s], 2);  // both issuers' commits
     }
     for (int s = 0; s < SCS; ++s) {
       mbar_init(&sc_full[s], 1);
       mbar_init(&sc_empty[s], kEpiWarps);
     }
     for (int b = 0; b < NGB; ++b) {
-      mbar_init(&afull[b], 1);
+      mbar_init(&afull[b], 2);  // both issuers' commits
       mbar_init(&aempty[b], kEpiWarps);
     }
-    mbar_init(drained, 1);
+    mbar_init(&drained[0], 1);
+    mbar_init(&drained[1], 1);
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -392,8 +398,11 @@ __global__ void __launch_bounds__(BmmLayout<NS, F16S>::kThreads, 1)
         wait_phase(&sc_full[s % SCS], (s / SCS) & 1, abort_flag, a.err, kBatchWaitLoad, false);
     }
     __syncwarp();
-  } else if (warp == 1) {
-    // ---- MMA issuer: one K = 32 MMA per Q8 block, G blocks per accumulator group ----
+  } else if (warp == 1 || warp == L::kIssuer2) {
+    // ---- MMA issuers: one K = 32 MMA per Q8 block; issuer i takes blocks
+    // [i G/2, (i+1) G/2) of every accumulator group and commits the group and
+    // the stage once (the barriers count both issuers) ----
+    const int half = warp == 1 ? 0 : 1;
     if (lane == 0) {
       constexpr unsigned idesc = idesc_i8(kBmmRows, NS);
       bool ok = true;
@@ -414,7 +423,7 @@ __global__ void __launch_bounds__(BmmLayout<NS, F16S>::kThreads, 1)
             }
             tc_fence_after();
 #pragma unroll
-            for (int u = 0; u < G; ++u) {
+            for (int u = half * (G / 2); u < (half + 1) * (G / 2); ++u) {
               const int kb = g8 * G + u;
               const uint64_t ad = smem_desc(st + kb * 256, 128, 2048);
               const uint64_t bd = smem_desc(st + L::kB + kb * 256, 128, 2048);
@@ -427,8 +436,8 @@ __global__ void __launch_bounds__(BmmLayout<NS, F16S>::kThreads, 1)
       }
       if (!ok && gq > 0) {
         // MMAs still in flight must finish before the accumulators are freed.
-        tc_commit(drained);
-        wait_phase(drained, 0, abort_flag, a.err, kBatchWaitMma, false);
+        tc_commit(&drained[half]);
+        wait_phase(&drained[half], 0, abort_flag, a.err, kBatchWaitMma, false);
       }
     }
     __syncwarp();
