@@ -288,6 +288,77 @@ def batch_bench(be, path, name, steps, warmup, rank, world, dist, local, barrier
     }
 
 
+PHASES = (  # (name, (CTA set, event) at the phase's end, (CTA set, event) at its start); -1: previous layer
+    ("x -> Q inputs gathered", ("g", 0), ("g", -1)),
+    ("Q norm + quantise", ("g", 1), ("g", 0)),
+    ("Q/K/V GEMV", ("g", 3), ("g", 1)),
+    ("q/k/v hand-off", ("a", 1), ("g", 3)),
+    ("attn QK-norm, RoPE, KV write", ("a", 2), ("a", 1)),
+    ("attn scores", ("a", 3), ("a", 2)),
+    ("attn softmax", ("a", 4), ("a", 3)),
+    ("attn V sums + publish", ("a", 5), ("a", 4)),
+    ("attention -> O hand-off", ("g", 4), ("a", 5)),
+    ("O GEMV + residual", ("g", 7), ("g", 4)),
+    ("a -> gate/up hand-off", ("g", 8), ("g", 7)),
+    ("gate/up norm + quantise", ("g", 9), ("g", 8)),
+    ("gate/up GEMV + SiLU", ("g", 11), ("g", 9)),
+    ("SiLU -> down hand-off", ("g", 12), ("g", 11)),
+    ("down GEMV + residual", ("g", 15), ("g", 12)),
+    ("layer", ("g", 15), ("g", -1)),
+)
+
+
+def phase_table(be, path, reps=5, steps=4):
+    """Per-phase critical path of the persistent decode kernel at positions
+    408.. (config 2), from `fa_session_set_trace`'s %globaltimer stamps of each
+    launch's first step: for every layer after the first, the latest CTA's
+    stamp at a phase's end minus the latest stamp at its start.  Prints the
+    median and 90th percentile over layers and repetitions."""
+    from funasrnet_b200.decoder import CudaModel, QwenDecoder
+
+    audio, ids, _, _ = CONFIGS["bs1_400"]
+    cm = CudaModel(be, path, capacity=2048)
+    dec = QwenDecoder(cm)
+    att_ctas = cm.heads
+    emb, frames = prefix(cm.width, audio, ids, cm.vocab, dec.embed)
+    rows, plain = [], []
+    for rep in range(reps + 1):
+        dec.reset()
+        dec.decode(emb, frames, want_logits=False)
+        dec.generate(steps, end_ids=())
+        plain.append(dec.last_generate_ms() / steps * 1000.0)
+        dec.reset()
+        dec.decode(emb, frames, want_logits=False)
+        dec.trace_phases(True)
+        dec.generate(steps, end_ids=())
+        tr = dec.phase_trace().astype(np.float64)
+        dec.trace_phases(False)
+        if rep == 0:
+            continue  # warm-up
+        sets = {"a": tr[:att_ctas], "g": tr[att_ctas:]}
+
+        def latest(which, event):
+            v = sets[which][:, event]
+            v = v[v > 0]
+            return v.max() if v.size else np.nan
+
+        for layer in range(1, cm.layers):
+            b, pb = 16 * layer, 16 * (layer - 1)
+            r = {}
+            for name, (ew, ee), (sw, se) in PHASES:
+                start = latest(sw, pb + 15) if se == -1 else latest(sw, b + se)
+                r[name] = latest(ew, b + ee) - start
+            rows.append(r)
+    print(f"decode_mega_kernel phase trace: Qwen3-0.6B Q8_0, prefix {audio + ids}, first step of {reps} launches; "
+          f"untraced {np.median(plain[1:]):.1f} us/step")
+    print(f"{'phase (per layer, layers 1..27)':34s} {'median ns':>10s} {'p90 ns':>8s}")
+    for name, _, _ in PHASES:
+        v = np.array([r[name] for r in rows])
+        print(f"{name:34s} {np.nanmedian(v):10.0f} {np.nanpercentile(v, 90):8.0f}")
+    dec.close()
+    cm.close()
+
+
 def fp32_bench(be, warmup, world, dist, local, barrier, peak, peak_kind):
     """Config 3 (FP32 weights, prefix 100+8, greedy 128) on one GPU: the CUDA
     graph step with the FP32 GEMV, timed over all 128 decode steps."""
@@ -350,6 +421,8 @@ def main():
     ap.add_argument("--cpu-baseline-steps", type=int, default=24)
     ap.add_argument("--no-fp32", action="store_true", help="skip the FP32 (config 3) entry of the default run")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--phase-trace", action="store_true",
+                    help="print the persistent kernel's per-phase table (config 2, one GPU) instead of the JSON line")
     args = ap.parse_args()
     batched = args.config in BATCH_CONFIGS
     cfg = CONFIGS["bs1_400" if batched else args.config]
@@ -408,6 +481,10 @@ def main():
 
     path = ensure_model(quantized, rank, barrier)
     be = CudaFloatBackend(local)
+    if args.phase_trace:
+        phase_table(be, path)
+        be.dispose()
+        return
     if batched:
         r = batch_bench(be, path, args.config, args.steps, warmup, rank, world, dist, local, barrier,
                         sessions=args.sessions, profile=args.profile_range)
