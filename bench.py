@@ -321,7 +321,7 @@ def phase_table(be, path, reps=5, steps=4):
     dec = QwenDecoder(cm)
     att_ctas = cm.heads
     emb, frames = prefix(cm.width, audio, ids, cm.vocab, dec.embed)
-    rows, plain = [], []
+    rows, plain, cyc = [], [], []
     for rep in range(reps + 1):
         dec.reset()
         dec.decode(emb, frames, want_logits=False)
@@ -349,12 +349,17 @@ def phase_table(be, path, reps=5, steps=4):
                 start = latest(sw, pb + 15) if se == -1 else latest(sw, b + se)
                 r[name] = latest(ew, b + ee) - start
             rows.append(r)
+            cyc.append(sets["a"][:, b + 6:b + 10])
     print(f"decode_mega_kernel phase trace: Qwen3-0.6B Q8_0, prefix {audio + ids}, first step of {reps} launches; "
           f"untraced {np.median(plain[1:]):.1f} us/step")
     print(f"{'phase (per layer, layers 1..27)':34s} {'median ns':>10s} {'p90 ns':>8s}")
     for name, _, _ in PHASES:
         v = np.array([r[name] for r in rows])
         print(f"{name:34s} {np.nanmedian(v):10.0f} {np.nanpercentile(v, 90):8.0f}")
+    c = np.concatenate(cyc)  # [layers x attention CTAs, 4] SM cycles
+    print(f"{'attention CTA, SM cycles per layer':34s} {'median':>10s} {'p90':>8s}")
+    for k, name in enumerate(("waiting for K chunks", "waiting for V chunks", "score loop", "V loop")):
+        print(f"{name:34s} {np.median(c[:, k]):10.0f} {np.percentile(c[:, k], 90):8.0f}")
     dec.close()
     cm.close()
 
