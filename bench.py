@@ -321,7 +321,7 @@ def phase_table(be, path, reps=5, steps=4):
     dec = QwenDecoder(cm)
     att_ctas = cm.heads
     emb, frames = prefix(cm.width, audio, ids, cm.vocab, dec.embed)
-    rows, plain, cyc = [], [], []
+    rows, plain, cyc, gcyc = [], [], [], []
     for rep in range(reps + 1):
         dec.reset()
         dec.decode(emb, frames, want_logits=False)
@@ -331,7 +331,8 @@ def phase_table(be, path, reps=5, steps=4):
         dec.decode(emb, frames, want_logits=False)
         dec.trace_phases(True)
         dec.generate(steps, end_ids=())
-        tr = dec.phase_trace().astype(np.float64)
+        raw = dec.phase_trace().astype(np.uint64)
+        tr = raw.astype(np.float64)
         dec.trace_phases(False)
         if rep == 0:
             continue  # warm-up
@@ -350,6 +351,12 @@ def phase_table(be, path, reps=5, steps=4):
                 r[name] = latest(ew, b + ee) - start
             rows.append(r)
             cyc.append(sets["a"][:, b + 6:b + 10])
+            g = sets["g"]
+            w = g[:, [b + 2, b + 6, b + 10, b + 14]]
+            span = g[:, [b + 3, b + 7, b + 11, b + 15]] - g[:, [b + 1, b + 4, b + 9, b + 12]]
+            busy = (w > 0) & (span > 0)  # CTAs with rows in the phase
+            gcyc.append(np.where(busy, w, np.nan))
+            gcyc.append(np.where(busy, span, np.nan))
     print(f"decode_mega_kernel phase trace: Qwen3-0.6B Q8_0, prefix {audio + ids}, first step of {reps} launches; "
           f"untraced {np.median(plain[1:]):.1f} us/step")
     print(f"{'phase (per layer, layers 1..27)':34s} {'median ns':>10s} {'p90 ns':>8s}")
@@ -360,6 +367,11 @@ def phase_table(be, path, reps=5, steps=4):
     print(f"{'attention CTA, SM cycles per layer':34s} {'median':>10s} {'p90':>8s}")
     for k, name in enumerate(("waiting for K chunks", "waiting for V chunks", "score loop", "V loop")):
         print(f"{name:34s} {np.median(c[:, k]):10.0f} {np.percentile(c[:, k], 90):8.0f}")
+    gw, gc = np.concatenate(gcyc[0::2]), np.concatenate(gcyc[1::2])  # [layers x GEMV CTAs, 4 phases]
+    print(f"{'GEMV CTA, per layer':34s} {'median':>10s} {'p90':>8s}")
+    for k, ph in enumerate(("Q/K/V", "O", "gate/up", "down")):
+        print(f"{ph + ' weight wait, SM cycles':34s} {np.nanmedian(gw[:, k]):10.0f} {np.nanpercentile(gw[:, k], 90):8.0f}")
+        print(f"{ph + ' phase of this CTA, ns':34s} {np.nanmedian(gc[:, k]):10.0f} {np.nanpercentile(gc[:, k], 90):8.0f}")
     dec.close()
     cm.close()
 

@@ -548,20 +548,29 @@ __device__ __forceinline__ float tile_segment(Ctx& c, const uint8_t* tile, int t
   return sum;
 }
 
+// Waits (bounded) for the weight pieces of a phase of nt tiles in pieces of
+// `per` (whole warps).  Called before the phase gathers its inputs: the
+// pieces landed long before, but each probe costs a few hundred cycles, which
+// the input wait then hides.  False when the kernel aborts.
+__device__ __forceinline__ bool phase_weights(Ctx& c, int nt, int per) {
+  const long long w0 = c.trace != nullptr ? clock64() : 0;
+  const bool ok = ring_acquire_all(ring_w(), c.nw, (nt + per - 1) / per, c.sh(), c.A->ctrl);
+  if (c.trace && c.tid == 0 && c.wait_ev >= 0) c.trace[c.wait_ev] = (unsigned long long)(clock64() - w0);
+  return ok;
+}
+
 // One projection phase over this CTA's nt tiles of K columns, streamed in ring
-// pieces of `per` tiles.  epi(t, r, sum) runs in the lanes that hold the sum
-// of row r of tile t.  False when the kernel aborts.
+// pieces of `per` tiles (acquired by phase_weights; `ready` is its result).
+// epi(t, r, sum) runs in the lanes that hold the sum of row r of tile t.
+// False when the kernel aborts.
 template <int K, typename Epi>
-__device__ __forceinline__ bool w8a8_phase(Ctx& c, int nt, int per, Epi epi) {
+__device__ __forceinline__ bool w8a8_phase(Ctx& c, int nt, int per, bool ready, Epi epi) {
   constexpr int NS = K / 1024, TB = 8 * K + (K / 32) * 16;
   const int np = (nt + per - 1) / per;
-  const long long w0 = c.trace != nullptr ? clock64() : 0;
-  const bool failed = !ring_acquire_all(ring_w(), c.nw, np, c.sh(), c.A->ctrl);
-  if (c.trace && c.tid == 0 && c.wait_ev >= 0) c.trace[c.wait_ev] = (unsigned long long)(clock64() - w0);
   // Every warp takes the same branch: the jobs below wait on each other at
   // named barriers, which have no time limit.  (On failure the drain waits
   // for the copies in flight.)
-  if (csync_or(failed || c.sh()->abort)) return false;
+  if (csync_or(!ready || c.sh()->abort)) return false;
   for (int j = c.warp; j < nt * NS; j += CWARPS) {  // warp-uniform
     const int t = j / NS, s = j - t * NS, piece = t / per;
     const uint8_t* tile = ring_w().base + (size_t)((c.nw + piece) % WSLOTS) * WSLOT + (size_t)(t - piece * per) * TB;
@@ -774,6 +783,20 @@ __device__ __forceinline__ void head_rope(Ctx& c, float* v, float co, float si, 
 __device__ __noinline__ int attention(Ctx c, int layer, int pos, unsigned tag_in, unsigned tag_out, float co, float si) {
   const MegaArgs& A = *c.A;
   const int h = blockIdx.x, g = h >> 1;
+  const int chunks = (pos + CHUNK - 1) / CHUNK;
+  const bool timed = c.trace != nullptr;  // wait and loop cycles for the trace
+  // When the layer's K chunks fit in the ring together they are all issued by
+  // now (the previous layer's V loop released their slots): probe them here,
+  // where the probes (a few hundred cycles each) overlap the wait for q/k/v,
+  // instead of one per chunk in the score loop.
+  const bool whole_k = chunks <= ASLOTS;
+  long long kwait = 0;
+  bool failed = false;
+  if (whole_k) {
+    const long long k0 = timed ? clock64() : 0;
+    failed = !ring_acquire_all(ring_a(), c.na, chunks, c.sh(), A.ctrl);
+    if (timed) kwait = clock64() - k0;
+  }
   // norm weight of this thread's q (warps 0..3) or k (warps 4..7) channel,
   // requested before the wait for q/k/v
   float gn = 0.0f;
@@ -815,15 +838,16 @@ __device__ __noinline__ int attention(Ctx c, int layer, int pos, unsigned tag_in
   float qj[D / 8];
 #pragma unroll
   for (int i = 0; i < D / 8; ++i) qj[i] = c.aq()[j + 8 * i];
-  const int chunks = (pos + CHUNK - 1) / CHUNK;
-  const bool timed = c.trace != nullptr;  // wait and loop cycles for the trace
-  bool failed = false;
-  long long kwait = 0;
   const long long s0 = timed ? clock64() : 0;
   for (int ch = 0; ch < chunks; ++ch) {
-    const long long k0 = timed ? clock64() : 0;
-    const uint8_t* kb = failed ? nullptr : ring_acquire(ring_a(), c.na, c.sh(), A.ctrl);
-    if (timed) kwait += clock64() - k0;
+    const uint8_t* kb = nullptr;
+    if (whole_k) {
+      if (!failed) kb = ring_a().base + (size_t)(c.na % ASLOTS) * CSLOT;
+    } else {
+      const long long k0 = timed ? clock64() : 0;
+      kb = failed ? nullptr : ring_acquire(ring_a(), c.na, c.sh(), A.ctrl);
+      if (timed) kwait += clock64() - k0;
+    }
     if (kb == nullptr) {  // abort: stop consuming; all warps leave together below
       failed = true;
       continue;
@@ -1094,6 +1118,8 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(const Mega
         continue;
       }
       // ---- Q: x -> RMSNorm -> quantise -> q/k/v rows ----
+      c.wait_ev = ev + 2;
+      const bool wq = phase_weights(c, sp.qn, 3);
       {
         float v[3];
         if (layer > 0) {
@@ -1109,10 +1135,9 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(const Mega
       {
         const unsigned tag = tl + kTagQkv;
         const int q0 = sp.q0;
-        c.wait_ev = ev + 2;
         // Failure-path test hook: the named CTA leaves its first q/k/v rows unpublished.
         const bool hold = A.withhold == (int)blockIdx.x && step == 0 && layer == 0;
-        if (!w8a8_phase<W>(c, sp.qn, 3, [&](int t, int r, float v) {
+        if (!w8a8_phase<W>(c, sp.qn, 3, wq, [&](int t, int r, float v) {
               if (!hold) st_word(A.qkv_t + (q0 + t) * 8 + r, pack(v, tag));
             }))
           goto drain;
@@ -1129,12 +1154,13 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(const Mega
       }
       // ---- O: quantised attention output -> o + x ----
       if (sp.on > 0) {
+        c.wait_ev = ev + 6;
+        const bool wo = phase_weights(c, sp.on, 1);
         gather_q8<400>(c, A.attn_t, QW, tl + kTagAttn);
         MEGA_TRACE(ev + 4);
         const unsigned tag = tl + kTagA;
         const int o0 = sp.o0;
-        c.wait_ev = ev + 6;
-        if (!w8a8_phase<QW>(c, sp.on, 1, [&](int t, int r, float v) {
+        if (!w8a8_phase<QW>(c, sp.on, 1, wo, [&](int t, int r, float v) {
               const int row = (o0 + t) * 8 + r;
               st_word(A.a_t + row, pack(__fadd_rn(v, c.xres()[row]), tag));
             }))
@@ -1142,6 +1168,8 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(const Mega
         MEGA_TRACE(ev + 7);
       }
       // ---- GU: a -> RMSNorm -> quantise -> SiLU(gate) * up -> quantised act ----
+      c.wait_ev = ev + 10;
+      const bool wg = sp.gbn > 0 ? phase_weights(c, 8, 3) : true;
       {
         float v[3];
         gather<3>(c, A.a_t, W, tl + kTagA, v);
@@ -1157,8 +1185,9 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(const Mega
       }
       MEGA_TRACE(ev + 9);
       for (int bj = 0; bj < sp.gbn; ++bj) {
-        c.wait_ev = bj == 0 ? ev + 10 : -1;
-        if (!w8a8_phase<W>(c, 8, 3, [&](int t, int r, float v) { c.part()[t * 8 + r] = v; })) goto drain;
+        c.wait_ev = -1;
+        const bool ready = bj == 0 ? wg : phase_weights(c, 8, 3);
+        if (!w8a8_phase<W>(c, 8, 3, ready, [&](int t, int r, float v) { c.part()[t * 8 + r] = v; })) goto drain;
         if (warp == 0) {  // lane = 8 * pair + row: the block's 32 SiLU(gate) * up values
           const float act = silu_mul1(c.part()[(lane >> 3) * 16 + (lane & 7)], c.part()[(lane >> 3) * 16 + 8 + (lane & 7)]);
           publish_block(A.act_t, FFN, sp.gb0 + bj, act, tl + kTagAct, lane);
@@ -1168,12 +1197,13 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(const Mega
       MEGA_TRACE(ev + 11);
       // ---- D: quantised act -> down + a ----
       if (sp.dn > 0) {
+        c.wait_ev = ev + 14;
+        const bool wd = phase_weights(c, sp.dn, 1);
         gather_q8<400>(c, A.act_t, FFN, tl + kTagAct);
         MEGA_TRACE(ev + 12);
         const unsigned tag = tl + kTagX;
         const int d0 = sp.d0;
-        c.wait_ev = ev + 14;
-        if (!w8a8_phase<FFN>(c, sp.dn, 1, [&](int t, int r, float v) {
+        if (!w8a8_phase<FFN>(c, sp.dn, 1, wd, [&](int t, int r, float v) {
               const int row = (d0 + t) * 8 + r;
               st_word(A.x_t + row, pack(__fadd_rn(v, c.ares()[row]), tag));
             }))
