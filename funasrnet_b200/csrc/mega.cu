@@ -935,25 +935,41 @@ __device__ __noinline__ int attention(Ctx c, int layer, int pos, unsigned tag_in
       redf[31] = __double2float_rn(__ddiv_rn(1.0, acc));
     }
   }
+  // Meanwhile the V warps probe the layer's V chunks when they fit in the ring
+  // together (the score loop released the K slots they need).
+  const bool whole_v = chunks <= ASLOTS;
+  long long vwait = 0;
+  bool vok = true;
+  if (whole_v && c.warp >= 1 && c.warp <= 4) {
+    const long long t0 = timed ? clock64() : 0;
+    vok = ring_acquire_all(ring_a(), c.na, chunks, c.sh(), A.ctrl);
+    if (timed) vwait = clock64() - t0;
+  }
   csync();
   const float inv = redf[31];
   for (int t = c.tid; t < len; t += CTHREADS) c.sc()[t] = __fmul_rn(c.sc()[t], inv);
   csync();
   if (c.trace && c.tid == 0) c.trace[kTraceLayerEvents * layer + 4] = global_ns();
   // V sum per channel in position order (TensorMath.AttentionAvx.cs:188-213):
-  // warps 0..3, thread = channel.  A full chunk runs as five groups of 12
+  // warps 1..4, thread = channel.  A full chunk runs as five groups of 12
   // positions, each group's V values and weights loaded into registers while
   // the previous group's products and dependent adds run.
-  if (c.warp < 4) {
+  if (c.warp >= 1 && c.warp <= 4) {
+    const int ci = c.tid - 32;  // channel
     float acc = 0.0f;
-    long long vwait = 0;
     const long long v0 = timed ? clock64() : 0;
+    if (!vok) return c.na;
     for (int ch = 0; ch < chunks; ++ch) {
-      const long long t0 = timed ? clock64() : 0;
-      const uint8_t* vb = ring_acquire(ring_a(), c.na + ch, c.sh(), A.ctrl);
-      if (timed) vwait += clock64() - t0;
-      if (vb == nullptr) return c.na + ch;
-      const __half* vv = reinterpret_cast<const __half*>(vb) + c.tid;
+      const uint8_t* vb;
+      if (whole_v) {
+        vb = ring_a().base + (size_t)((c.na + ch) % ASLOTS) * CSLOT;
+      } else {
+        const long long t0 = timed ? clock64() : 0;
+        vb = ring_acquire(ring_a(), c.na + ch, c.sh(), A.ctrl);
+        if (timed) vwait += clock64() - t0;
+        if (vb == nullptr) return c.na + ch;
+      }
+      const __half* vv = reinterpret_cast<const __half*>(vb) + ci;
       const float* pr = c.sc() + ch * CHUNK;
       const int n = min(CHUNK, pos - ch * CHUNK);
       if (n == CHUNK) {
@@ -981,18 +997,23 @@ __device__ __noinline__ int attention(Ctx c, int layer, int pos, unsigned tag_in
       } else {
         for (int t = 0; t < n; ++t) acc = __fadd_rn(acc, __fmul_rn(__half2float(vv[t * D]), pr[t]));
       }
-      // The four V warps' arrivals make up the slot's CWARPS.
-      __syncwarp();
-      if (c.lane == 0) mbar_arrive_count(&ring_a().empty[(c.na + ch) % ASLOTS], c.warp == 0 ? CWARPS - 3 : 1);
+      if (!whole_v) {  // the four V warps' arrivals make up the slot's CWARPS
+        __syncwarp();
+        if (c.lane == 0) mbar_arrive_count(&ring_a().empty[(c.na + ch) % ASLOTS], c.warp == 1 ? CWARPS - 3 : 1);
+      }
     }
-    acc = __fadd_rn(acc, __fmul_rn(c.av()[c.tid], c.sc()[pos]));
-    if (c.trace && c.tid == 0) {
+    if (whole_v) {
+      __syncwarp();
+      if (c.lane < chunks) mbar_arrive_count(&ring_a().empty[(c.na + c.lane) % ASLOTS], c.warp == 1 ? CWARPS - 3 : 1);
+    }
+    acc = __fadd_rn(acc, __fmul_rn(c.av()[ci], c.sc()[pos]));
+    if (c.trace && ci == 0) {
       c.trace[kTraceLayerEvents * layer + 7] = (unsigned long long)vwait;
       c.trace[kTraceLayerEvents * layer + 9] = (unsigned long long)(clock64() - v0);
     }
     // The O projection's input quantisation of this head's four blocks
-    // (block 4h + warp), done once here instead of in every GEMV CTA.
-    publish_block(A.attn_t, QW, h * 4 + c.warp, acc, tag_out, c.lane);
+    // (block 4h + warp - 1), done once here instead of in every GEMV CTA.
+    publish_block(A.attn_t, QW, h * 4 + c.warp - 1, acc, tag_out, c.lane);
   }
   return c.na + chunks;
 }
