@@ -72,6 +72,7 @@ SIGNATURES = {
     "fa_session_kernels_per_step": (i32, [vp]),
     "fa_session_uses_persistent_kernel": (i32, [vp]),
     "fa_session_set_persistent_kernel": (i32, [vp, i32]),
+    "fa_session_set_resident": (i32, [vp, i32, i32]),
     "fa_session_set_trace": (i32, [vp, i32]),
     "fa_session_set_fault_test": (i32, [vp, C.c_uint32, i32]),
     "fa_session_get_trace": (i32, [vp, vp, i32]),

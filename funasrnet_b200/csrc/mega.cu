@@ -185,6 +185,23 @@ __device__ __forceinline__ unsigned long long ld_word_acquire(const unsigned lon
 __device__ __forceinline__ void st_word_release(unsigned long long* p, unsigned long long v) {
   asm volatile("st.release.gpu.global.b64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
+// System-scope accesses of the resident-serving mailbox (mapped host memory).
+__device__ __forceinline__ int ld_acquire_sys(const int* p) {
+  int v;
+  asm volatile("ld.acquire.sys.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ int ld_relaxed_sys(const int* p) {
+  int v;
+  asm volatile("ld.relaxed.sys.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_relaxed_sys(int* p, int v) {
+  asm volatile("st.relaxed.sys.global.b32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ void st_release_sys(int* p, int v) {
+  asm volatile("st.release.sys.global.b32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
 __device__ __forceinline__ int ld_flag(const int* p) {
   int v;
   asm volatile("ld.relaxed.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
@@ -1018,6 +1035,48 @@ __device__ __noinline__ int attention(Ctx c, int layer, int pos, unsigned tag_in
   return c.na + chunks;
 }
 
+// Resident serving: the token step `step` consumes (thread 0 of each CTA);
+// -1 when the host stops the launch, -2 when no token comes within the idle
+// limit, -3 when the kernel aborts.  CTA 0 polls the host mailbox and relays
+// what it read; the other CTAs wait for the relay, bounded by the leader's
+// idle limit plus a second.
+__device__ __noinline__ int resident_token(const MegaArgs& A, Shared* sh, MegaCtrl* ctrl, int step) {
+  const unsigned tag = A.relay_base + (unsigned)step;
+  const unsigned long long t0 = global_ns();
+  if (blockIdx.x == 0) {
+    const int want = (int)(A.seq0 + (unsigned)step + 1u);
+    int tok = -2;
+    for (unsigned it = 0;; ++it) {
+      if (ld_acquire_sys(A.mbox) == want) {
+        tok = ld_relaxed_sys(A.mbox + 1);
+        break;
+      }
+      if ((it & 15) == 15) {
+        if (sh->abort || ld_flag(&ctrl->error)) {
+          tok = -3;
+          break;
+        }
+        if (global_ns() - t0 > A.idle_ns) break;
+      }
+    }
+    st_word_release(A.relay, ((unsigned long long)tag << 32) | (unsigned)tok);
+    return tok;
+  }
+  const unsigned long long limit = A.idle_ns + 1000000000ull;
+  for (unsigned it = 0;; ++it) {
+    const unsigned long long w = ld_word_acquire(A.relay);
+    if ((unsigned)(w >> 32) == tag) return (int)(unsigned)w;
+    __nanosleep(100);
+    if ((it & 63) == 63) {
+      if (sh->abort || ld_flag(&ctrl->error)) return -3;
+      if (global_ns() - t0 > limit) {
+        raise_error(sh, ctrl, kErrWaitData);
+        return -3;
+      }
+    }
+  }
+}
+
 // Records a phase timestamp of the first step (thread 0 only; a no-op unless tracing).
 #define MEGA_TRACE(event)                                                                 \
   do {                                                                                    \
@@ -1106,6 +1165,13 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(const Mega
       // this fence orders the partial exchange's acquires before the flag.
       __threadfence();
       sh->go = step + 1;
+    }
+    if (A.mbox != nullptr) {  // resident serving: the host's token (the step's copies are already requested)
+      if (tid == 0) sh->token = resident_token(A, sh, ctrl, step);
+      csync();
+      const int posted = sh->token;
+      if (posted < 0) break;  // stop, idle or abort: `token` keeps the last argmax
+      token = posted;
     }
     const int pos = pos0 + step;
     const unsigned tbase = epoch + (unsigned)step * tps;
@@ -1369,6 +1435,10 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(const Mega
       MEGA_TRACE(ev + 4);
       token = sh->token;
       ++steps;
+      if (A.mbox != nullptr && blockIdx.x == 0 && tid == 0) {  // the step's argmax, then its sequence number
+        st_relaxed_sys(A.mbox + 3, token);
+        st_release_sys(A.mbox + 2, (int)(A.seq0 + (unsigned)step + 1u));
+      }
     }
   }
 drain:

@@ -79,6 +79,18 @@ struct MegaArgs {
   // first step's layer-0 q/k/v rows unpublished (-1: none).
   unsigned wait_limit = 0;
   int withhold = -1;
+  // Resident serving (fa_session_set_resident): when mbox is non-null every
+  // step takes its token from the host.  mbox is mapped pinned host memory:
+  // [0] the sequence number the host posted, [1] its token (-1: stop the
+  // launch); the kernel writes [3] the step's argmax, then [2] the sequence
+  // number it consumed.  Step k consumes sequence seq0 + k + 1.  CTA 0 polls
+  // the mailbox and relays the token to the other CTAs through `relay` with
+  // tag relay_base + k (unique over the session's launches).  A step whose
+  // token does not come within idle_ns ends the launch (the host relaunches).
+  int* mbox = nullptr;
+  unsigned long long* relay = nullptr;
+  unsigned seq0 = 0, relay_base = 0;
+  unsigned long long idle_ns = 0;
 };
 constexpr int kTraceLayerEvents = 16;
 constexpr int kTraceEvents = kTraceLayerEvents * 28 + 8;

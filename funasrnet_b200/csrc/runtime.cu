@@ -5,6 +5,8 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <atomic>
+#include <chrono>
 #include <cmath>
 #include <cstddef>
 #include <cstdlib>
@@ -23,6 +25,12 @@
 #include "mega.h"
 
 using namespace fa;
+
+struct fa_session;
+extern "C" {  // resident serving, defined with the persistent-kernel launch code
+static void resident_stop(fa_session* s);
+static void mbox_post(fa_session* s, int token);
+}
 
 namespace {
 
@@ -166,6 +174,18 @@ struct fa_session {
   int test_withhold = -1;
   bool trace = false;
   DevBuf trace_buf;                          // [grid x kTraceEvents] phase timestamps
+  // resident serving (fa_session_set_resident): one persistent launch keeps
+  // decoding the tokens that later fa_session_step calls post to a mailbox
+  bool resident = false;
+  bool resident_live = false;                // such a launch runs on the stream
+  unsigned long long resident_idle_ns = 20000000ull;
+  int* mbox = nullptr;                       // mapped pinned mailbox (host view; layout in MegaArgs)
+  int* mbox_dev = nullptr;                   // its device address
+  unsigned res_seq = 0;                      // last sequence number posted
+  unsigned relay_next = 1;                   // relay tag base of the next resident launch
+  DevBuf relay;                              // CTA 0 -> other CTAs token relay word
+  MegaCtrl res_in{};                         // control block the running launch started from
+  int res_steps = 0;                         // its step limit
   DevBuf bxq, bxs, bxq2, bxs2;               // frame-tile operands of tensor-core prefill projections
   int* d_int(int i) const { return ints.as<int>() + i; }
 };
@@ -1297,12 +1317,15 @@ cudaGraphExec_t capture(fa_session* s, bool generate, int n_end) {
   return exec;
 }
 
+// Every session call but the resident step runs with the session's resident
+// launch (if any) stopped first.
 template <typename F>
-int with_session(fa_session* s, F&& body) {
+int with_session(fa_session* s, F&& body, bool keep_resident = false) {
   return guarded([&] {
     if (!s) throw Error(kErrArgument, "null session");
     std::lock_guard<std::mutex> lk(s->mu);
     DeviceGuard g(s->device);
+    if (!keep_resident) resident_stop(s);
     return body();
   });
 }
@@ -1397,7 +1420,12 @@ int fa_session_free(fa_session* s) {
     if (!s) throw Error(kErrArgument, "null session");
     {
       DeviceGuard g(s->device);
+      if (s->resident_live) {  // its error, if any, no longer matters
+        mbox_post(s, -1);
+        s->resident_live = false;
+      }
       cudaStreamSynchronize(s->stream);
+      if (s->mbox) cudaFreeHost(s->mbox);
       if (s->step_graph) cudaGraphExecDestroy(s->step_graph);
       if (s->gen_graph) cudaGraphExecDestroy(s->gen_graph);
       cudaEventDestroy(s->ev0);
@@ -1486,10 +1514,8 @@ int fa_session_decode(fa_session* s, const float* embeddings, int frames, int ou
   });
 }
 
-// One persistent-kernel launch of `steps` decode steps (mega.cu).  The first
-// token is the host's (host_token >= 0) or the device argmax of the last
-// decode.  Returns the control block after the launch.
-static MegaCtrl run_mega(fa_session* s, int steps, int record, int n_end, int host_token, bool want_logits) {
+// Launch arguments of the persistent kernel (mega.cu) for `steps` decode steps.
+static MegaArgs mega_args(fa_session* s, int steps, int record, int n_end, bool want_logits) {
   fa_model* m = s->m;
   MegaArgs a;
   a.layers = s->m->mega_layers.as<MegaLayer>();
@@ -1530,6 +1556,34 @@ static MegaCtrl run_mega(fa_session* s, int steps, int record, int n_end, int ho
     FA_CUDA(cudaMemsetAsync(s->trace_buf.p, 0, bytes, s->stream));
     a.trace = s->trace_buf.as<unsigned long long>();
   }
+  // the graph path's position and token words follow the launch (written by the kernel)
+  a.out_pos = s->d_int(0);
+  a.out_token = s->d_int(1);
+  return a;
+}
+
+// The control block a finished launch left (read back after the stream
+// drained): the session's tag base, position and error.  `in` is the block
+// the launch started from, `steps` its step limit.
+static MegaCtrl mega_finish(fa_session* s, const MegaCtrl& in, int steps) {
+  MegaCtrl c;
+  std::memcpy(&c, s->pinned + 16, sizeof(c));
+  // After a failed launch its exchange words may carry any tag of its steps:
+  // the next launch starts past all of them.
+  s->mega_epoch = c.error != 0 ? in.epoch + (unsigned)steps * (unsigned)((s->m->layers + 1) * 8) : c.epoch;
+  if (c.error != 0)
+    throw Error(kErrTimeout, "persistent decode kernel: a bounded wait gave up (code " + std::to_string(c.error) +
+                                 ", CTA " + std::to_string(c.where / 32) + " warp " + std::to_string(c.where % 32) +
+                                 ")");
+  s->pos = c.pos;
+  return c;
+}
+
+// One persistent-kernel launch of `steps` decode steps (mega.cu).  The first
+// token is the host's (host_token >= 0) or the device argmax of the last
+// decode.  Returns the control block after the launch.
+static MegaCtrl run_mega(fa_session* s, int steps, int record, int n_end, int host_token, bool want_logits) {
+  MegaArgs a = mega_args(s, steps, record, n_end, want_logits);
   // the whole control block in one copy: pos, token (host or last device
   // argmax), counters and error cleared, the tag base the last launch left
   MegaCtrl in{};
@@ -1541,9 +1595,6 @@ static MegaCtrl run_mega(fa_session* s, int steps, int record, int n_end, int ho
   char* ctrl = static_cast<char*>(s->mctrl.p);
   FA_CUDA(cudaMemcpyAsync(ctrl, s->pinned + 8, sizeof(MegaCtrl), cudaMemcpyHostToDevice, s->stream));
   if (host_token < 0) FA_CUDA(cudaMemcpyAsync(ctrl + 4, s->d_int(1), 4, cudaMemcpyDeviceToDevice, s->stream));
-  // the graph path's position and token words follow the launch (written by the kernel)
-  a.out_pos = s->d_int(0);
-  a.out_token = s->d_int(1);
   const bool timed = record != 0;  // generate reports its device time; a single step does not
   if (timed) FA_CUDA(cudaEventRecord(s->ev0, s->stream));
   launch_mega(a, s->mega_grid, s->stream);
@@ -1551,24 +1602,104 @@ static MegaCtrl run_mega(fa_session* s, int steps, int record, int n_end, int ho
   FA_CUDA(cudaMemcpyAsync(s->pinned + 16, ctrl, sizeof(MegaCtrl), cudaMemcpyDeviceToHost, s->stream));
   FA_CUDA(cudaStreamSynchronize(s->stream));
   if (timed) FA_CUDA(cudaEventElapsedTime(&s->last_ms, s->ev0, s->ev1));
-  MegaCtrl c;
-  std::memcpy(&c, s->pinned + 16, sizeof(c));
-  // After a failed launch its exchange words may carry any tag of its steps:
-  // the next launch starts past all of them.
-  s->mega_epoch = c.error != 0 ? in.epoch + (unsigned)steps * (unsigned)((m->layers + 1) * 8) : c.epoch;
-  if (c.error != 0)
-    throw Error(kErrTimeout, "persistent decode kernel: a bounded wait gave up (code " + std::to_string(c.error) +
-                                 ", CTA " + std::to_string(c.where / 32) + " warp " + std::to_string(c.where % 32) +
-                                 ")");
-  s->pos = c.pos;
-  return c;
+  return mega_finish(s, in, steps);
+}
+
+// ---- resident serving ----
+// The mailbox words are shared with the running kernel: volatile accesses,
+// the token before its sequence number (x86 keeps stores in order; the fence
+// keeps the compiler from reordering them).
+static void mbox_post(fa_session* s, int token) {
+  volatile int* mb = s->mbox;
+  mb[1] = token;
+  std::atomic_thread_fence(std::memory_order_release);
+  mb[0] = (int)++s->res_seq;
+}
+
+// Starts a persistent launch whose step k decodes the token posted with
+// sequence number res_seq + k + 1 (it does not wait for it to start).
+static void resident_launch(fa_session* s) {
+  const int steps = s->m->capacity - s->pos;
+  MegaArgs a = mega_args(s, steps, 0, 0, false);
+  a.mbox = s->mbox_dev;
+  a.relay = s->relay.as<unsigned long long>();
+  a.seq0 = s->res_seq;
+  a.relay_base = s->relay_next;
+  s->relay_next += (unsigned)steps + 1u;
+  a.idle_ns = s->resident_idle_ns;
+  MegaCtrl in{};
+  in.pos = s->pos;
+  in.epoch = s->mega_epoch;
+  std::memcpy(s->pinned + 8, &in, sizeof(in));
+  char* ctrl = static_cast<char*>(s->mctrl.p);
+  FA_CUDA(cudaMemcpyAsync(ctrl, s->pinned + 8, sizeof(MegaCtrl), cudaMemcpyHostToDevice, s->stream));
+  launch_mega(a, s->mega_grid, s->stream);
+  FA_CUDA(cudaMemcpyAsync(s->pinned + 16, ctrl, sizeof(MegaCtrl), cudaMemcpyDeviceToHost, s->stream));
+  s->res_in = in;
+  s->res_steps = steps;
+  s->resident_live = true;
+}
+
+// Waits for a resident launch that has been told to stop (or has stopped)
+// and takes over its control block.
+static void resident_join(fa_session* s) {
+  s->resident_live = false;
+  FA_CUDA(cudaStreamSynchronize(s->stream));
+  mega_finish(s, s->res_in, s->res_steps);
+}
+
+// Ends the session's resident launch, if one runs: every other session call
+// does this first, so nothing else runs on the stream (or on the device,
+// whose SMs the launch holds) beside it.
+static void resident_stop(fa_session* s) {
+  if (!s->resident_live) return;
+  mbox_post(s, -1);
+  resident_join(s);
+}
+
+// One decode step of the resident launch: posts the token and spins on the
+// mailbox for the argmax.  A launch that ended before taking the token (its
+// idle limit ran out first) is joined and relaunched with the token still
+// posted; one that failed raises its error.
+static int resident_step(fa_session* s, int token) {
+  if (!s->resident_live) resident_launch(s);
+  mbox_post(s, token);
+  const int want = (int)s->res_seq;
+  volatile int* mb = s->mbox;
+  const auto t0 = std::chrono::steady_clock::now();
+  for (unsigned it = 1;; ++it) {
+    if (mb[2] == want) break;
+    if ((it & 255) != 0) continue;
+    const cudaError_t q = cudaStreamQuery(s->stream);
+    if (q == cudaErrorNotReady) {
+      if (std::chrono::steady_clock::now() - t0 > std::chrono::seconds(60))
+        throw Error(kErrTimeout, "resident decode: no result within 60 s");
+      continue;
+    }
+    if (q != cudaSuccess) FA_CUDA(q);
+    if (mb[2] == want) break;  // the step finished, then the launch ended
+    resident_join(s);          // throws the launch's error, if any
+    s->res_seq = (unsigned)want - 1u;
+    resident_launch(s);        // its first step takes the posted token
+    s->res_seq = (unsigned)want;
+  }
+  std::atomic_thread_fence(std::memory_order_acquire);
+  s->pos += 1;
+  return mb[3];
 }
 
 int fa_session_step(fa_session* s, int32_t token, float* logits, int32_t* next) {
+  const bool resident = s && s->resident && s->use_mega && s->exact_attention && !logits;
   return with_session(s, [&] {
     fa_model* m = s->m;
     check_tokens(s, &token, 1);
     if (s->pos + 1 > m->capacity) throw Error(kErrArgument, "Decoder context exhausted or invalid embeddings");
+    if (resident) {
+      const int t = resident_step(s, token);
+      s->have_token = true;
+      if (next) *next = t;
+      return (int)kHandled;
+    }
     if (s->use_mega && s->exact_attention) {
       const MegaCtrl c = run_mega(s, 1, 0, 0, token, logits != nullptr);
       if (logits) FA_CUDA(cudaMemcpy(logits, s->logits.p, (size_t)m->vocab * 4, cudaMemcpyDeviceToHost));
@@ -1589,7 +1720,7 @@ int fa_session_step(fa_session* s, int32_t token, float* logits, int32_t* next) 
     s->have_token = true;
     if (next) *next = s->pinned[1];
     return (int)kHandled;
-  });
+  }, resident);
 }
 
 int fa_session_generate(fa_session* s, int max_tokens, const int32_t* end_ids, int n_end, int32_t* tokens,
@@ -1673,6 +1804,8 @@ int fa_session_share_prefix(fa_session* dst, fa_session* src) {
     if (src->cached_prefix == 0) throw Error(kErrArgument, "share_prefix: the source has no cached prefix");
     if (dst->cached_prefix != 0) throw Error(kErrArgument, "Prefix is already cached");
     DeviceGuard g(dst->device);
+    resident_stop(dst);
+    resident_stop(src);
     fa_model* m = dst->m;
     const int n = src->cached_prefix, kvh = m->kv_heads, D = m->head_size;
     // rows [0, n) of every (layer, KV head) block: one strided copy per cache
@@ -1743,6 +1876,24 @@ int fa_session_set_persistent_kernel(fa_session* s, int on) {
   return with_session(s, [&] {
     if (on && s->mega_grid <= 0) return (int)kDeclined;
     s->use_mega = on != 0;
+    return (int)kHandled;
+  });
+}
+
+int fa_session_set_resident(fa_session* s, int on, int idle_us) {
+  return with_session(s, [&] {  // stops a running resident launch first
+    if (idle_us < 0) throw Error(kErrArgument, "idle_us must be >= 0");
+    if (on && s->mega_grid <= 0) return (int)kDeclined;
+    if (on && !s->mbox) {
+      FA_CUDA(cudaHostAlloc(&s->mbox, 64, cudaHostAllocMapped));
+      std::memset(s->mbox, 0, 64);
+      FA_CUDA(cudaHostGetDevicePointer((void**)&s->mbox_dev, s->mbox, 0));
+      s->relay.ensure(8);
+      FA_CUDA(cudaMemset(s->relay.p, 0, 8));  // tag 0 is never a relay tag
+      s->res_seq = 0;
+    }
+    s->resident = on != 0;
+    s->resident_idle_ns = (unsigned long long)(idle_us > 0 ? idle_us : 20000) * 1000ull;
     return (int)kHandled;
   });
 }
@@ -2007,6 +2158,7 @@ int with_batch(fa_batch* b, F&& body) {
     locks.reserve(order.size());
     for (fa_session* s : order) locks.emplace_back(s->mu);
     DeviceGuard g(b->device);
+    for (fa_session* s : order) resident_stop(s);
     return body();
   });
 }

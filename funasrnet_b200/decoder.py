@@ -133,6 +133,13 @@ class QwenDecoder:
     def set_persistent(self, on: bool = True) -> bool:
         return check(lib().fa_session_set_persistent_kernel(self._h, 1 if on else 0)) == FA_OK
 
+    def set_resident(self, on: bool = True, idle_us: int = 0) -> bool:
+        """Resident serving: step() without logits posts its token to one
+        persistent launch that stays running between calls (ends after idle_us
+        without a token, 0 = 20 ms, or at any other call).  False when the
+        persistent kernel is unavailable."""
+        return check(lib().fa_session_set_resident(self._h, 1 if on else 0, int(idle_us))) == FA_OK
+
     def set_fault_test(self, wait_limit: int = 0, withhold_cta: int = -1) -> None:
         """Failure-path test hook for the next persistent-kernel launch only: a
         shorter bounded-wait limit (polls) and a GEMV CTA whose first q/k/v rows

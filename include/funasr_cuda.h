@@ -193,6 +193,19 @@ int fa_session_uses_persistent_kernel(const fa_session* session);
 /* Selects the persistent kernel (1) or the CUDA-graph step (0); FA_DECLINED when
  * the persistent kernel is unavailable for this model or device. */
 int fa_session_set_persistent_kernel(fa_session* session, int on);
+/* Resident serving, for a host that decodes one token per fa_session_step
+ * call (FunAsr.Transcribe's loop, FunAsr.cs:167-178, with the token crossing
+ * the host each step).  When on, fa_session_step (without logits) leaves one
+ * persistent launch running between calls: each call posts its token to a
+ * mailbox in mapped pinned memory and spins until the launch writes back the
+ * argmax, so a step costs no kernel launch, prologue or pipeline fill.  The
+ * launch holds every SM while it waits for the next token: it ends after
+ * idle_us microseconds without one (0: 20000; the next step relaunches), and
+ * every other call on the session, or on a batch holding it, ends it first.
+ * Results are bit-identical to the other step paths.  FA_DECLINED when the
+ * persistent kernel is unavailable for this model or device.  No counterpart
+ * in the reference (whose Decode runs on the host). */
+int fa_session_set_resident(fa_session* session, int on, int idle_us);
 /* Profiling hook of the persistent kernel: when on, each launch records
  * %globaltimer stamps (ns) of its first step's phases per CTA; get_trace copies
  * [grid x events] stamps and returns grid*events.  Layer l owns events
