@@ -567,12 +567,13 @@ __global__ void __launch_bounds__(256) attn_scores_block_kernel(const AttnArgs a
   const int qw = a.heads * D, kvw = a.kv_heads * D;
   const int stride = a.qkv_stride ? a.qkv_stride : qw + 2 * kvw;
   const int nf = min(FG, a.frames - f0);
+  const int base = *a.pos + a.pos_offset;  // frame f sees positions [0, base + f]
+  if (blockIdx.y * 32 >= base + f0 + nf) return;  // a position block no frame of the group sees (causal)
   for (int i = threadIdx.x; i < 2 * FG * D; i += 256) {
     const int p = i / D, c = i - p * D;
     qs[p][c] = p < 2 * nf ? a.qkv[(size_t)(f0 + (p >> 1)) * stride + (size_t)(2 * g + (p & 1)) * D + c] : 0.0f;
   }
   __syncthreads();
-  const int base = *a.pos + a.pos_offset;  // frame f sees positions [0, base + f]
   float k[M];
   if (t < base + f0 + nf) {
     const uint4* kr = reinterpret_cast<const uint4*>(a.k_cache + ((size_t)g * a.capacity + t) * D + j * M);
@@ -669,6 +670,152 @@ __global__ void __launch_bounds__(128) attn_softmax_v_kernel(const AttnArgs a) {
   }
   for (; t < len; ++t) acc = __fadd_rn(acc, __fmul_rn(__half2float(vc[(size_t)t * D]), e[t]));
   a.attn[(size_t)f * a.heads * D + (size_t)h * D + c] = acc;
+}
+
+// Softmax + weighted V sum of kSvFrames consecutive frames and both query
+// heads of KV head g (prefill launches), each (frame, head) row in exactly
+// attn_softmax_v_kernel's order: max; e_t = exp(s_t - max); the double sum
+// over 8 lane accumulators folded (s0+s2)+(s1+s3) with s_k = lane_k +
+// lane_{k+4}, then the len % 8 tail; p_t = e_t * (float)(1/sum); each
+// channel accumulates acc + v_t * p_t in position order.  Warp w takes rows
+// w and w + 4 (r = 2 fl + h) through the softmax; then thread = channel runs
+// the 2 x kSvFrames chains of its channel, so each V value is read once for
+// all of them, from chunks of kSvChunk rows that cp.async stages into shared
+// memory one chunk ahead.  grid (kv_heads, ceil(frames / kSvFrames)), 128
+// threads; dynamic smem: 2 chunks of V rows, then max_len x 2 x kSvFrames
+// floats of probabilities ([t][h][frame]).
+constexpr int kSvFrames = 4, kSvChunk = 64;
+
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((unsigned)__cvta_generic_to_shared(dst)), "l"(src)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_one() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
+// Two IEEE products v * p0 and v * p1 in one instruction (each rounded as __fmul_rn).
+__device__ __forceinline__ void mul2(float v, float p0, float p1, float& r0, float& r1) {
+  unsigned long long a, b, c;
+  asm("mov.b64 %0, {%1, %1};" : "=l"(a) : "f"(v));
+  asm("mov.b64 %0, {%1, %2};" : "=l"(b) : "f"(p0), "f"(p1));
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(c) : "l"(a), "l"(b));
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(r0), "=f"(r1) : "l"(c));
+}
+
+size_t softmax_v_group_smem(int max_len) {
+  return (size_t)2 * kSvChunk * 128 * 2 + (size_t)max_len * 2 * kSvFrames * 4;
+}
+
+__global__ void __launch_bounds__(128) attn_softmax_v_group_kernel(const AttnArgs a) {
+  if (skipped(a.skip)) return;
+  constexpr int D = 128, FG = kSvFrames, R = 2 * FG, CH = kSvChunk;
+  extern __shared__ __align__(16) uint8_t smem[];
+  __half* vbuf = reinterpret_cast<__half*>(smem);                  // [2][CH][D]
+  float* e = reinterpret_cast<float*>(smem + 2 * CH * D * 2);       // [t][h][frame]
+  __shared__ float s_inv[R];
+  const int g = blockIdx.x, f0 = blockIdx.y * FG;
+  const int nf = min(FG, a.frames - f0);
+  const int base = *a.pos + a.pos_offset;  // frame f sees positions [0, base + f]
+  const int len0 = base + f0 + 1;          // row of frame f0 + fl: len0 + fl positions
+  const int lmax = len0 + nf - 1;
+  if (lmax > a.max_len) return;            // beyond the shared-memory rows the host sized (never by design)
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const __half* vsrc = a.v_cache + (size_t)g * a.capacity * D;
+  const int nch = (lmax + CH - 1) / CH;
+  auto stage = [&](int ch) {  // rows [ch CH, min(ch CH + CH, lmax)) into buffer ch & 1
+    const int t0 = ch * CH, n16 = min(CH, lmax - t0) * (D * 2 / 16);
+    const uint4* src = reinterpret_cast<const uint4*>(vsrc + (size_t)t0 * D);
+    uint4* dst = reinterpret_cast<uint4*>(vbuf + (size_t)(ch & 1) * CH * D);
+    for (int i = threadIdx.x; i < n16; i += 128) cp_async16(dst + i, src + i);
+    cp_async_commit();
+  };
+  stage(0);  // lands while the softmax runs
+  for (int r = warp; r < R; r += 4) {
+    const int fl = r >> 1, h = r & 1;
+    if (fl >= nf) continue;
+    const int len = len0 + fl;
+    const float* sc = a.scores + ((size_t)(f0 + fl) * a.heads + 2 * g + h) * a.capacity;
+    float* er = e + h * FG + fl;  // element t at er[t * R]
+    float mx = -INFINITY;
+#pragma unroll 8
+    for (int t = lane; t < len; t += 32) {
+      const float v = sc[t];
+      er[t * R] = v;
+      mx = fmaxf(mx, v);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    for (int t = lane; t < len; t += 32) er[t * R] = exp_ref(__fsub_rn(er[t * R], mx));
+    __syncwarp();
+    const int full = len & ~7;
+    double acc = 0.0;
+    if (lane < 8)
+      for (int t = lane; t < full; t += 8) acc = __dadd_rn(acc, (double)er[t * R]);
+    acc = __dadd_rn(acc, __shfl_down_sync(0xffffffffu, acc, 4));
+    acc = __dadd_rn(acc, __shfl_down_sync(0xffffffffu, acc, 2));
+    acc = __dadd_rn(acc, __shfl_down_sync(0xffffffffu, acc, 1));
+    if (lane == 0) {
+      for (int t = full; t < len; ++t) acc = __dadd_rn(acc, (double)er[t * R]);
+      s_inv[r] = __double2float_rn(__ddiv_rn(1.0, acc));
+    }
+    __syncwarp();
+    const float inv = s_inv[r];
+    for (int t = lane; t < len; t += 32) er[t * R] = __fmul_rn(er[t * R], inv);
+  }
+  // V sums: positions [0, len0) belong to every row, position len0 + i to the
+  // rows of frames fl > i.  Rows past nf accumulate unused values.
+  const int c = threadIdx.x;
+  float acc[2][FG];
+#pragma unroll
+  for (int h = 0; h < 2; ++h)
+#pragma unroll
+    for (int k = 0; k < FG; ++k) acc[h][k] = 0.0f;
+  for (int ch = 0; ch < nch; ++ch) {
+    if (ch + 1 < nch) stage(ch + 1);
+    else cp_async_commit();  // an empty group: the wait below always leaves one group pending
+    cp_async_wait_one();
+    __syncthreads();  // chunk ch (every thread's copies) and, the first time, the probabilities
+    const __half* vb = vbuf + (size_t)(ch & 1) * CH * D + c;
+    const int t0 = ch * CH, n = min(CH, lmax - t0);
+    const int nall = max(0, min(n, len0 - t0));  // rows of this chunk that every frame sees
+    int u = 0;
+    for (; u + 8 <= nall; u += 8) {
+      float v[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) v[k] = __half2float(vb[(u + k) * D]);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const float4 p0 = *reinterpret_cast<const float4*>(e + (t0 + u + k) * R);
+        const float4 p1 = *reinterpret_cast<const float4*>(e + (t0 + u + k) * R + 4);
+        float q[8];
+        mul2(v[k], p0.x, p0.y, q[0], q[1]);
+        mul2(v[k], p0.z, p0.w, q[2], q[3]);
+        mul2(v[k], p1.x, p1.y, q[4], q[5]);
+        mul2(v[k], p1.z, p1.w, q[6], q[7]);
+#pragma unroll
+        for (int i = 0; i < FG; ++i) {
+          acc[0][i] = __fadd_rn(acc[0][i], q[i]);
+          acc[1][i] = __fadd_rn(acc[1][i], q[FG + i]);
+        }
+      }
+    }
+    for (; u < n; ++u) {
+      const int t = t0 + u;
+      const float v = __half2float(vb[u * D]);
+      const int first = t - len0 + 1;  // rows fl >= first contain position t
+#pragma unroll
+      for (int i = 0; i < FG; ++i)
+        if (i >= first) {
+          acc[0][i] = __fadd_rn(acc[0][i], __fmul_rn(v, e[t * R + i]));
+          acc[1][i] = __fadd_rn(acc[1][i], __fmul_rn(v, e[t * R + FG + i]));
+        }
+    }
+    __syncthreads();  // buffer ch & 1 is refilled by stage(ch + 2)
+  }
+#pragma unroll
+  for (int h = 0; h < 2; ++h)
+#pragma unroll
+    for (int fl = 0; fl < FG; ++fl)
+      if (fl < nf) a.attn[(size_t)(f0 + fl) * a.heads * D + (size_t)(2 * g + h) * D + c] = acc[h][fl];
 }
 
 // ------------------------------------------------------------- FP32 ----
@@ -848,6 +995,9 @@ void ensure_gemv_attributes() {
   FA_CUDA(cudaFuncSetAttribute(gemv_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemvMaxSmem));
   FA_CUDA(cudaFuncSetAttribute(gemv_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemvMaxSmem));
   FA_CUDA(cudaFuncSetAttribute(gemv_f32_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemvMaxSmem));
+  FA_CUDA(cudaFuncSetAttribute(attn_softmax_v_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemvMaxSmem));
+  FA_CUDA(cudaFuncSetAttribute(attn_softmax_v_group_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               kGemvMaxSmem));
   done[dev] = ctx;
 }
 
@@ -953,8 +1103,16 @@ void launch_attention(const AttnArgs& a, cudaStream_t stream) {
       attn_scores_kernel<<<g1, 256, 0, stream>>>(a);
     }
     FA_CUDA(cudaGetLastError());
-    dim3 g2(a.frames, a.heads);
-    attn_softmax_v_kernel<<<g2, 128, (size_t)a.capacity * 4, stream>>>(a);
+    const size_t group_smem = a.max_len > 0 ? softmax_v_group_smem(a.max_len) : 0;
+    if (a.frames >= kSvFrames && a.max_len > 0 && a.skip == nullptr && group_smem <= (size_t)kGemvMaxSmem) {
+      // prefill: kSvFrames frames x both heads of a KV head per CTA, one V read for all of them
+      ensure_gemv_attributes();
+      dim3 g2(a.kv_heads, (a.frames + kSvFrames - 1) / kSvFrames);
+      attn_softmax_v_group_kernel<<<g2, 128, group_smem, stream>>>(a);
+    } else {
+      dim3 g2(a.frames, a.heads);
+      attn_softmax_v_kernel<<<g2, 128, (size_t)a.capacity * 4, stream>>>(a);
+    }
     FA_CUDA(cudaGetLastError());
     return;
   }

@@ -579,9 +579,12 @@ __device__ __forceinline__ bool phase_weights(Ctx& c, int nt, int per) {
 // One projection phase over this CTA's nt tiles of K columns, streamed in ring
 // pieces of `per` tiles (acquired by phase_weights; `ready` is its result).
 // epi(t, r, sum) runs in the lanes that hold the sum of row r of tile t.
-// False when the kernel aborts.
+// Opens with a barrier, which also publishes the activations the caller just
+// wrote to shared memory.  sync_after: close with a barrier (needed when the
+// next writer of xq/xs/part comes before any other barrier).  False when the
+// kernel aborts.
 template <int K, typename Epi>
-__device__ __forceinline__ bool w8a8_phase(Ctx& c, int nt, int per, bool ready, Epi epi) {
+__device__ __forceinline__ bool w8a8_phase(Ctx& c, int nt, int per, bool ready, bool sync_after, Epi epi) {
   constexpr int NS = K / 1024, TB = 8 * K + (K / 32) * 16;
   const int np = (nt + per - 1) / per;
   // Every warp takes the same branch: the jobs below wait on each other at
@@ -596,7 +599,7 @@ __device__ __forceinline__ bool w8a8_phase(Ctx& c, int nt, int per, bool ready, 
   }
   for (int p = 0; p < np; ++p) ring_release(ring_w(), c.nw + p, c.lane);
   c.nw += np;
-  csync();  // the next phase rewrites xq/xs and part
+  if (sync_after) csync();
   return true;
 }
 
@@ -619,6 +622,8 @@ __device__ __forceinline__ void publish_block(unsigned long long* dst, int n, in
 // gate/up blocks), and unpaced polls of the same few lines slow the stores
 // and copies the other CTAs make meanwhile (400 ns measured best on B200:
 // -7 % per step against the unpaced wait; 100-200 and 800-1600 slower).
+// The caller's next barrier publishes the shared-memory writes: a projection
+// phase's opening barrier (w8a8_phase) when it follows directly.
 template <int POLL_NS = 0>
 __device__ __forceinline__ void gather_q8(Ctx& c, const unsigned long long* src, int n, unsigned tag) {
   const int total = n / 4 + n / 32;  // <= 2 * CTHREADS
@@ -652,7 +657,6 @@ __device__ __forceinline__ void gather_q8(Ctx& c, const unsigned long long* src,
       }
     }
   }
-  csync();
 }
 
 // This thread's RMSNorm weights in norm_quant's block mapping (block
@@ -743,7 +747,10 @@ __device__ __forceinline__ void quant_regs(Ctx& c, const float (&y)[NW], int K) 
 // RMSNorm(v) * gamma then quantisation (K = W), v in gather's mapping.  The
 // sum of squares runs over this thread's elements tid, tid + 480, ... in
 // order, then over the warps in order.  keep: optional shared copy of v.
-__device__ __forceinline__ void norm_quant(Ctx& c, const float (&v)[3], const Gamma& gamma, float eps, float* keep) {
+// sync: end with a barrier (false when a projection phase's opening barrier
+// follows directly).
+__device__ __forceinline__ void norm_quant(Ctx& c, const float (&v)[3], const Gamma& gamma, float eps, float* keep,
+                                           bool sync) {
   double part = 0.0;
 #pragma unroll
   for (int k = 0; k < 3; ++k)
@@ -762,7 +769,7 @@ __device__ __forceinline__ void norm_quant(Ctx& c, const float (&v)[3], const Ga
 #pragma unroll
   for (int k = 0; k < 3; ++k) y[k] = __fmul_rn(__fmul_rn(v[k], inv), gamma.g[k]);
   quant_regs<3>(c, y, W);
-  csync();
+  if (sync) csync();
 }
 
 // RMSNorm of one 128-wide head held by 4 warps (warp0..warp0+3) in place, g
@@ -1216,7 +1223,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(const Mega
           for (int k = 0; k < 3; ++k) v[k] = c.tid + k * CTHREADS < W ? c.xres()[c.tid + k * CTHREADS] : 0.0f;
         }
         MEGA_TRACE(ev + 0);
-        norm_quant(c, v, load_gamma(c, s_attn), A.eps, layer > 0 ? c.xres() : nullptr);
+        norm_quant(c, v, load_gamma(c, s_attn), A.eps, layer > 0 ? c.xres() : nullptr, false);
       }
       MEGA_TRACE(ev + 1);
       {
@@ -1224,7 +1231,8 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(const Mega
         const int q0 = sp.q0;
         // Failure-path test hook: the named CTA leaves its first q/k/v rows unpublished.
         const bool hold = A.withhold == (int)blockIdx.x && step == 0 && layer == 0;
-        if (!w8a8_phase<W>(c, sp.qn, 3, wq, [&](int t, int r, float v) {
+        // closing barrier: the O phase's gather writes xq/xs next
+        if (!w8a8_phase<W>(c, sp.qn, 3, wq, true, [&](int t, int r, float v) {
               if (!hold) st_word(A.qkv_t + (q0 + t) * 8 + r, pack(v, tag));
             }))
           goto drain;
@@ -1247,7 +1255,8 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(const Mega
         MEGA_TRACE(ev + 4);
         const unsigned tag = tl + kTagA;
         const int o0 = sp.o0;
-        if (!w8a8_phase<QW>(c, sp.on, 1, wo, [&](int t, int r, float v) {
+        // no closing barrier: the GU phase's norm_quant has one before it writes xq/xs
+        if (!w8a8_phase<QW>(c, sp.on, 1, wo, false, [&](int t, int r, float v) {
               const int row = (o0 + t) * 8 + r;
               st_word(A.a_t + row, pack(__fadd_rn(v, c.xres()[row]), tag));
             }))
@@ -1262,7 +1271,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(const Mega
         gather<3>(c, A.a_t, W, tl + kTagA, v);
         MEGA_TRACE(ev + 8);
         if (sp.gbn > 0) {
-          norm_quant(c, v, load_gamma(c, s_ffn), A.eps, c.ares());
+          norm_quant(c, v, load_gamma(c, s_ffn), A.eps, c.ares(), false);
         } else {  // no gate/up block here: keep a for the down projection's residual
 #pragma unroll
           for (int k = 0; k < 3; ++k)
@@ -1274,7 +1283,8 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(const Mega
       for (int bj = 0; bj < sp.gbn; ++bj) {
         c.wait_ev = -1;
         const bool ready = bj == 0 ? wg : phase_weights(c, 8, 3);
-        if (!w8a8_phase<W>(c, 8, 3, ready, [&](int t, int r, float v) { c.part()[t * 8 + r] = v; })) goto drain;
+        // closing barrier: warp 0 reads part next
+        if (!w8a8_phase<W>(c, 8, 3, ready, true, [&](int t, int r, float v) { c.part()[t * 8 + r] = v; })) goto drain;
         if (warp == 0) {  // lane = 8 * pair + row: the block's 32 SiLU(gate) * up values
           const float act = silu_mul1(c.part()[(lane >> 3) * 16 + (lane & 7)], c.part()[(lane >> 3) * 16 + 8 + (lane & 7)]);
           publish_block(A.act_t, FFN, sp.gb0 + bj, act, tl + kTagAct, lane);
@@ -1290,7 +1300,8 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(const Mega
         MEGA_TRACE(ev + 12);
         const unsigned tag = tl + kTagX;
         const int d0 = sp.d0;
-        if (!w8a8_phase<FFN>(c, sp.dn, 1, wd, [&](int t, int r, float v) {
+        // no closing barrier: the next Q (or LM) norm_quant has one before it writes xq/xs
+        if (!w8a8_phase<FFN>(c, sp.dn, 1, wd, false, [&](int t, int r, float v) {
               const int row = (d0 + t) * 8 + r;
               st_word(A.x_t + row, pack(__fadd_rn(v, c.ares()[row]), tag));
             }))
@@ -1310,7 +1321,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(const Mega
           float v[3];
           gather<3>(c, A.x_t, W, tlm - 8 + kTagX, v);
           MEGA_TRACE(ev + 0);
-          norm_quant(c, v, load_gamma(c, s_out), A.eps, nullptr);
+          norm_quant(c, v, load_gamma(c, s_out), A.eps, nullptr, true);
         }
         MEGA_TRACE(ev + 1);
         // Rounds of 15 tiles (5 ring pieces of 3 tiles), one tile per warp,

@@ -35,7 +35,7 @@ static void mbox_post(fa_session* s, int token);
 namespace {
 
 constexpr int kMaxChunkFrames = 256;  // prefill frames per layer sequence (one weight pass each)
-constexpr int kAttnChunkFrames = 64;  // frames per attention launch (its scores / partials buffers)
+constexpr int kAttnChunkFrames = 256;  // frames per attention launch (its scores / partials buffers)
 constexpr int kAttnSplits = 16;       // split-K CTAs per (frame, KV head)
 constexpr int kBmmMinFrames = 16;     // frames from which projections run on the tensor cores
 constexpr int kSessionInts = 128;     // device words of a session
