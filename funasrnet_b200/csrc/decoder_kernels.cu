@@ -554,14 +554,25 @@ __global__ void __launch_bounds__(256) attn_scores_kernel(const AttnArgs a) {
   }
 }
 
+// Two IEEE products a0 * b0 and a1 * b1 in one instruction (each rounded as
+// __fmul_rn); the sums that consume them stay scalar adds.
+__device__ __forceinline__ void mul2pair(float a0, float b0, float a1, float b1, float& r0, float& r1) {
+  unsigned long long x, y, z;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(x) : "f"(a0), "f"(a1));
+  asm("mov.b64 %0, {%1, %2};" : "=l"(y) : "f"(b0), "f"(b1));
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(z) : "l"(x), "l"(y));
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(r0), "=f"(r1) : "l"(z));
+}
+
 // The same scores for a prefill launch whose length bound the host knows:
 // grid (kv_heads, position blocks of 32, frame groups of 8), 256 threads
 // (8 per position).  A thread loads its lane's 16 K values of one position
 // once and forms the dots of all 8 frames x 2 query heads of its group with
 // them; each dot keeps the 8-lane order and fold of attn_scores_kernel.
 __global__ void __launch_bounds__(256) attn_scores_block_kernel(const AttnArgs a) {
-  constexpr int D = 128, M = D / 8, FG = 8;
-  __shared__ float qs[2 * FG][D];
+  constexpr int D = 128, M = D / 8, FG = 8, QS = M + 4;  // QS: lane j's 16 q values, padded (no bank conflicts)
+  // qs[p][j][i] = q_p[j + 8 i]: lane j reads its 16 values as four 16-byte loads
+  __shared__ __align__(16) float qs[2 * FG][8][QS];
   const int g = blockIdx.x, t = blockIdx.y * 32 + (threadIdx.x >> 3), f0 = blockIdx.z * FG;
   const int j = threadIdx.x & 7;
   const int qw = a.heads * D, kvw = a.kv_heads * D;
@@ -571,7 +582,8 @@ __global__ void __launch_bounds__(256) attn_scores_block_kernel(const AttnArgs a
   if (blockIdx.y * 32 >= base + f0 + nf) return;  // a position block no frame of the group sees (causal)
   for (int i = threadIdx.x; i < 2 * FG * D; i += 256) {
     const int p = i / D, c = i - p * D;
-    qs[p][c] = p < 2 * nf ? a.qkv[(size_t)(f0 + (p >> 1)) * stride + (size_t)(2 * g + (p & 1)) * D + c] : 0.0f;
+    qs[p][c & 7][c >> 3] =
+        p < 2 * nf ? a.qkv[(size_t)(f0 + (p >> 1)) * stride + (size_t)(2 * g + (p & 1)) * D + c] : 0.0f;
   }
   __syncthreads();
   float k[M];
@@ -588,10 +600,17 @@ __global__ void __launch_bounds__(256) attn_scores_block_kernel(const AttnArgs a
   }
   const float divisor = __fsqrt_rn((float)D);
   for (int p = 0; p < 2 * nf; ++p) {  // block-uniform: every lane takes part in the folds
-    const float* q = qs[p];
-    float acc = 0.0f;
+    const float4* q4 = reinterpret_cast<const float4*>(qs[p][j]);
+    float prod[M];
 #pragma unroll
-    for (int i = 0; i < M; ++i) acc = __fadd_rn(acc, __fmul_rn(q[j + 8 * i], k[i]));
+    for (int i4 = 0; i4 < M / 4; ++i4) {
+      const float4 q = q4[i4];
+      mul2pair(q.x, k[4 * i4], q.y, k[4 * i4 + 1], prod[4 * i4], prod[4 * i4 + 1]);
+      mul2pair(q.z, k[4 * i4 + 2], q.w, k[4 * i4 + 3], prod[4 * i4 + 2], prod[4 * i4 + 3]);
+    }
+    float acc = 0.0f;  // lane j's channels j, j + 8, ... in order
+#pragma unroll
+    for (int i = 0; i < M; ++i) acc = __fadd_rn(acc, prod[i]);
     acc = __fadd_rn(acc, __shfl_down_sync(0xffffffffu, acc, 4));
     acc = __fadd_rn(acc, __shfl_down_sync(0xffffffffu, acc, 1));
     acc = __fadd_rn(acc, __shfl_down_sync(0xffffffffu, acc, 2));
