@@ -616,7 +616,7 @@ def main():
     }
     line["prefill"] = {"frames": frames, "ms": prefill_s * 1e3, "frames_per_s": frames / prefill_s,
                        "h2d_bytes": frames * cm.width * 4,
-                       "path": "fa_session_decode: chunks of 256 frames (projections on the tcgen05 kernel), attention in launches of 64 frames"}
+                       "path": "fa_session_decode: chunks of up to 512 frames (projections on the tcgen05 kernel, one weight pass per chunk), attention in launches of up to 512 frames"}
     if lm_ms:
         a = lm_bytes / (lm_ms * 1e-3) / 1e9
         line["gemv_lm_head"] = {"ms": lm_ms, "bytes": lm_bytes, "achieved": a, "frac": a / peak}

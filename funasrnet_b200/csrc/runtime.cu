@@ -34,8 +34,9 @@ static void mbox_post(fa_session* s, int token);
 
 namespace {
 
-constexpr int kMaxChunkFrames = 256;  // prefill frames per layer sequence (one weight pass each)
-constexpr int kAttnChunkFrames = 256;  // frames per attention launch (its scores / partials buffers)
+constexpr int kMaxChunkFrames = 512;  // prefill frames per layer sequence (one weight pass each)
+constexpr int kAttnChunkFrames = 512;      // frames per exact attention launch (its scores buffer)
+constexpr int kAttnSplitChunkFrames = 64;  // frames per split-K attention launch (its partials buffer)
 constexpr int kAttnSplits = 16;       // split-K CTAs per (frame, KV head)
 constexpr int kBmmMinFrames = 16;     // frames from which projections run on the tensor cores
 constexpr int kSessionInts = 128;     // device words of a session
@@ -1050,14 +1051,16 @@ AttnArgs attn_args(fa_session* s, int layer, int frames, const int* skip) {
 }
 
 // QK-norm + RoPE + KV write and attention of `frames` frames of layer l, in
-// launches of at most kAttnChunkFrames frames (the scores and partials buffers
-// hold that many); each launch's frames follow the previous launch's in the
-// KV cache, so the causal order is kept.
+// launches of at most kAttnChunkFrames frames (kAttnSplitChunkFrames in the
+// split-K mode: the scores and partials buffers hold that many); each
+// launch's frames follow the previous launch's in the KV cache, so the causal
+// order is kept.
 void enqueue_attention(fa_session* s, int l, int frames, const int* skip) {
   fa_model* m = s->m;
   const int qw = m->heads * m->head_size, kvw = m->kv_heads * m->head_size;
-  for (int f0 = 0; f0 < frames; f0 += kAttnChunkFrames) {
-    const int n = std::min(kAttnChunkFrames, frames - f0);
+  const int chunk = s->exact_attention ? std::min(kAttnChunkFrames, m->capacity) : kAttnSplitChunkFrames;
+  for (int f0 = 0; f0 < frames; f0 += chunk) {
+    const int n = std::min(chunk, frames - f0);
     AttnArgs a = attn_args(s, l, n, skip);
     a.qkv += (size_t)f0 * (qw + 2 * kvw);
     a.attn += (size_t)f0 * qw;
@@ -1359,8 +1362,8 @@ int fa_session_create(fa_model* m, fa_session** out) {
     s->attn.ensure((size_t)F * qw * 4);
     s->act.ensure((size_t)F * m->ffn * 4);
     if (!m->quantized) s->gu.ensure((size_t)F * 2 * m->ffn * 4);
-    s->part.ensure((size_t)kAttnChunkFrames * m->kv_heads * kAttnSplits * (4 + 2 * D) * 4);
-    s->scores.ensure((size_t)kAttnChunkFrames * m->heads * m->capacity * 4);
+    s->part.ensure((size_t)kAttnSplitChunkFrames * m->kv_heads * kAttnSplits * (4 + 2 * D) * 4);
+    s->scores.ensure((size_t)std::min(kAttnChunkFrames, m->capacity) * m->heads * m->capacity * 4);
     s->logits.ensure((size_t)m->vocab * 4);
     const int lm_ctas = (m->vocab + kTileRows - 1) / kTileRows;
     s->am_val.ensure((size_t)lm_ctas * 4);
