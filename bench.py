@@ -197,13 +197,14 @@ def source_digest() -> str:
 
 # DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) of the persistent
 # kernel on the bs1_400 workload, from one `ncu` capture of the bench's first
-# 3-step launch (positions 408..410): 2,046,384,128 bytes, 682.13 MB per step
-# against 680.52 MB algorithmic, keyed by the digest of mega.cu it was captured
-# on.  The bench reports traffic = that ratio x its own algorithmic bytes per
-# step (the KV share grows with the position in proportion); when the source
-# differs it reports null (not measured on this build).
-MEASURED_TRAFFIC = {"bs1_400": {"traffic_over_algorithmic": 682.128e6 / 680.519e6,
-                                "mega_cu_sha256_16": "f6b97a0e32ca46f8", "captured": "2026-12-02"}}
+# 3-step launch (positions 408..410): 2,060,064,256 + 25,017,344 bytes, 695.03 MB
+# per step against 680.52 MB algorithmic (the writes include dirty L2 lines the
+# preceding prefill left), keyed by the digest of mega.cu it was captured on.
+# The bench reports traffic = that ratio x its own algorithmic bytes per step
+# (the KV share grows with the position in proportion); when the source differs
+# it reports null (not measured on this build).
+MEASURED_TRAFFIC = {"bs1_400": {"traffic_over_algorithmic": 695.027e6 / 680.519e6,
+                                "mega_cu_sha256_16": "be93d9610d431463", "captured": "2026-12-02"}}
 
 
 def profile_range(on: bool):
