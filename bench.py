@@ -197,14 +197,13 @@ def source_digest() -> str:
 
 # DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) of the persistent
 # kernel on the bs1_400 workload, from one `ncu` capture of the bench's first
-# 3-step launch (positions 408..410): 2,060,064,256 + 25,017,344 bytes, 695.03 MB
-# per step against 680.52 MB algorithmic (the writes include dirty L2 lines the
-# preceding prefill left), keyed by the digest of mega.cu it was captured on.
-# The bench reports traffic = that ratio x its own algorithmic bytes per step
-# (the KV share grows with the position in proportion); when the source differs
-# it reports null (not measured on this build).
-MEASURED_TRAFFIC = {"bs1_400": {"traffic_over_algorithmic": 695.027e6 / 680.519e6,
-                                "mega_cu_sha256_16": "be93d9610d431463", "captured": "2026-12-02"}}
+# 3-step launch (positions 408..410): 2,042,037,760 + 3,902,976 bytes, 681.98 MB
+# per step against 680.52 MB algorithmic, keyed by the digest of mega.cu it was
+# captured on.  The bench reports traffic = that ratio x its own algorithmic
+# bytes per step (the KV share grows with the position in proportion); when the
+# source differs it reports null (not measured on this build).
+MEASURED_TRAFFIC = {"bs1_400": {"traffic_over_algorithmic": 681.980e6 / 680.519e6,
+                                "mega_cu_sha256_16": "4f557952b6deb048", "captured": "2026-12-02"}}
 
 
 def profile_range(on: bool):
@@ -294,6 +293,7 @@ PHASES = (  # (name, (CTA set, event) at the phase's end, (CTA set, event) at it
     ("Q norm + quantise", ("g", 1), ("g", 0)),
     ("Q/K/V GEMV", ("g", 3), ("g", 1)),
     ("q/k/v hand-off", ("a", 1), ("g", 3)),
+    ("score assist (GEMV CTAs)", ("g", 5), ("g", 3)),
     ("attn QK-norm, RoPE, KV write", ("a", 2), ("a", 1)),
     ("attn scores", ("a", 3), ("a", 2)),
     ("attn softmax", ("a", 4), ("a", 3)),
@@ -366,7 +366,7 @@ def phase_table(be, path, reps=5, steps=4):
         print(f"{name:34s} {np.nanmedian(v):10.0f} {np.nanpercentile(v, 90):8.0f}")
     c = np.concatenate(cyc)  # [layers x attention CTAs, 4] SM cycles
     print(f"{'attention CTA, SM cycles per layer':34s} {'median':>10s} {'p90':>8s}")
-    for k, name in enumerate(("waiting for K chunks", "waiting for V chunks", "score loop", "V loop")):
+    for k, name in enumerate(("waiting for assisted scores", "waiting for V chunks", "scores gathered", "V loop")):
         print(f"{name:34s} {np.median(c[:, k]):10.0f} {np.percentile(c[:, k], 90):8.0f}")
     gw, gc = np.concatenate(gcyc[0::2]), np.concatenate(gcyc[1::2])  # [layers x GEMV CTAs, 4 phases]
     print(f"{'GEMV CTA, per layer':34s} {'median':>10s} {'p90':>8s}")

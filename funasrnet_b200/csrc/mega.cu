@@ -8,16 +8,18 @@
 //   GEMV CTAs stream their static share of every projection: contiguous runs
 //   of 8-row weight tiles, through a 7-slot ring, phase after phase, layer
 //   after layer, then their share of the lm_head.
-//   Attention CTAs stream their KV head's history, each layer's K chunks and
-//   then its V chunks (60 positions each), through one 11-slot ring in the
-//   order they are consumed: the V chunks a layer's start cannot hold are
-//   requested while its scores run, the next layer's K while its V sum runs.
-//   The history does not depend on the current token.
+//   Attention CTAs stream their KV head's V history (chunks of 60 positions)
+//   through one 11-slot ring, layer after layer; the history does not depend
+//   on the current token.  The K history is scored by the GEMV CTAs while the
+//   attention runs (score_assist): each loads the K rows of its positions from
+//   the cache before the queries arrive, dots them with every head's query in
+//   the reference's 8-lane order and publishes the raw dots as tagged words.
 //
 // Phases of one step (QwenDecoder.Decode, QwenDecoder.cs:180-268):
 //   embed (each GEMV CTA computes the token's row itself)
 //   per layer: Q  RMSNorm + quantise x, q/k/v rows                  GEMV CTAs
 //              A  QK-norm, RoPE, F16 KV write, exact attention       attention CTAs
+//                 (the history's q.k dots: score_assist)             GEMV CTAs
 //              O  quantise attention output, o rows + residual       GEMV CTAs
 //              GU RMSNorm + quantise a, gate/up rows, SiLU*up        GEMV CTAs
 //              D  quantise act, down rows + residual                 GEMV CTAs
@@ -62,7 +64,7 @@ constexpr int TB_F = 8 * FFN + (FFN / 32) * 16;  // 26112: K = 3072
 constexpr int WSLOTS = 7, WSLOT = TB_F;          // weight ring: 3 K=1024 tiles or 1 K=3072 tile per slot
 constexpr int CHUNK = 60;                        // KV positions per attention chunk (8 threads each)
 constexpr int CSLOT = CHUNK * D * 2;             // 15360 bytes
-constexpr int ASLOTS = 11;                       // attention ring: K then V chunks of each layer
+constexpr int ASLOTS = 11;                       // attention ring: V chunks of each layer
 constexpr int ATT_CTAS = H;
 constexpr unsigned kWaitLimit = 1u << 22;
 
@@ -70,7 +72,7 @@ static_assert(ASLOTS * CSLOT <= WSLOTS * WSLOT, "the attention ring shares the w
 static_assert(2 * WSLOTS <= 16 && 16 + 2 * ASLOTS <= 48, "disjoint mbarrier ranges");
 
 
-enum { kTagQkv = 1, kTagAttn = 2, kTagA = 3, kTagAct = 4, kTagX = 5, kTagPart = 6 };
+enum { kTagSc = 0, kTagQkv = 1, kTagAttn = 2, kTagA = 3, kTagAct = 4, kTagX = 5, kTagPart = 6, kTagQh = 7 };
 enum { kErrWaitData = 1, kErrWaitFull = 2, kErrWaitEmpty = 3, kErrWaitGo = 4, kErrWaitDrain = 5, kErrWaitWindow = 6 };
 
 struct Spans {
@@ -113,7 +115,8 @@ constexpr int kOffGAttn = kOffAres + W * 4;                        // attn_norm 
 constexpr int kOffGFfn = kOffGAttn + W * 4;                        // ffn_norm of the coming GU phase
 constexpr int kOffGOut = kOffGFfn + W * 4;                         // output norm
 constexpr int kOffPart = kOffGOut + W * 4;                         // row sums crossing warps [32 x 8]
-constexpr int kGemvEnd = kOffPart + 32 * 8 * 4;
+constexpr int kOffQh = kOffPart + 32 * 8 * 4;                      // every head's query (score assist)
+constexpr int kGemvEnd = kOffQh + H * D * 4;
 // Attention CTAs: the score row of the query head.
 constexpr int kOffScores = kOffRole;                               // [capacity]
 
@@ -459,14 +462,13 @@ __device__ void producer_attention(const MegaArgs& A, const Ring& ar, Shared* sh
     __threadfence();
     asm volatile("fence.proxy.async.global;" ::: "memory");
     const int pos = pos0 + step, chunks = (pos + CHUNK - 1) / CHUNK;
-    for (int l = 0; l < A.n_layers; ++l)
-      for (int kv = 0; kv < 2; ++kv) {
-        const __half* cache = (kv == 0 ? A.k_cache : A.v_cache) + (((size_t)l * KH + g) * A.capacity) * D;
-        for (int ch = 0; ch < chunks; ++ch)
-          if (!ring_issue(ar, n, cache + (size_t)ch * CHUNK * D, (unsigned)(min(CHUNK, pos - ch * CHUNK) * D * 2), sh,
-                          A.ctrl))
-            return;
-      }
+    for (int l = 0; l < A.n_layers; ++l) {  // V only: the GEMV CTAs score the K history (score_assist)
+      const __half* cache = A.v_cache + (((size_t)l * KH + g) * A.capacity) * D;
+      for (int ch = 0; ch < chunks; ++ch)
+        if (!ring_issue(ar, n, cache + (size_t)ch * CHUNK * D, (unsigned)(min(CHUNK, pos - ch * CHUNK) * D * 2), sh,
+                        A.ctrl))
+          return;
+    }
   }
 }
 
@@ -484,6 +486,7 @@ struct Ctx {
   __device__ float* xres() const { return sm<float>(kOffXres); }
   __device__ float* ares() const { return sm<float>(kOffAres); }
   __device__ float* part() const { return sm<float>(kOffPart); }
+  __device__ float* qh() const { return sm<float>(kOffQh); }
   __device__ float* aq() const { return sm<float>(kOffAttQ); }
   __device__ float* ak() const { return sm<float>(kOffAttK); }
   __device__ float* av() const { return sm<float>(kOffAttV); }
@@ -807,20 +810,8 @@ __device__ __forceinline__ void head_rope(Ctx& c, float* v, float co, float si, 
 __device__ __noinline__ int attention(Ctx c, int layer, int pos, unsigned tag_in, unsigned tag_out, float co, float si) {
   const MegaArgs& A = *c.A;
   const int h = blockIdx.x, g = h >> 1;
-  const int chunks = (pos + CHUNK - 1) / CHUNK;
+  const int chunks = (pos + CHUNK - 1) / CHUNK;  // V chunks of the history
   const bool timed = c.trace != nullptr;  // wait and loop cycles for the trace
-  // When the layer's K chunks fit in the ring together they are all issued by
-  // now (the previous layer's V loop released their slots): probe them here,
-  // where the probes (a few hundred cycles each) overlap the wait for q/k/v,
-  // instead of one per chunk in the score loop.
-  const bool whole_k = chunks <= ASLOTS;
-  long long kwait = 0;
-  bool failed = false;
-  if (whole_k) {
-    const long long k0 = timed ? clock64() : 0;
-    failed = !ring_acquire_all(ring_a(), c.na, chunks, c.sh(), A.ctrl);
-    if (timed) kwait = clock64() - k0;
-  }
   // norm weight of this thread's q (warps 0..3) or k (warps 4..7) channel,
   // requested before the wait for q/k/v
   float gn = 0.0f;
@@ -844,6 +835,8 @@ __device__ __noinline__ int attention(Ctx c, int layer, int pos, unsigned tag_in
     head_rope(c, c.ak(), co, si, 4, 3);
   }
   csync();
+  // The query goes to the GEMV CTAs, which score the history positions with it.
+  if (c.tid < D) st_word(A.q_t + h * D + c.tid, pack(c.aq()[c.tid], tag_in - kTagQkv + kTagQh));
   const size_t head_off = (((size_t)layer * KH + g) * A.capacity) * D;
   if (c.tid < D) {  // binary16 rounding of k and v (QwenDecoder.cs:199-200)
     const __half kh = __float2half_rn(c.ak()[c.tid]);
@@ -857,47 +850,23 @@ __device__ __noinline__ int attention(Ctx c, int layer, int pos, unsigned tag_in
   }
   csync();
   if (c.trace && c.tid == 0) c.trace[kTraceLayerEvents * layer + 2] = global_ns();
-  // Scores: one position per 8 threads, lane j sums channels j, j+8, ... in order.
+  // Scores: the GEMV CTAs' raw dots of positions [0, pos) (score_assist, the
+  // same 8-lane order), gathered here; position pos from the fresh k below.
   const int j = c.lane & 7, slot = c.tid >> 3;
   float qj[D / 8];
 #pragma unroll
   for (int i = 0; i < D / 8; ++i) qj[i] = c.aq()[j + 8 * i];
   const long long s0 = timed ? clock64() : 0;
-  for (int ch = 0; ch < chunks; ++ch) {
-    const uint8_t* kb = nullptr;
-    if (whole_k) {
-      if (!failed) kb = ring_a().base + (size_t)(c.na % ASLOTS) * CSLOT;
-    } else {
-      const long long k0 = timed ? clock64() : 0;
-      kb = failed ? nullptr : ring_acquire(ring_a(), c.na, c.sh(), A.ctrl);
-      if (timed) kwait += clock64() - k0;
+  {
+    const unsigned tag_sc = tag_in - kTagQkv + kTagSc;
+    const unsigned long long* src = A.sc_t + (size_t)h * A.capacity;
+    for (int t = c.tid; t < pos; t += CTHREADS) {
+      float v;
+      if (!wait_word(src + t, tag_sc, v, c.sh(), A.ctrl)) break;
+      c.sc()[t] = v;  // raw dot: divided by sqrt(D) in the softmax pass
     }
-    if (kb == nullptr) {  // abort: stop consuming; all warps leave together below
-      failed = true;
-      continue;
-    }
-    const int t = ch * CHUNK + slot;
-    float acc = 0.0f;
-    if (t < pos) {
-      // lane j's channels j, j+8, ... are contiguous in the lane-permuted row
-      const __half2* kr = reinterpret_cast<const __half2*>(kb + (size_t)slot * D * 2 + j * (D / 8) * 2);
-      __half2 kh[D / 16];
-#pragma unroll
-      for (int i = 0; i < D / 16; ++i) kh[i] = kr[i];
-#pragma unroll
-      for (int i = 0; i < D / 16; ++i) {
-        const float2 kv = __half22float2(kh[i]);
-        acc = __fadd_rn(acc, __fmul_rn(qj[2 * i], kv.x));
-        acc = __fadd_rn(acc, __fmul_rn(qj[2 * i + 1], kv.y));
-      }
-    }
-    acc = __fadd_rn(acc, __shfl_down_sync(0xffffffffu, acc, 4));
-    acc = __fadd_rn(acc, __shfl_down_sync(0xffffffffu, acc, 1));
-    acc = __fadd_rn(acc, __shfl_down_sync(0xffffffffu, acc, 2));
-    if (j == 0 && t < pos) c.sc()[t] = acc;  // raw dot: divided by sqrt(D) in the softmax pass
-    ring_release(ring_a(), c.na, c.lane);
-    ++c.na;
   }
+  const long long kwait = timed ? clock64() - s0 : 0;
   if (c.warp == 0) {  // position pos from the fresh k
     float acc = 0.0f;
     if (slot == 0) {
@@ -1042,20 +1011,106 @@ __device__ __noinline__ int attention(Ctx c, int layer, int pos, unsigned tag_in
   return c.na + chunks;
 }
 
+// Score assist (GEMV CTA i of n, while the attention CTAs run): the raw q.k
+// dots of positions t = i, i + n, ... < pos for every query head, each in the
+// reference's order (TensorMath.AttentionAvx.cs: lane j of 8 sums channels
+// j, j+8, ... in order, the lanes fold as +4, +1, +2), published as tagged
+// words for the attention CTAs.  Eight threads per dot; the K rows of the
+// first round are loaded before the queries arrive (the history was written
+// by earlier steps).  On an abort the waits give up and the CTA runs on.
+__device__ __forceinline__ void score_assist(Ctx& c, int layer, int pos, int i, int n, unsigned tag_q, unsigned tag_sc) {
+  const MegaArgs& A = *c.A;
+  constexpr int GROUPS = CTHREADS / 8;  // dots per round
+  const int j = c.tid & 7, grp = c.tid >> 3;
+  const int npos = pos > i ? (pos - i + n - 1) / n : 0;
+  const int dots = npos * H, rounds = (dots + GROUPS - 1) / GROUPS;
+  auto k_row = [&](int d, uint4& ka, uint4& kb) {  // lane j's 16 K values of dot d
+    const int m = d / H, h = d - m * H, t = i + m * n;
+    const uint4* kr = reinterpret_cast<const uint4*>(
+        A.k_cache + (((size_t)layer * KH + (h >> 1)) * A.capacity + t) * D + j * (D / 8));
+    ka = kr[0];
+    kb = kr[1];
+  };
+  // the K rows of the first two rounds (all of them up to 8 n positions) in
+  // flight while the queries are awaited
+  uint4 ka = make_uint4(0, 0, 0, 0), kb = ka, ka1 = ka, kb1 = ka;
+  if (grp < dots) k_row(grp, ka, kb);
+  if (GROUPS + grp < dots) k_row(GROUPS + grp, ka1, kb1);
+  // Every head's query: this thread's five words polled together, passes
+  // paced by 100 ns (the queries come about a microsecond after this CTA gets
+  // here; unpaced polls of 132 CTAs would slow the copies around them, and
+  // 100 ns measured faster than 400 ns).
+  constexpr int QW_PER = (H * D + CTHREADS - 1) / CTHREADS;
+  unsigned pending = 0;
+#pragma unroll
+  for (int k = 0; k < QW_PER; ++k)
+    if (c.tid + k * CTHREADS < H * D) pending |= 1u << k;
+  for (unsigned it = 0; pending != 0; ++it) {
+    unsigned long long w[QW_PER];
+#pragma unroll
+    for (int k = 0; k < QW_PER; ++k) w[k] = (pending >> k) & 1u ? ld_word(A.q_t + c.tid + k * CTHREADS) : 0ull;
+#pragma unroll
+    for (int k = 0; k < QW_PER; ++k)
+      if (((pending >> k) & 1u) && (unsigned)(w[k] >> 32) == tag_q) {
+        c.qh()[c.tid + k * CTHREADS] = __uint_as_float((unsigned)w[k]);
+        pending &= ~(1u << k);
+      }
+    if (pending == 0) break;
+    __nanosleep(100);
+    if ((it & 255) == 255) {
+      if (c.sh()->abort || ld_flag(&A.ctrl->error)) {
+        c.sh()->abort = 1;
+        break;
+      }
+      if (it > c.sh()->wait_limit) {
+        raise_error(c.sh(), A.ctrl, kErrWaitData);
+        break;
+      }
+    }
+  }
+  csync();
+  for (int r = 0; r < rounds; ++r) {  // CTA-uniform: every lane takes part in the folds
+    const int d = r * GROUPS + grp;
+    const bool valid = d < dots;
+    if (r == 1) {
+      ka = ka1;
+      kb = kb1;
+    } else if (r > 1 && valid) {
+      k_row(d, ka, kb);
+    }
+    const int m = valid ? d / H : 0, h = valid ? d - m * H : 0;
+    const float* q = c.qh() + h * D + j;
+    const __half* k0 = reinterpret_cast<const __half*>(&ka);
+    const __half* k1 = reinterpret_cast<const __half*>(&kb);
+    float acc = 0.0f;
+#pragma unroll
+    for (int s = 0; s < D / 8; ++s)
+      acc = __fadd_rn(acc, __fmul_rn(q[8 * s], __half2float(s < 8 ? k0[s] : k1[s - 8])));
+    acc = __fadd_rn(acc, __shfl_down_sync(0xffffffffu, acc, 4));
+    acc = __fadd_rn(acc, __shfl_down_sync(0xffffffffu, acc, 1));
+    acc = __fadd_rn(acc, __shfl_down_sync(0xffffffffu, acc, 2));
+    if (valid && j == 0) st_word(A.sc_t + (size_t)h * A.capacity + (i + m * n), pack(acc, tag_sc));
+  }
+}
+
 // Resident serving: the token step `step` consumes (thread 0 of each CTA);
 // -1 when the host stops the launch, -2 when no token comes within the idle
 // limit, -3 when the kernel aborts.  CTA 0 polls the host mailbox and relays
 // what it read; the other CTAs wait for the relay, bounded by the leader's
 // idle limit plus a second.
-__device__ __noinline__ int resident_token(const MegaArgs& A, Shared* sh, MegaCtrl* ctrl, int step) {
-  const unsigned tag = A.relay_base + (unsigned)step;
+// (The launch's fields come by value: a reference to the kernel's parameter
+// block would make every thread keep a local copy of it.)
+__device__ __noinline__ int resident_token(const int* mbox, unsigned long long* relay, unsigned seq0,
+                                           unsigned relay_base, unsigned long long idle_ns, Shared* sh,
+                                           MegaCtrl* ctrl, int step) {
+  const unsigned tag = relay_base + (unsigned)step;
   const unsigned long long t0 = global_ns();
   if (blockIdx.x == 0) {
-    const int want = (int)(A.seq0 + (unsigned)step + 1u);
+    const int want = (int)(seq0 + (unsigned)step + 1u);
     int tok = -2;
     for (unsigned it = 0;; ++it) {
-      if (ld_acquire_sys(A.mbox) == want) {
-        tok = ld_relaxed_sys(A.mbox + 1);
+      if (ld_acquire_sys(mbox) == want) {
+        tok = ld_relaxed_sys(mbox + 1);
         break;
       }
       if ((it & 15) == 15) {
@@ -1063,15 +1118,15 @@ __device__ __noinline__ int resident_token(const MegaArgs& A, Shared* sh, MegaCt
           tok = -3;
           break;
         }
-        if (global_ns() - t0 > A.idle_ns) break;
+        if (global_ns() - t0 > idle_ns) break;
       }
     }
-    st_word_release(A.relay, ((unsigned long long)tag << 32) | (unsigned)tok);
+    st_word_release(relay, ((unsigned long long)tag << 32) | (unsigned)tok);
     return tok;
   }
-  const unsigned long long limit = A.idle_ns + 1000000000ull;
+  const unsigned long long limit = idle_ns + 1000000000ull;
   for (unsigned it = 0;; ++it) {
-    const unsigned long long w = ld_word_acquire(A.relay);
+    const unsigned long long w = ld_word_acquire(relay);
     if ((unsigned)(w >> 32) == tag) return (int)(unsigned)w;
     __nanosleep(100);
     if ((it & 63) == 63) {
@@ -1174,7 +1229,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(const Mega
       sh->go = step + 1;
     }
     if (A.mbox != nullptr) {  // resident serving: the host's token (the step's copies are already requested)
-      if (tid == 0) sh->token = resident_token(A, sh, ctrl, step);
+      if (tid == 0) sh->token = resident_token(A.mbox, A.relay, A.seq0, A.relay_base, A.idle_ns, sh, ctrl, step);
       csync();
       const int posted = sh->token;
       if (posted < 0) break;  // stop, idle or abort: `token` keeps the last argmax
@@ -1239,6 +1294,9 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(const Mega
       }
       MEGA_TRACE(ev + 3);
       if (tid == 0) sh->window = step * A.n_layers + layer + 1;  // the weight stream may refill now
+      // the history's q.k dots for the attention CTAs
+      score_assist(c, layer, pos, blockIdx.x - ATT_CTAS, gridDim.x - ATT_CTAS, tl + kTagQh, tl + kTagSc);
+      MEGA_TRACE(ev + 5);
       {  // stage ffn_norm and the next Q phase's attn_norm during the attention round trip
         const float* fsrc = A.layers[layer].ffn_norm;
         const float* asrc = A.layers[layer + 1 < A.n_layers ? layer + 1 : 0].attn_norm;

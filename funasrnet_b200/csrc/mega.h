@@ -49,6 +49,8 @@ struct MegaArgs {
   unsigned long long* x_t = nullptr;     // [width]
   unsigned long long* qkv_t = nullptr;   // [q + 2 kv width]
   unsigned long long* attn_t = nullptr;  // [q width]
+  unsigned long long* q_t = nullptr;     // [heads x head]: normalised, roped queries (score assist)
+  unsigned long long* sc_t = nullptr;    // [heads x capacity]: raw q.k dots from the GEMV CTAs
   unsigned long long* a_t = nullptr;     // [width]
   unsigned long long* act_t = nullptr;   // [ffn]
   unsigned long long* part_v = nullptr;  // [grid] argmax partial values
@@ -67,10 +69,11 @@ struct MegaArgs {
   // trace[cta * kTraceEvents + event].  Events of layer l are 16*l + e.
   // GEMV CTAs: per phase p (0 Q, 1 O, 2 GU, 3 D) e = 4p + {0 inputs ready,
   // 1 activations quantised, 2 SM cycles spent waiting for the phase's weight
-  // pieces, 3 outputs stored}.  Attention CTAs: e = {0 layer start, 1 q/k/v
-  // loaded, 2 norm + RoPE + KV write, 3 scores, 4 softmax, 5 output stored},
-  // then SM cycles: 6 waiting for K chunks, 7 waiting for V chunks, 8 in the
-  // score loop, 9 in the V loop.  Then 16*layers + {0 LM
+  // pieces, 3 outputs stored}, and e = 5: the score assist done.  Attention
+  // CTAs: e = {0 layer start, 1 q/k/v loaded, 2 norm + RoPE + KV write,
+  // 3 scores, 4 softmax, 5 output stored}, then SM cycles: 6 waiting for the
+  // assisted scores, 7 waiting for V chunks, 8 until the scores were gathered,
+  // 9 in the V loop.  Then 16*layers + {0 LM
   // inputs ready, 1 quantised, 2 lm_head rows done, 3 partials published,
   // 4 token known, 5 all partials read}.
   unsigned long long* trace = nullptr;

@@ -168,7 +168,7 @@ struct fa_session {
   // persistent decode kernel state
   bool use_mega = false;
   int mega_grid = 0;
-  DevBuf mx, mqkv, mattn, ma, mact, mpv, mpi, mctrl;
+  DevBuf mx, mqkv, mattn, ma, mact, mpv, mpi, mctrl, mq, msc;
   unsigned mega_epoch = 1;  // the control block's tag base, as the last launch left it
   int host_pos = -1;        // position of the prefill chunk being enqueued (-1: unknown, e.g. in a graph)
   unsigned test_wait_limit = 0;  // failure-path test hooks for the next persistent launch
@@ -1404,7 +1404,9 @@ int fa_session_create(fa_model* m, fa_session** out) {
         s->mpv.ensure((size_t)s->mega_grid * 8);
         s->mpi.ensure((size_t)s->mega_grid * 8);
         s->mctrl.ensure(sizeof(MegaCtrl));
-        for (DevBuf* b : {&s->mx, &s->mqkv, &s->mattn, &s->ma, &s->mact, &s->mpv, &s->mpi})
+        s->mq.ensure((size_t)qw * 8);
+        s->msc.ensure((size_t)m->heads * m->capacity * 8);
+        for (DevBuf* b : {&s->mx, &s->mqkv, &s->mattn, &s->ma, &s->mact, &s->mpv, &s->mpi, &s->mq, &s->msc})
           FA_CUDA(cudaMemset(b->p, 0, b->bytes));  // tag 0 is never a valid tag
         MegaCtrl c{};
         c.epoch = 1;
@@ -1537,6 +1539,8 @@ static MegaArgs mega_args(fa_session* s, int steps, int record, int n_end, bool 
   a.x_t = s->mx.as<unsigned long long>();
   a.qkv_t = s->mqkv.as<unsigned long long>();
   a.attn_t = s->mattn.as<unsigned long long>();
+  a.q_t = s->mq.as<unsigned long long>();
+  a.sc_t = s->msc.as<unsigned long long>();
   a.a_t = s->ma.as<unsigned long long>();
   a.act_t = s->mact.as<unsigned long long>();
   a.part_v = s->mpv.as<unsigned long long>();

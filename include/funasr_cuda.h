@@ -211,10 +211,12 @@ int fa_session_set_resident(fa_session* session, int on, int idle_us);
  * [grid x events] stamps and returns grid*events.  Layer l owns events
  * 16l + e.  GEMV CTAs: for phase p (0 q/k/v, 1 o, 2 gate/up, 3 down)
  * e = 4p + {0 inputs ready, 1 activations quantised, 2 SM clock cycles spent
- * waiting for the phase's weights, 3 outputs stored}.  Attention CTAs:
+ * waiting for the phase's weights, 3 outputs stored}, and e = 5 when the
+ * CTA's share of the history's q.k dots is published.  Attention CTAs:
  * e = {0 layer start, 1 q/k/v loaded, 2 norm + RoPE + KV write, 3 scores,
- * 4 softmax, 5 output stored}, then SM clock cycles {6 waiting for K chunks,
- * 7 waiting for V chunks, 8 in the score loop, 9 in the V loop}.  After the
+ * 4 softmax, 5 output stored}, then SM clock cycles {6 waiting for the
+ * GEMV CTAs' dots, 7 waiting for V chunks, 8 until the scores are gathered,
+ * 9 in the V loop}.  After the
  * layers: {0 lm_head inputs ready, 1 quantised, 2 rows done, 3 partials
  * published, 4 token known, 5 all partials read}. */
 int fa_session_set_trace(fa_session* session, int on);
