@@ -1293,10 +1293,13 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(const Mega
           goto drain;
       }
       MEGA_TRACE(ev + 3);
-      if (tid == 0) sh->window = step * A.n_layers + layer + 1;  // the weight stream may refill now
       // the history's q.k dots for the attention CTAs
       score_assist(c, layer, pos, blockIdx.x - ATT_CTAS, gridDim.x - ATT_CTAS, tl + kTagQh, tl + kTagSc);
       MEGA_TRACE(ev + 5);
+      // The weight stream refills now, after the assist: its burst of copies
+      // (the layer's o, gate/up, down and the next q/k/v pieces) would
+      // otherwise share HBM and L2 with the assist's K loads and polls.
+      if (tid == 0) sh->window = step * A.n_layers + layer + 1;
       {  // stage ffn_norm and the next Q phase's attn_norm during the attention round trip
         const float* fsrc = A.layers[layer].ffn_norm;
         const float* asrc = A.layers[layer + 1 < A.n_layers ? layer + 1 : 0].attn_norm;
