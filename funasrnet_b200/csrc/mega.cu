@@ -622,9 +622,12 @@ __device__ __forceinline__ void publish_block(unsigned long long* dst, int n, in
 // Waits for n quantised values in that format and unpacks them into xq/xs.
 // POLL_NS > 0 paces the polls: the o and down projections' inputs are
 // awaited for microseconds by every GEMV CTA at once (the attention, the
-// gate/up blocks), and unpaced polls of the same few lines slow the stores
-// and copies the other CTAs make meanwhile (400 ns measured best on B200:
-// -7 % per step against the unpaced wait; 100-200 and 800-1600 slower).
+// gate/up blocks), and unpaced polls of the same few lines slowed the stores
+// and copies the other CTAs make meanwhile (400 ns once measured best for
+// both, -7 % per step against unpaced).  Since the weight window opens after
+// the score assist, the o projection's wait measures best at 100 ns (-1.3 %
+// against 400 ns; unpaced equal); the down projection's stays at 400 ns
+// (100 ns measured equal).
 // The caller's next barrier publishes the shared-memory writes: a projection
 // phase's opening barrier (w8a8_phase) when it follows directly.
 template <int POLL_NS = 0>
@@ -1312,7 +1315,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(const Mega
       if (sp.on > 0) {
         c.wait_ev = ev + 6;
         const bool wo = phase_weights(c, sp.on, 1);
-        gather_q8<400>(c, A.attn_t, QW, tl + kTagAttn);
+        gather_q8<100>(c, A.attn_t, QW, tl + kTagAttn);
         MEGA_TRACE(ev + 4);
         const unsigned tag = tl + kTagA;
         const int o0 = sp.o0;
