@@ -308,6 +308,7 @@ __device__ bool ring_issue(const Ring& r, int& n, const void* src, unsigned byte
     const unsigned parity = (unsigned)((n / r.nslot - 1) & 1);
     for (unsigned it = 0;; ++it) {
       if (mbar_try_wait(&r.empty[slot], parity)) break;
+      __nanosleep(200);  // the ring runs ahead: back off (-0.5 % per step against spinning)
       if ((it & 63) == 63) {
         if (sh->abort || sh->quit) return false;
         if (it > sh->wait_limit) {
