@@ -197,13 +197,13 @@ def source_digest() -> str:
 
 # DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) of the persistent
 # kernel on the bs1_400 workload, from one `ncu` capture of the bench's first
-# 3-step launch (positions 408..410): 2,042,023,936 + 4,085,760 bytes, 682.04 MB
+# 3-step launch (positions 408..410): 2,042,230,528 + 4,323,328 bytes, 682.18 MB
 # per step against 680.52 MB algorithmic, keyed by the digest of mega.cu it was
 # captured on.  The bench reports traffic = that ratio x its own algorithmic
 # bytes per step (the KV share grows with the position in proportion); when the
 # source differs it reports null (not measured on this build).
-MEASURED_TRAFFIC = {"bs1_400": {"traffic_over_algorithmic": 682.037e6 / 680.519e6,
-                                "mega_cu_sha256_16": "f401958e28b03cd3", "captured": "2026-12-02"}}
+MEASURED_TRAFFIC = {"bs1_400": {"traffic_over_algorithmic": 682.185e6 / 680.519e6,
+                                "mega_cu_sha256_16": "d9e9182465d6a733", "captured": "2026-12-02"}}
 
 
 def profile_range(on: bool):
