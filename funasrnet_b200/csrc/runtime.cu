@@ -1696,9 +1696,12 @@ static int resident_step(fa_session* s, int token) {
 }
 
 int fa_session_step(fa_session* s, int32_t token, float* logits, int32_t* next) {
-  const bool resident = s && s->resident && s->use_mega && s->exact_attention && !logits;
   return with_session(s, [&] {
     fa_model* m = s->m;
+    // decided under the session lock: a step with logits (or without the
+    // persistent kernel) ends a running resident launch first
+    const bool resident = s->resident && s->use_mega && s->exact_attention && !logits;
+    if (!resident) resident_stop(s);
     check_tokens(s, &token, 1);
     if (s->pos + 1 > m->capacity) throw Error(kErrArgument, "Decoder context exhausted or invalid embeddings");
     if (resident) {
@@ -1727,7 +1730,7 @@ int fa_session_step(fa_session* s, int32_t token, float* logits, int32_t* next) 
     s->have_token = true;
     if (next) *next = s->pinned[1];
     return (int)kHandled;
-  }, resident);
+  }, /*keep_resident=*/true);
 }
 
 int fa_session_generate(fa_session* s, int max_tokens, const int32_t* end_ids, int n_end, int32_t* tokens,

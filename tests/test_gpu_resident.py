@@ -112,3 +112,27 @@ def test_other_session_runs_while_one_is_resident(small):
         toks_a = a.generate(10, end_ids=())
         toks_b = b.generate(10, end_ids=())  # stops the resident launch first
         assert toks_a == toks_b
+
+
+def test_batch_ends_a_members_resident_launch(small):
+    """A batch call stops a member's resident launch first; the batch's tokens
+    equal the per-session tokens, and the member then steps resident again."""
+    from funasrnet_b200.decoder import BatchDecoder
+
+    cm, om = small
+    a, b, tok = _pair(cm, om, 23, 45)
+    with a, b:
+        ta = tb = tok
+        for i in range(5):
+            ta, _ = a.step(ta)
+            tb, _ = b.step(tb)
+            assert ta == tb, f"step {i}"
+        ga = a.generate(6, end_ids=())
+        with BatchDecoder([b]) as g:
+            gb = g.generate(6)[:, 0].tolist()
+        assert ga == gb
+        na, nb = ga[-1], gb[-1]
+        for i in range(4):
+            na, _ = a.step(na)
+            nb, _ = b.step(nb)
+            assert na == nb, f"step {i} after the batch"
