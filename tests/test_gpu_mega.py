@@ -162,3 +162,29 @@ def test_fault_test_hook_rejects_attention_ctas(small):
             d.set_fault_test(withhold_cta=3)
         with pytest.raises(FaError):
             d.set_fault_test(withhold_cta=d.persistent_grid())
+
+
+def test_persistent_kernel_at_large_capacity(backend, small, small_gguf):
+    """At a cache capacity of 4,096 positions (a 16 KB score row per attention
+    CTA on top of the GEMV staging) the persistent kernel still launches, and
+    its tokens and logits equal the CUDA-graph path's."""
+    from funasrnet_b200.decoder import CudaModel, QwenDecoder
+
+    _, om = small
+    cm = CudaModel(backend, small_gguf, capacity=4096)
+    try:
+        emb, frames = prefix_embeddings(om, 30, 8, seed=35)
+        with QwenDecoder(cm) as a, QwenDecoder(cm) as b:
+            assert a.persistent_grid() > 0
+            assert b.set_persistent(False)
+            for d in (a, b):
+                d.decode(emb, frames, want_logits=False)
+            ta = a.generate(12, end_ids=())
+            tb = b.generate(12, end_ids=())
+            assert ta == tb
+            na, la = a.step(ta[-1], want_logits=True)
+            nb, lb = b.step(tb[-1], want_logits=True)
+            assert na == nb
+            assert_bits_equal(la, lb, "persistent vs graph step logits at capacity 4096")
+    finally:
+        cm.close()
