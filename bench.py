@@ -436,7 +436,9 @@ def main():
     ap.add_argument("--sessions", type=int, default=None, help="batched configs: sessions per GPU (profiling runs)")
     ap.add_argument("--profile-range", action="store_true",
                     help="bracket the timed region with cudaProfilerStart/Stop (ncu --profile-from-start off)")
-    ap.add_argument("--cpu-baseline-steps", type=int, default=24)
+    ap.add_argument("--cpu-baseline-steps", type=int, default=256,
+                    help="greedy decode steps of the CPU restatement on all host threads (a third of them on 4); "
+                         "its tokens are also compared with the GPU's")
     ap.add_argument("--no-fp32", action="store_true", help="skip the FP32 (config 3) entry of the default run")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--phase-trace", action="store_true",
