@@ -454,7 +454,7 @@ def main():
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
     dist = None
-    if world > 1:
+    if world > 1 and args.impl != "reference":  # the CPU reference arm needs no process group
         import datetime
 
         import torch
@@ -491,9 +491,7 @@ def main():
                                      "sample": f"{steps} decode steps after the {audio + ids}-frame prefill"},
                     "e2e": {"value": rate, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
             print(json.dumps(line), flush=True)
-        if dist is not None:
-            dist.destroy_process_group()
-        return
+        return  # under torchrun the other ranks leave without work
 
     from funasrnet_b200.backend import CudaFloatBackend
     from funasrnet_b200.decoder import CudaModel, QwenDecoder

@@ -7,6 +7,7 @@ needs no GPU and never loads the product library."""
 
 import json
 import os
+import socket
 import subprocess
 import sys
 from pathlib import Path
@@ -45,3 +46,23 @@ def test_reference_arm_prints_one_contract_line():
     assert "2 decode steps after the 108-frame prefill" in cb["sample"]
     # the product library stayed unloaded
     assert "MAPPED 0" in out.stdout.splitlines(), out.stdout[-500:]
+
+
+def test_reference_arm_under_torchrun_prints_once():
+    """Launched like the CUDA arm at N > 1 (torchrun, one process per GPU),
+    rank 0 alone runs the CPU reference and prints; the other rank exits 0
+    without work and without a process group."""
+    env = dict(os.environ)
+    with socket.socket() as sock:
+        sock.bind(("127.0.0.1", 0))
+        port = sock.getsockname()[1]
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node", "2",
+           "--master-addr", "127.0.0.1", "--master-port", str(port), "bench.py", "--impl", "reference",
+           "--gpus", "2", "--config", "bs1_100", "--steps", "2", "--warmup", "3"]
+    out = subprocess.run(cmd, cwd=ROOT, env=env, capture_output=True, text=True, timeout=600)
+    assert out.returncode == 0, out.stderr[-2000:]
+    lines = [ln for ln in out.stdout.splitlines() if ln.startswith("{")]
+    assert len(lines) == 1, out.stdout[-2000:]
+    d = json.loads(lines[0])
+    assert d["impl"] == "reference" and d["n_gpus"] == 2 and d["value"] > 0
+    assert d["config"]["parallelism"] == "replicas x2"
