@@ -33,6 +33,40 @@ def test_binding_declares_every_symbol():
     assert set(header_functions()) == set(SIGNATURES)
 
 
+def test_binding_matches_header_prototypes():
+    """Each ctypes declaration has the header prototype's parameters: the
+    same count, and per parameter the same kind (pointer, integer, float) and
+    width, so no call passes a 32-bit value where the C side reads 64 bits."""
+    import ctypes
+
+    from funasrnet_b200._lib import SIGNATURES
+
+    text = re.sub(r"/\*.*?\*/", "", HEADER.read_text(), flags=re.S)
+    text = re.sub(r"//[^\n]*", "", text)
+    protos = re.findall(r"\b(fa_[a-z0-9_]+)\s*\(([^;{]*?)\)\s*;", text, flags=re.S)
+    scalars = {"int": ("int", 4), "int32_t": ("int", 4), "uint32_t": ("int", 4), "unsigned": ("int", 4),
+               "int64_t": ("int", 8), "uint64_t": ("int", 8), "size_t": ("int", 8), "float": ("float", 4),
+               "double": ("float", 8)}
+
+    def header_kind(param):
+        if "*" in param:
+            return ("pointer", 8)
+        words = param.replace("const ", "").split()
+        return scalars.get(" ".join(words[:-1]), ("unknown", param))
+
+    def binding_kind(t):
+        if t in (ctypes.c_void_p, ctypes.c_char_p) or issubclass(t, ctypes._Pointer):
+            return ("pointer", 8)
+        return ("float" if t in (ctypes.c_float, ctypes.c_double) else "int", ctypes.sizeof(t))
+
+    assert {name for name, _ in protos} == set(SIGNATURES)
+    for name, params in protos:
+        params = params.strip()
+        want = [] if params in ("", "void") else [header_kind(x.strip()) for x in params.split(",")]
+        got = [binding_kind(t) for t in SIGNATURES[name][1]]
+        assert want == got, name
+
+
 def test_binding_loads(built_lib):
     from funasrnet_b200._lib import lib
 
