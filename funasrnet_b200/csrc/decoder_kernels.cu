@@ -915,6 +915,90 @@ __global__ void __launch_bounds__(256) gemv_f32_kernel(const F32GemvArgs a) {
   }
 }
 
+// FP32 projections of Linear calls with 4 frames or more, in the orders the
+// reference picks for them on an AVX2 + FMA host (TensorMath.cs:106-176):
+//  seg (>= 16 frames, cols >= 16, rows >= 4): PackedFloatLinearAvx and its
+//    six-row / unrolled forms (TensorMath.Avx.cs:123-225, TensorMath.SixAvx.cs:
+//    18-165): per 128-column segment one fused multiply-add chain from 0 in
+//    column order, added to a running sum from 0;
+//  otherwise whole groups of four frames through Dot4x4 / Dot4 (TensorMath.cs:
+//    226-360; x64 Mac = a + b*c): 4 lanes, (v0+v1)+(v2+v3); the remaining
+//    frames through AudioKernels.Dot (AudioKernels.cs:94-143): 8 lanes folded
+//    as FloatRows4Avx folds them.
+// Output = bias (or 0) + sum, then the residual.  Block: 8 warps, warp = one
+// row, lane = one frame of 32; x staged per 128-column segment as [column][frame]
+// (RMSNorm applied when gamma is set: 1/rms per frame from one warp's double
+// sum of squares).  Weights in the permuted FP32 layout (pack_f32).
+constexpr int kOrdRows = 8, kOrdFrames = 32, kOrdSeg = 128;
+
+__global__ void __launch_bounds__(256) gemv_f32_order_kernel(const F32GemvArgs a, int order_frames, int seg) {
+  if (skipped(a.skip)) return;
+  __shared__ float xs[kOrdSeg][kOrdFrames + 1];  // padded: the staging writes run down a column
+  __shared__ float inv_s[kOrdFrames];
+  const int K = a.w.cols, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int f0 = blockIdx.y * kOrdFrames, fc = min(kOrdFrames, a.frames - f0);
+  if (a.gamma != nullptr) {
+    for (int fi = warp; fi < fc; fi += 8) {
+      const float* xr = a.x + (size_t)(f0 + fi) * K;
+      double part = 0.0;
+      for (int k = lane; k < K; k += 32) {
+        const double z = (double)xr[k];
+        part = __dadd_rn(part, __dmul_rn(z, z));
+      }
+      part = warp_sum_d(part);
+      if (lane == 0) inv_s[fi] = rms_inverse(part, K, a.eps);
+    }
+  }
+  const int row = blockIdx.x * kOrdRows + warp;
+  const bool valid = row < a.w.rows && lane < fc;
+  const int f = f0 + lane;
+  // 2: fused segments; 1: four lanes; 0: eight lanes
+  const int mode = seg ? 2 : (f < order_frames / 4 * 4 ? 1 : 0);
+  const float* wr = a.w.w + (size_t)(row < a.w.rows ? row : 0) * K;
+  float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+  float sum = 0.0f;
+  for (int s0 = 0; s0 < K; s0 += kOrdSeg) {
+    const int n = min(kOrdSeg, K - s0);  // a multiple of 32
+    __syncthreads();  // the previous segment is consumed (and inv_s is written)
+    for (int i = threadIdx.x; i < kOrdSeg * kOrdFrames; i += 256) {
+      const int fi = i / kOrdSeg, k = i - fi * kOrdSeg;
+      float v = 0.0f;
+      if (fi < fc && k < n) {
+        v = a.x[(size_t)(f0 + fi) * K + s0 + k];
+        if (a.gamma != nullptr) v = __fmul_rn(__fmul_rn(v, inv_s[fi]), a.gamma[s0 + k]);
+      }
+      xs[k][fi] = v;
+    }
+    __syncthreads();
+    if (!valid) continue;
+    float chain = 0.0f;
+    for (int k = 0; k < n; k += 32) {
+      const float* wg = wr + s0 + k;  // one permuted 32-group: column c at 4 (c & 7) + (c >> 3)
+#pragma unroll
+      for (int c = 0; c < 32; ++c) {
+        const float w = __ldg(wg + 4 * (c & 7) + (c >> 3)), x = xs[k + c][lane];
+        if (mode == 2) chain = __fmaf_rn(x, w, chain);
+        else if (mode == 1) acc[c & 3] = __fadd_rn(acc[c & 3], __fmul_rn(w, x));
+        else acc[c & 7] = __fadd_rn(acc[c & 7], __fmul_rn(x, w));
+      }
+    }
+    sum = __fadd_rn(sum, chain);
+  }
+  if (!valid) return;
+  float v;
+  if (mode == 2) {
+    v = sum;
+  } else if (mode == 1) {
+    v = __fadd_rn(__fadd_rn(acc[0], acc[1]), __fadd_rn(acc[2], acc[3]));
+  } else {
+    v = __fadd_rn(__fadd_rn(__fadd_rn(acc[0], acc[4]), __fadd_rn(acc[1], acc[5])),
+                  __fadd_rn(__fadd_rn(acc[2], acc[6]), __fadd_rn(acc[3], acc[7])));
+  }
+  v = __fadd_rn(a.bias != nullptr ? a.bias[row] : 0.0f, v);
+  float* o = a.out + (size_t)f * a.out_stride + row;
+  *o = a.epilogue == kEpiResidual ? __fadd_rn(v, a.res[(size_t)f * a.out_stride + row]) : v;
+}
+
 __global__ void silu_pair_kernel(const float* buf, int frames, int ffn, float* act, const int* skip) {
   if (skipped(skip)) return;
   const long long n = (long long)frames * ffn;
@@ -1154,6 +1238,16 @@ void pack_f32(const float* w, int rows, int cols, float* out) {
 int gemv_f32_smem_bytes(int K) { return kF32Frames * K * 4; }
 
 void launch_gemv_f32(const F32GemvArgs& a, cudaStream_t stream) {
+  const int order_frames = a.order_frames > 0 ? a.order_frames : a.frames;
+  if (order_frames >= 4) {  // the reference's orders for calls of 4 frames or more
+    if (a.w.cols % 32 != 0) throw Error(kErrArgument, "FP32 GEMV needs cols % 32 == 0");
+    if (a.epilogue != kEpiStore && a.epilogue != kEpiResidual) throw Error(kErrArgument, "FP32 GEMV epilogue");
+    const int seg = order_frames >= 16 && a.w.cols >= 16 && a.w.rows >= 4;
+    dim3 grid((a.w.rows + kOrdRows - 1) / kOrdRows, (a.frames + kOrdFrames - 1) / kOrdFrames);
+    gemv_f32_order_kernel<<<grid, 256, 0, stream>>>(a, order_frames, seg);
+    FA_CUDA(cudaGetLastError());
+    return;
+  }
   if (launch_gemv_f32_stream(a, stream)) return;
   const int smem = gemv_f32_smem_bytes(a.w.cols);
   if (smem > kGemvMaxSmem) throw Error(kErrCapacity, "GEMV inner dimension too large for shared memory");

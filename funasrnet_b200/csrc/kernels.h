@@ -77,6 +77,10 @@ struct F32GemvArgs {
   const float* bias = nullptr;
   const int* skip = nullptr;
   int* err = nullptr;         // optional error word (a bounded wait gave up)
+  // Frames of the reference's Linear call these frames belong to (0: frames):
+  // it picks the summation order (TensorMath.cs:106-176), and a prefill runs
+  // its call's frames in chunks.
+  int order_frames = 0;
 };
 void launch_gemv_f32(const F32GemvArgs& a, cudaStream_t stream);
 // Streaming one-frame FP32 GEMV (f32_stream.cu): TMA-fed persistent CTAs,

@@ -1096,7 +1096,9 @@ void enqueue_layer_bmm(fa_session* s, int l, int frames) {
 
 // QwenDecoder.Decode's layer loop (QwenDecoder.cs:180-252) for `frames`
 // frames already in s->x; KV positions come from the device word pos.
-void enqueue_layers(fa_session* s, int frames, const int* skip) {
+// call_frames: the frames of the Decode call this chunk belongs to (0: frames),
+// which pick the FP32 projections' summation order.
+void enqueue_layers(fa_session* s, int frames, const int* skip, int call_frames = 0) {
   fa_model* m = s->m;
   const int W = m->width, qw = m->heads * m->head_size, kvw = m->kv_heads * m->head_size;
   cudaStream_t st = s->stream;
@@ -1130,6 +1132,7 @@ void enqueue_layers(fa_session* s, int frames, const int* skip) {
       g.out_stride = qw + 2 * kvw;
       g.skip = skip;
       g.err = s->d_int(kErrWord);
+      g.order_frames = call_frames;
       launch_gemv_f32(g, st);
     }
     enqueue_attention(s, l, frames, skip);
@@ -1176,6 +1179,7 @@ void enqueue_layers(fa_session* s, int frames, const int* skip) {
       g.out_stride = W;
       g.skip = skip;
       g.err = s->d_int(kErrWord);
+      g.order_frames = call_frames;
       launch_gemv_f32(g, st);
       F32GemvArgs u;
       u.x = s->a.as<float>();
@@ -1187,6 +1191,7 @@ void enqueue_layers(fa_session* s, int frames, const int* skip) {
       u.out_stride = 2 * m->ffn;
       u.skip = skip;
       u.err = s->d_int(kErrWord);
+      u.order_frames = call_frames;
       launch_gemv_f32(u, st);
       launch_silu_pair(s->gu.as<float>(), frames, m->ffn, s->act.as<float>(), skip, st);
       F32GemvArgs d;
@@ -1199,6 +1204,7 @@ void enqueue_layers(fa_session* s, int frames, const int* skip) {
       d.out_stride = W;
       d.skip = skip;
       d.err = s->d_int(kErrWord);
+      d.order_frames = call_frames;
       launch_gemv_f32(d, st);
     }
     if (l == 0 && s->debug) {
@@ -1488,7 +1494,7 @@ static int session_decode_locked(fa_session* s, const float* emb, const int32_t*
       enqueue_embed(s, s->tokens.as<int>(), c, nullptr);
     }
     s->host_pos = s->pos + done;
-    enqueue_layers(s, c, nullptr);
+    enqueue_layers(s, c, nullptr, frames);
     s->host_pos = -1;
     done += c;
     if (done == frames && output_logits) enqueue_head(s, s->x.as<float>() + (size_t)(c - 1) * W, nullptr);

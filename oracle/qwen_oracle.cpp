@@ -207,21 +207,71 @@ int or_q8_linear(const float* x, int frames, const int8_t* w, const float* ws, i
   return 0;
 }
 
+// One FP32 output (row wr, frame xt) in each of the orders TensorMath.Linear
+// picks on an AVX2 + FMA host (TensorMath.cs:106-129); `bias` is the row's
+// bias or 0.
+
+// FloatRows4Avx (TensorMath.FloatRowsAvx.cs:27-53) and AudioKernels.Dot
+// (AudioKernels.cs:94-143): lane j of 8 sums x*w (two roundings) over columns
+// j, j+8, ...; Vector128.Sum(lower + upper); the tail columns in order; then
+// bias + sum (both kernels add the bias last, on the left).
+static float f32_dot8(const float* xt, const float* wr, int cols, float bias) {
+  float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+  int c = 0;
+  for (; c <= cols - 8; c += 8)
+    for (int j = 0; j < 8; ++j) acc[j] = acc[j] + xt[c + j] * wr[c + j];
+  float s = fold8(acc);
+  for (; c < cols; ++c) s += xt[c] * wr[c];
+  return bias + s;
+}
+
+// Dot4x4 / Dot4 (TensorMath.cs:226-360) on x64 (Mac = a + b*c): lane j of 4
+// sums w*x over columns j, j+4, ...; Vector128.Sum + bias, then the tail.
+static float f32_dot4(const float* xt, const float* wr, int cols, float bias) {
+  float acc[4] = {0, 0, 0, 0};
+  int c = 0;
+  for (; c <= cols - 4; c += 4)
+    for (int j = 0; j < 4; ++j) acc[j] = acc[j] + wr[c + j] * xt[c + j];
+  float s = sum4(acc[0], acc[1], acc[2], acc[3]) + bias;
+  for (; c < cols; ++c) s += wr[c] * xt[c];
+  return s;
+}
+
+// PackedFloatLinearAvx and its six-row / unrolled forms (TensorMath.Avx.cs:
+// 123-225, TensorMath.SixAvx.cs:18-165, TensorMath.UnrolledAvx.cs): columns in
+// segments of 128 (FloatAvxSegment); per segment one fused multiply-add chain
+// from 0 in column order, added to a running sum from 0; then sum + bias.
+static float f32_seg(const float* xt, const float* wr, int cols, float bias) {
+  float sum = 0.0f;
+  for (int start = 0; start < cols; start += 128) {
+    float acc = 0.0f;
+    for (int c = start; c < std::min(cols, start + 128); ++c) acc = std::fma(xt[c], wr[c], acc);
+    sum = sum + acc;
+  }
+  return sum + bias;
+}
+
 int or_f32_linear(const float* x, int frames, const float* w, int rows, int cols,
                   const float* bias, float* out) {
   if (frames < 0 || rows < 0 || cols < 0) return -1;
+  // TensorMath.cs:106-110 (packed, frames >= 16), :124-128 (FloatRows4Avx,
+  // frames < 4), else the generic blocks :130-176 (frames in groups of four
+  // through Dot4x4 / Dot4, the rest through AudioKernels.Dot).
+  const bool shaped = cols >= 16 && rows >= 4;
+  const int mode = shaped && frames >= 16 ? 2 : (shaped && frames < 4 ? 0 : 1);
+  const int grouped = frames / 4 * 4;
 #pragma omp parallel for schedule(static) num_threads(g_threads)
   for (int r = 0; r < rows; ++r) {
     const float* wr = w + (size_t)r * cols;
+    const float b = bias ? bias[r] : 0.0f;
     for (int t = 0; t < frames; ++t) {
       const float* xt = x + (size_t)t * cols;
-      float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-      int c = 0;
-      for (; c <= cols - 8; c += 8)
-        for (int j = 0; j < 8; ++j) acc[j] = acc[j] + xt[c + j] * wr[c + j];
-      float s = fold8(acc);
-      for (; c < cols; ++c) s += xt[c] * wr[c];
-      out[(size_t)t * rows + r] = (bias ? bias[r] : 0.0f) + s;
+      float v;
+      if (mode == 2) v = f32_seg(xt, wr, cols, b);
+      else if (mode == 0) v = f32_dot8(xt, wr, cols, b);
+      else if (t < grouped) v = f32_dot4(xt, wr, cols, b);
+      else v = f32_dot8(xt, wr, cols, b);
+      out[(size_t)t * rows + r] = v;
     }
   }
   return 0;

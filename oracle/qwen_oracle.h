@@ -41,8 +41,12 @@ int or_quantize(const float* x, int64_t n, int8_t* q, float* scales);
 int or_q8_linear(const float* x, int frames, const int8_t* w, const float* ws,
                  int rows, int cols, const float* bias, float* out);
 
-/* FloatRows4Avx (TensorMath.FloatRowsAvx.cs:15-80) for FP32 weights:
- * 8 lane accumulators, lanes folded as ((l0+l4)+(l1+l5))+((l2+l6)+(l3+l7)). */
+/* TensorMath.Linear for FP32 weights on an AVX2 + FMA host (TensorMath.cs:106-176):
+ * frames < 4: FloatRows4Avx (8 lane accumulators, lanes folded as
+ * ((l0+l4)+(l1+l5))+((l2+l6)+(l3+l7))); frames >= 16: the packed kernels (per
+ * 128-column segment one fused multiply-add chain, segments summed in order);
+ * otherwise Dot4x4 (4 lanes) for whole groups of four frames, Dot (8 lanes)
+ * for the rest. */
 int or_f32_linear(const float* x, int frames, const float* w, int rows, int cols,
                   const float* bias, float* out);
 

@@ -89,12 +89,16 @@ def test_linear_declines_and_keeps_output(backend):
         backend.try_quantized_linear(np.zeros(63, np.float32), 1, w, None, out)
 
 
-@pytest.mark.parametrize("frames", [1, 2, 3, 7])
+@pytest.mark.parametrize("frames", [1, 2, 3, 4, 7, 15, 16, 33])
 def test_f32_linear(backend, oracle, frames):
+    """FP32 projections in the order the reference picks for the call's frame
+    count (TensorMath.cs:106-176): FloatRows4Avx below 4 frames, Dot4x4 groups
+    of four plus Dot for the rest up to 15, the fused-segment packed kernels
+    from 16 (33 frames: two frame tiles; 1003 rows: a partial row block)."""
     from funasrnet_b200.backend import Weight
 
     rng = np.random.default_rng(frames)
-    rows, cols = 1000, 1024
+    rows, cols = 1003, 1024
     wv = (rng.standard_normal((rows, cols)) * 0.02).astype(np.float32)
     x = rng.standard_normal(frames * cols).astype(np.float32)
     bias = rng.standard_normal(rows).astype(np.float32)
@@ -102,8 +106,7 @@ def test_f32_linear(backend, oracle, frames):
     out = np.empty(frames * rows, np.float32)
     assert backend.try_linear(x, frames, w, Weight("b", (rows,), values=bias), out)
     exp = oracle.f32_linear(x, frames, wv, rows, cols, bias)
-    # FloatRows4Avx order (frames < 4) is reproduced bit for bit.
-    assert_bits_equal(out, exp, "FP32 GEMV")
+    assert_bits_equal(out, exp, f"FP32 GEMV, {frames} frames")
 
 
 @pytest.mark.parametrize("width,rows", [(1024, 5), (128, 24), (96, 3), (3072, 2)])
