@@ -274,6 +274,30 @@ def test_shared_prefix_across_sessions(small, oracle):
         d.close()
 
 
+def test_fp32_prefill_across_chunks_keeps_the_call_order(backend, oracle, small_gguf_f32):
+    """A 520-frame FP32 prefill runs as chunks of 512 and 8 frames; the 8-frame
+    chunk still takes the order of the whole 520-frame Linear call (the packed
+    kernels' fused segments), so the logits equal the oracle's one-call decode."""
+    from funasrnet_b200.decoder import CudaModel, QwenDecoder
+
+    cm = CudaModel(backend, small_gguf_f32, capacity=640)
+    om = oracle.Model(small_gguf_f32, 640)
+    emb, frames = prefix_embeddings(om, 516, 4, seed=77)
+    assert frames == 520
+    d = QwenDecoder(cm)
+    os_ = oracle.Session(om)
+    lg, _ = d.decode(emb, frames)
+    exp = os_.decode(emb, frames)
+    check_logits(lg, exp, "fp32 prefill of 520 frames")
+    tok = oracle.greedy(exp)
+    _, lg = d.step(tok, want_logits=True)
+    check_logits(lg, os_.decode(om.embed([tok]), 1), "fp32 step after the chunked prefill")
+    d.close()
+    os_.close()
+    cm.close()
+    om.close()
+
+
 def test_fp32_weights_model(backend, oracle, small_gguf_f32):
     from funasrnet_b200.decoder import CudaModel, QwenDecoder
 
